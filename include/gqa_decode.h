@@ -1,0 +1,166 @@
+/*
+ * gqa_decode.h - C ABI of the B200 (sm_100a) paged-KV GQA decode engine.
+ *
+ * Operator (python/reference.py:21-40 of the reference):
+ *   out[b, h, :] = softmax_t(q[b, h, :] . K[t, hk, :] * scale) @ V[t, hk, :]
+ *   for t < seq_lens[b], hk = h / (Hq / Hkv), with token t of request b
+ *   stored in physical block block_table[b, t / block_size], slot
+ *   t % block_size.
+ *
+ * Layouts (all row-major, contiguous, device memory):
+ *   q            bf16  [B, Hq, 128]
+ *   k_cache      bf16  [num_blocks, block_size, Hkv, 128]   (NHD pages)
+ *   v_cache      bf16  [num_blocks, block_size, Hkv, 128]
+ *   block_table  int32 [B, max_blocks]
+ *   seq_lens     int32 [B]
+ *   out          bf16  [B, Hq, 128]
+ * q, k_cache, v_cache, out and any workspace must be 16-byte aligned.
+ *
+ * Every launcher is asynchronous on `stream`, allocates nothing and does not
+ * synchronise.  The first three keep the reference's signatures exactly (a
+ * caller compiled against the reference header links against this library
+ * unchanged); they return void as the reference does, and report argument
+ * errors through gqa_decode_last_error().  The remaining entry points are
+ * additions and return cudaError_t.
+ */
+#ifndef GQA_DECODE_B200_H_
+#define GQA_DECODE_B200_H_
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+#include <cuda_bf16.h>
+typedef __nv_bfloat16 gqa_bf16;
+extern "C" {
+#else
+#include <stdint.h>
+typedef uint16_t gqa_bf16; /* raw bf16 bits */
+#endif
+
+/* Replaces gqa_decode_v0_launch (reference include/gqa_decode.h:6-10,
+ * kernels/gqa_decode/v0_naive.cu:27-36).  Here: the CUDA-core grouped scan,
+ * one CTA per (request, kv head), no tensor cores and no TMA - the ablation
+ * rung. */
+void gqa_decode_v0_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                          const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
+                          int Hq, int Hkv, int block_size, int max_blocks, float scale,
+                          cudaStream_t stream);
+
+/* Replaces gqa_decode_v1_launch (reference include/gqa_decode.h:12-16,
+ * kernels/gqa_decode/v1_vectorized.cu:73-82).  Here: the unsplit scan - the
+ * pipelined TMA + tensor-core kernel with one segment per request. */
+void gqa_decode_v1_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                          const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
+                          int Hq, int Hkv, int block_size, int max_blocks, float scale,
+                          cudaStream_t stream);
+
+/* Replaces gqa_decode_v2_launch (reference include/gqa_decode.h:18-23,
+ * kernels/gqa_decode/v2_splitkv.cu:110-125).  Split-KV: each request's
+ * tokens are cut into num_splits chunks (1..512), partial states go to the
+ * caller's fp32 workspace ws_acc [B, Hq, num_splits, 128], ws_m and
+ * ws_l [B, Hq, num_splits] (same sizes as the reference), then a merge
+ * kernel on the same stream writes out.  num_splits == 1 runs exactly the
+ * arithmetic of gqa_decode_v1_launch (bitwise-equal output) and needs no
+ * workspace. */
+void gqa_decode_v2_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                          const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
+                          int Hq, int Hkv, int block_size, int max_blocks, float scale,
+                          int num_splits, float* ws_acc, float* ws_m, float* ws_l,
+                          cudaStream_t stream);
+
+/* Status of the calling thread's last v0/v1/v2 launch; reading it resets it
+ * to cudaSuccess.  The reference's launchers have no error channel
+ * (include/gqa_decode.h:6-23); the reference extension validated in
+ * python/gqa_decode_ext.cpp:16-62 instead. */
+cudaError_t gqa_decode_last_error(void);
+
+/* Shape plan of the pipelined kernel (no device access). */
+typedef struct gqa_decode_plan {
+  int group;             /* q heads per kv head, Hq / Hkv */
+  int heads_per_row;     /* kv heads one CTA streams per token row */
+  int consumer_warps;    /* tensor-core warps per CTA */
+  int threads;           /* CTA size, consumer warps + one copy warp */
+  int stages;            /* depth of the shared-memory ring (16 tokens each) */
+  int smem_bytes;        /* dynamic shared memory per CTA */
+  int grid;              /* CTAs launched */
+  size_t workspace_bytes;/* bytes gqa_decode_launch needs for these dims */
+} gqa_decode_plan;
+
+/* Plan for the given dims on a GPU with num_sms SMs running ctas_per_sm CTAs
+ * of this kernel each.  num_splits: 0 = balanced schedule, 1..512 = fixed
+ * splits.  Returns 0, or -1 for invalid dims / -2 for Hq / Hkv > 128.
+ * No reference counterpart (the reference sizes its grid in each launcher). */
+int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, int ctas_per_sm,
+                          gqa_decode_plan* plan);
+
+/* Workspace bytes gqa_decode_launch / gqa_decode_partial_launch need on the
+ * current device; 0 when none is needed.  No reference counterpart (the
+ * reference extension allocates per call, python/gqa_decode_ext.cpp:106-109). */
+size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
+
+/* Zero a workspace before its first use.  The balanced schedule keeps
+ * per-row arrival counters there and every launch returns them to zero, so
+ * one initialisation serves any number of launches and shapes. */
+cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream);
+
+/* Decode with the split count chosen by the library (num_splits == 0) or
+ * given (1..512, same semantics as gqa_decode_v2_launch).  num_splits == 0
+ * selects the balanced schedule: one persistent CTA per SM, each streaming
+ * an equal share of all requests' KV, with partial rows merged in the same
+ * launch.  num_blocks > 0 makes the kernel check every block id against
+ * [0, num_blocks) (a bad id sets status bit 2 and reads block 0 instead).
+ * Workspace: gqa_decode_workspace_bytes, zeroed once with
+ * gqa_decode_workspace_init.  Concurrent launches must not share one
+ * workspace.  Additive to the reference API (its extension exposes
+ * num_splits only on v2, python/gqa_decode_ext.cpp:97-123). */
+cudaError_t gqa_decode_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
+                              const gqa_bf16* v_cache, const int* block_table,
+                              const int* seq_lens, gqa_bf16* out, int B, int Hq, int Hkv,
+                              int block_size, int max_blocks, int num_blocks, float scale,
+                              int num_splits, void* workspace, size_t workspace_bytes,
+                              cudaStream_t stream);
+
+/* Like gqa_decode_launch with num_splits == 0, but writes each (request, q
+ * head)'s unnormalised softmax state instead of out: state_m, state_l
+ * [B, Hq] (running max of score*scale*log2(e), and the sum of
+ * 2^(score*scale*log2(e) - m)) and state_acc [B, Hq, 128].  A request with
+ * no tokens gets m = -inf, l = 0, acc = 0.  Used to shard one request's KV
+ * range across GPUs; combine with gqa_decode_merge_states.  No reference
+ * counterpart (the reference keeps states internal,
+ * kernels/gqa_decode/v2_splitkv.cu:83-89). */
+cudaError_t gqa_decode_partial_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                      const gqa_bf16* v_cache, const int* block_table,
+                                      const int* seq_lens, float* state_m, float* state_l,
+                                      float* state_acc, int B, int Hq, int Hkv, int block_size,
+                                      int max_blocks, int num_blocks, float scale,
+                                      void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream);
+
+/* Merge nshards states per row (state i of row r at index i * rows + r, acc
+ * at (i * rows + r) * 128) into bf16 out [rows, 128] with the online-softmax
+ * identity of kernels/gqa_decode/v2_splitkv.cu:97-107 (reference); rows whose
+ * shards are all empty get 0. */
+cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
+                                    const float* state_acc, int nshards, int rows, gqa_bf16* out,
+                                    cudaStream_t stream);
+
+/* Fixed split count for the v2 schedule at a nominal seq_len: the count
+ * (1..512) that minimises the estimated makespan over num_sms SMs.  The
+ * reference picks it by offline sweep (bench/run_matrix.py:84-88). */
+int gqa_decode_pick_splits(int B, int Hq, int Hkv, int seq_len, int num_sms);
+
+/* Device status word of the current device: bit 0 = a pipeline wait timed
+ * out, bit 1 = a block id was out of range.  clear != 0 resets it.
+ * Synchronous. */
+cudaError_t gqa_decode_get_status(int* status, int clear);
+
+/* Library version string. */
+const char* gqa_decode_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* GQA_DECODE_B200_H_ */

@@ -1,0 +1,125 @@
+// Internal types shared by the decode kernels and the C-ABI entry points.
+//
+// Work model.  A "row" is one request b and one group of HG consecutive kv
+// heads (hg).  A row's tokens [0, S_b) are cut into "stages" of 16 tokens,
+// the unit of one pipeline slot and one tensor-core M tile.  The scan kernel
+// walks a sequence of "segments" (a row and a stage range) in one of two
+// schedules:
+//   * FIXED     - the reference's split-KV decomposition: every row is cut
+//                 into num_splits equal stage chunks (tasks), tasks are dealt
+//                 to CTAs round-robin (python/gqa_decode_ext.cpp:97-123,
+//                 kernels/gqa_decode/v2_splitkv.cu:30-32 split on tokens;
+//                 here the cut is on 16-token stages).
+//   * BALANCED  - the flattened sequence of all rows' stages is divided into
+//                 gridDim.x equal contiguous ranges, one per resident CTA, so
+//                 every SM streams the same number of KV bytes whatever the
+//                 batch's length distribution.
+// A segment that covers its whole row writes the normalised bf16 output; a
+// segment that covers part of a row writes an unnormalised fp32 partial
+// (m, l, acc) that a merge combines with the online-softmax identity
+// (kernels/gqa_decode/v2_splitkv.cu:97-107).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime_api.h>
+
+namespace gqa {
+
+constexpr int kHeadDim = 128;        // d, fixed by the reference API
+constexpr int kStageTokens = 16;     // tokens per pipeline stage / MMA M tile
+constexpr int kMaxConsumerWarps = 16;
+constexpr int kMaxSplits = 512;      // python/gqa_decode_ext.cpp:102-103
+constexpr int kSmemBudget = 200 * 1024;  // dynamic smem per CTA for the stage ring
+constexpr int kMaxStages = 8;
+
+enum Schedule : int { kFixed = 0, kBalanced = 1 };
+
+// Shape-only launch plan (no device state): how heads map to warps and how
+// large the stage ring is.
+struct ShapePlan {
+  int G;          // q heads per kv head (Hq / Hkv)
+  int NT;         // 8-head MMA column tiles per kv head = ceil(G / 8)
+  int HG;         // kv heads per row (per CTA)
+  int NHG;        // rows per request = Hkv / HG
+  int ncw;        // consumer warps = HG * NT
+  int threads;    // (ncw + 1) * 32, one producer warp
+  int row_bytes;  // bytes of one token's HG kv heads = HG * 256
+  int row_stride; // smem stride of one token row = row_bytes + 16 (bank skew)
+  int stage_bytes;// K and V rows of one 16-token stage
+  int nstages;    // depth of the ring
+  int smem_bytes; // dynamic shared memory per CTA
+};
+
+// Returns 0 on success, or a negative code for unsupported shapes.
+int make_shape_plan(int Hq, int Hkv, ShapePlan* plan);
+
+struct ScanParams {
+  const __nv_bfloat16* q;        // [B, Hq, 128]
+  const __nv_bfloat16* k;        // [num_blocks, bs, Hkv, 128]
+  const __nv_bfloat16* v;        // [num_blocks, bs, Hkv, 128]
+  const int* block_table;        // [B, max_blocks]
+  const int* seq_lens;           // [B]
+  __nv_bfloat16* out;            // [B, Hq, 128]; unused when out_partial
+  // Split partials.  FIXED: reference layout [B, Hq, num_splits](,128).
+  // BALANCED: slot layout [slot, HG*G](,128), slot = cta + row.
+  float* part_m;
+  float* part_l;
+  float* part_acc;
+  int* counters;                 // BALANCED: [rows * ncw] arrival counters
+  // out_partial: the final per-(b, q-head) state is written unnormalised
+  // here instead of bf16 `out` (KV-range sharding across GPUs).
+  float* res_m;                  // [B, Hq]
+  float* res_l;                  // [B, Hq]
+  float* res_acc;                // [B, Hq, 128]
+  int B, Hq, Hkv, bs, max_blocks;
+  int num_blocks;                // > 0: check block ids; 0: trust them
+  int G, NT, HG, NHG, ncw;
+  int row_bytes, row_stride, stage_bytes, nstages;
+  int schedule;                  // Schedule
+  int num_splits;                // FIXED
+  int out_partial;               // 0/1
+  float scale_log2;              // softmax scale * log2(e)
+};
+
+struct MergeParams {
+  const float* part_m;
+  const float* part_l;
+  const float* part_acc;
+  const int* seq_lens;
+  __nv_bfloat16* out;
+  int B, Hq, Hkv, bs, max_blocks, num_splits;
+};
+
+struct SimtParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const int* block_table;
+  const int* seq_lens;
+  __nv_bfloat16* out;
+  int B, Hq, Hkv, bs, max_blocks;
+  float scale_log2;
+};
+
+struct ShardMergeParams {
+  const float* m;    // [nshards, rows]
+  const float* l;    // [nshards, rows]
+  const float* acc;  // [nshards, rows, 128]
+  __nv_bfloat16* out;// [rows, 128]
+  int nshards;
+  int rows;          // B * Hq
+};
+
+// Kernel launchers (gqa_scan.cu / gqa_simt.cu).  They launch and return the
+// launch status; validation happens in the C-ABI layer.
+cudaError_t launch_scan(const ScanParams& p, int grid, int threads, int smem, cudaStream_t s);
+cudaError_t launch_fixed_merge(const MergeParams& p, cudaStream_t s);
+cudaError_t launch_simt(const SimtParams& p, cudaStream_t s);
+cudaError_t launch_shard_merge(const ShardMergeParams& p, cudaStream_t s);
+cudaError_t scan_kernel_set_smem(int smem_bytes);
+cudaError_t scan_kernel_occupancy(int threads, int smem_bytes, int* blocks_per_sm);
+cudaError_t read_status(int* status, int clear);
+
+}  // namespace gqa

@@ -1,0 +1,122 @@
+"""PyTorch entry points of the B200 paged GQA decode engine.
+
+Drop-in for the reference's python/binding.py (yuqiz7/mla-decode-kernels):
+``gqa_decode_v0``, ``gqa_decode_v1``, ``gqa_decode_v2(..., num_splits=8)``
+and the ``KERNELS`` registry (reference binding.py:25-31), with the same
+argument names, defaults and validation errors.  The reference JIT-builds an
+sm_90a extension at import; this module loads the in-tree sm_100a build
+(building it first if it is missing) and fails loudly if that is impossible -
+there is no CPU or eager fallback.
+
+Additions:
+  * ``gqa_decode(..., num_splits=0)``: the balanced single-launch schedule
+    (``num_splits=0``) or fixed splits, with a cached per-device workspace;
+    ``gqa_decode_v2(..., num_splits="auto")`` routes there too.
+  * ``gqa_decode_partial`` / ``merge_states``: unnormalised softmax states
+    for sharding one request's KV range across GPUs.
+"""
+
+import importlib.util
+import os
+import sys
+import threading
+
+import torch
+
+_PY_DIR = os.path.dirname(os.path.abspath(__file__))
+if _PY_DIR not in sys.path:
+    sys.path.insert(0, _PY_DIR)
+
+import gqa_build as _build  # noqa: E402
+
+
+def _load_ext():
+    if not os.path.exists(_build.LIB_PATH):
+        _build.build_lib()
+    _build.preload_lib()
+    if not os.path.exists(_build.EXT_PATH):
+        _build.build_ext()
+    spec = importlib.util.spec_from_file_location(_build.EXT_NAME, _build.EXT_PATH)
+    if spec is None:
+        raise ImportError(f"cannot load {_build.EXT_PATH}")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+_ext = _load_ext()
+
+LIB_PATH = _build.LIB_PATH
+EXT_PATH = _build.EXT_PATH
+
+gqa_decode_v0 = _ext.gqa_decode_v0
+gqa_decode_v1 = _ext.gqa_decode_v1
+merge_states = _ext.merge_states
+get_status = _ext.get_status
+pick_splits = _ext.pick_splits
+
+_ws_lock = threading.Lock()
+_ws_cache = {}
+
+
+def workspace(device, nbytes):
+    """Zero-initialised uint8 workspace of at least nbytes on device, cached.
+
+    The balanced schedule's arrival counters live at its start and every
+    launch leaves them at zero, so one zeroing serves all later launches.
+    """
+    device = torch.device(device)
+    key = (device.type, device.index)
+    with _ws_lock:
+        ws = _ws_cache.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(int(nbytes), 1 << 20)
+            if ws is not None:
+                size = max(size, 2 * ws.numel())
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _ws_cache[key] = ws
+        return ws
+
+
+def gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale, num_splits=0,
+               check_blocks=True, out=None):
+    """Paged GQA decode; num_splits=0 picks the balanced schedule.
+
+    check_blocks validates every block id against k_cache.shape[0] in the
+    kernel (an out-of-range id sets bit 1 of ``get_status()``).
+    """
+    if num_splits == "auto":
+        num_splits = 0
+    nbytes = _ext.workspace_bytes(q.shape[0], q.shape[1], k_cache.shape[2], int(num_splits)) \
+        if q.is_cuda else 0
+    ws = workspace(q.device, nbytes) if q.is_cuda else torch.empty(0, dtype=torch.uint8)
+    return _ext.gqa_decode(q, k_cache, v_cache, block_table, seq_lens, float(scale),
+                           int(num_splits), ws, bool(check_blocks), out)
+
+
+def gqa_decode_v2(q, k_cache, v_cache, block_table, seq_lens, scale, num_splits=8):
+    """Split-KV decode; identical contract to the reference's v2 (num_splits
+    in [1, 512], default 8).  num_splits="auto" selects the balanced
+    schedule of :func:`gqa_decode`."""
+    if num_splits == "auto":
+        return gqa_decode(q, k_cache, v_cache, block_table, seq_lens, scale, 0)
+    return _ext.gqa_decode_v2(q, k_cache, v_cache, block_table, seq_lens, scale,
+                              num_splits=num_splits)
+
+
+def gqa_decode_partial(q, k_cache, v_cache, block_table, seq_lens, scale, check_blocks=True):
+    """Unnormalised states (m, l, acc) per (request, q head): m and l [B, Hq]
+    in the log2 domain (m = max score*scale*log2(e)), acc [B, Hq, 128]."""
+    nbytes = _ext.workspace_bytes(q.shape[0], q.shape[1], k_cache.shape[2], 0)
+    ws = workspace(q.device, nbytes)
+    return _ext.gqa_decode_partial(q, k_cache, v_cache, block_table, seq_lens, float(scale), ws,
+                                   bool(check_blocks))
+
+
+# Reference registry (binding.py:31) plus the balanced schedule.
+KERNELS = {
+    "v0": gqa_decode_v0,
+    "v1": gqa_decode_v1,
+    "v2": gqa_decode_v2,
+    "auto": gqa_decode,
+}

@@ -1,0 +1,261 @@
+// PyTorch binding of the C ABI in include/gqa_decode.h.
+//
+// Mirrors the reference extension (python/gqa_decode_ext.cpp of
+// yuqiz7/mla-decode-kernels): the same three functions with the same
+// argument names, the same default num_splits = 8 and the same validation
+// messages (reference lines 16-62, 102-103), launching on the current torch
+// stream.  Everything below the tensor checks goes through the extern "C"
+// entry points of libgqa_decode_b200.so.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "gqa_decode.h"
+
+namespace {
+
+struct GqaDims {
+  int64_t B, Hq, Hkv, block_size, max_blocks, num_blocks;
+};
+
+GqaDims check_inputs(const torch::Tensor& q, const torch::Tensor& k_cache,
+                     const torch::Tensor& v_cache, const torch::Tensor& block_table,
+                     const torch::Tensor& seq_lens) {
+  TORCH_CHECK(q.is_cuda(), "q must be a CUDA tensor");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16, "q must be bf16");
+  TORCH_CHECK(q.is_contiguous(), "q must be contiguous");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128, "q must be [B, Hq, 128]");
+
+  TORCH_CHECK(k_cache.is_cuda() && v_cache.is_cuda(), "k_cache/v_cache must be CUDA tensors");
+  TORCH_CHECK(k_cache.scalar_type() == torch::kBFloat16 &&
+                  v_cache.scalar_type() == torch::kBFloat16,
+              "k_cache/v_cache must be bf16");
+  TORCH_CHECK(k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "k_cache/v_cache must be contiguous");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(3) == 128,
+              "k_cache must be [num_blocks, block_size, Hkv, 128]");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes(), "k_cache and v_cache must have the same shape");
+
+  TORCH_CHECK(block_table.is_cuda(), "block_table must be a CUDA tensor");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32, "block_table must be int32");
+  TORCH_CHECK(block_table.is_contiguous(), "block_table must be contiguous");
+  TORCH_CHECK(block_table.dim() == 2, "block_table must be [B, max_blocks]");
+
+  TORCH_CHECK(seq_lens.is_cuda(), "seq_lens must be a CUDA tensor");
+  TORCH_CHECK(seq_lens.scalar_type() == torch::kInt32, "seq_lens must be int32");
+  TORCH_CHECK(seq_lens.is_contiguous(), "seq_lens must be contiguous");
+  TORCH_CHECK(seq_lens.dim() == 1, "seq_lens must be [B]");
+
+  const int64_t B = q.size(0);
+  const int64_t Hq = q.size(1);
+  const int64_t Hkv = k_cache.size(2);
+  const int64_t block_size = k_cache.size(1);
+  const int64_t max_blocks = block_table.size(1);
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be divisible by Hkv");
+  TORCH_CHECK(block_table.size(0) == B, "block_table batch dim must match q");
+  TORCH_CHECK(seq_lens.size(0) == B, "seq_lens batch dim must match q");
+  TORCH_CHECK(q.device() == k_cache.device() && q.device() == v_cache.device() &&
+                  q.device() == block_table.device() && q.device() == seq_lens.device(),
+              "all tensors must be on the same device");
+  // Limits of this engine (not in the reference): the group fits 16 MMA
+  // column tiles, and the bulk-copy engine needs 16-byte aligned bases.
+  TORCH_CHECK(Hq / Hkv <= 128, "Hq / Hkv must be at most 128");
+  TORCH_CHECK(max_blocks >= 1, "block_table must have at least one column");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(k_cache.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(v_cache.data_ptr()) % 16 == 0,
+              "q/k_cache/v_cache must be 16-byte aligned");
+  TORCH_CHECK(B <= INT32_MAX && k_cache.size(0) <= INT32_MAX, "dimension too large");
+  return {B, Hq, Hkv, block_size, max_blocks, k_cache.size(0)};
+}
+
+const gqa_bf16* bf16_ptr(const torch::Tensor& t) {
+  return reinterpret_cast<const gqa_bf16*>(t.data_ptr());
+}
+
+void check_launch(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+using launch_fn_t = void (*)(const gqa_bf16*, const gqa_bf16*, const gqa_bf16*, const int*,
+                             const int*, gqa_bf16*, int, int, int, int, int, float, cudaStream_t);
+
+torch::Tensor gqa_decode_run(launch_fn_t launch, const char* name, torch::Tensor q,
+                             torch::Tensor k_cache, torch::Tensor v_cache,
+                             torch::Tensor block_table, torch::Tensor seq_lens, double scale) {
+  const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty_like(q);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  launch(bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache), block_table.data_ptr<int>(),
+         seq_lens.data_ptr<int>(), reinterpret_cast<gqa_bf16*>(out.data_ptr()),
+         static_cast<int>(d.B), static_cast<int>(d.Hq), static_cast<int>(d.Hkv),
+         static_cast<int>(d.block_size), static_cast<int>(d.max_blocks),
+         static_cast<float>(scale), stream);
+  check_launch(gqa_decode_last_error(), name);
+  return out;
+}
+
+}  // namespace
+
+torch::Tensor gqa_decode_v0(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_table, torch::Tensor seq_lens, double scale) {
+  return gqa_decode_run(gqa_decode_v0_launch, "gqa_decode_v0", q, k_cache, v_cache, block_table,
+                        seq_lens, scale);
+}
+
+torch::Tensor gqa_decode_v1(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_table, torch::Tensor seq_lens, double scale) {
+  return gqa_decode_run(gqa_decode_v1_launch, "gqa_decode_v1", q, k_cache, v_cache, block_table,
+                        seq_lens, scale);
+}
+
+torch::Tensor gqa_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                            torch::Tensor block_table, torch::Tensor seq_lens, double scale,
+                            int64_t num_splits) {
+  const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  TORCH_CHECK(num_splits >= 1 && num_splits <= 512, "num_splits must be in [1, 512]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty_like(q);
+  auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(q.device());
+  // Same per-call workspace as the reference extension (lines 106-109).
+  auto ws_acc = torch::empty({d.B, d.Hq, num_splits, 128}, f32);
+  auto ws_m = torch::empty({d.B, d.Hq, num_splits}, f32);
+  auto ws_l = torch::empty({d.B, d.Hq, num_splits}, f32);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  gqa_decode_v2_launch(bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache),
+                       block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),
+                       reinterpret_cast<gqa_bf16*>(out.data_ptr()), static_cast<int>(d.B),
+                       static_cast<int>(d.Hq), static_cast<int>(d.Hkv),
+                       static_cast<int>(d.block_size), static_cast<int>(d.max_blocks),
+                       static_cast<float>(scale), static_cast<int>(num_splits),
+                       ws_acc.data_ptr<float>(), ws_m.data_ptr<float>(), ws_l.data_ptr<float>(),
+                       stream);
+  check_launch(gqa_decode_last_error(), "gqa_decode_v2");
+  return out;
+}
+
+// Balanced (num_splits == 0) or fixed-split decode into `out` with a caller
+// workspace (uint8 CUDA tensor, zeroed once).  check_blocks validates every
+// block id against k_cache.size(0).
+torch::Tensor gqa_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                         torch::Tensor block_table, torch::Tensor seq_lens, double scale,
+                         int64_t num_splits, torch::Tensor workspace, bool check_blocks,
+                         c10::optional<torch::Tensor> out_opt) {
+  const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  TORCH_CHECK(num_splits >= 0 && num_splits <= 512, "num_splits must be in [0, 512]");
+  TORCH_CHECK(workspace.is_cuda() && workspace.device() == q.device() && workspace.is_contiguous(),
+              "workspace must be a contiguous CUDA tensor on q's device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = *out_opt;
+    TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == torch::kBFloat16 &&
+                    out.is_contiguous() && out.device() == q.device(),
+                "out must be a contiguous bf16 tensor shaped like q on q's device");
+  } else {
+    out = torch::empty_like(q);
+  }
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(
+      gqa_decode_launch(bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache),
+                        block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),
+                        reinterpret_cast<gqa_bf16*>(out.data_ptr()), static_cast<int>(d.B),
+                        static_cast<int>(d.Hq), static_cast<int>(d.Hkv),
+                        static_cast<int>(d.block_size), static_cast<int>(d.max_blocks),
+                        check_blocks ? static_cast<int>(d.num_blocks) : 0,
+                        static_cast<float>(scale), static_cast<int>(num_splits),
+                        workspace.data_ptr(), ws_bytes, stream),
+      "gqa_decode");
+  return out;
+}
+
+// Unnormalised per-(request, q head) softmax states (m, l, acc) for KV-range
+// sharding; see gqa_decode_partial_launch.
+std::vector<torch::Tensor> gqa_decode_partial(torch::Tensor q, torch::Tensor k_cache,
+                                              torch::Tensor v_cache, torch::Tensor block_table,
+                                              torch::Tensor seq_lens, double scale,
+                                              torch::Tensor workspace, bool check_blocks) {
+  const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  TORCH_CHECK(workspace.is_cuda() && workspace.device() == q.device() && workspace.is_contiguous(),
+              "workspace must be a contiguous CUDA tensor on q's device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(q.device());
+  auto m = torch::empty({d.B, d.Hq}, f32);
+  auto l = torch::empty({d.B, d.Hq}, f32);
+  auto acc = torch::empty({d.B, d.Hq, 128}, f32);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(gqa_decode_partial_launch(
+                   bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache), block_table.data_ptr<int>(),
+                   seq_lens.data_ptr<int>(), m.data_ptr<float>(), l.data_ptr<float>(),
+                   acc.data_ptr<float>(), static_cast<int>(d.B), static_cast<int>(d.Hq),
+                   static_cast<int>(d.Hkv), static_cast<int>(d.block_size),
+                   static_cast<int>(d.max_blocks), check_blocks ? static_cast<int>(d.num_blocks) : 0,
+                   static_cast<float>(scale), workspace.data_ptr(), ws_bytes, stream),
+               "gqa_decode_partial");
+  return {m, l, acc};
+}
+
+// Merge states [nshards, rows] (+ acc [nshards, rows, 128]) into bf16 [rows, 128].
+torch::Tensor merge_states(torch::Tensor m, torch::Tensor l, torch::Tensor acc) {
+  TORCH_CHECK(m.is_cuda() && l.is_cuda() && acc.is_cuda(), "states must be CUDA tensors");
+  TORCH_CHECK(m.scalar_type() == torch::kFloat32 && l.scalar_type() == torch::kFloat32 &&
+                  acc.scalar_type() == torch::kFloat32,
+              "states must be fp32");
+  TORCH_CHECK(m.is_contiguous() && l.is_contiguous() && acc.is_contiguous(),
+              "states must be contiguous");
+  TORCH_CHECK(m.dim() == 2 && l.sizes() == m.sizes() && acc.dim() == 3 &&
+                  acc.size(0) == m.size(0) && acc.size(1) == m.size(1) && acc.size(2) == 128,
+              "states must be m, l [n, rows] and acc [n, rows, 128]");
+  const c10::cuda::CUDAGuard guard(m.device());
+  auto out = torch::empty({m.size(1), 128},
+                          torch::TensorOptions().dtype(torch::kBFloat16).device(m.device()));
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_launch(gqa_decode_merge_states(m.data_ptr<float>(), l.data_ptr<float>(),
+                                       acc.data_ptr<float>(), static_cast<int>(m.size(0)),
+                                       static_cast<int>(m.size(1)),
+                                       reinterpret_cast<gqa_bf16*>(out.data_ptr()), stream),
+               "merge_states");
+  return out;
+}
+
+int64_t workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t num_splits) {
+  return static_cast<int64_t>(gqa_decode_workspace_bytes(
+      static_cast<int>(B), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(num_splits)));
+}
+
+int64_t get_status(bool clear) {
+  int s = 0;
+  check_launch(gqa_decode_get_status(&s, clear ? 1 : 0), "gqa_decode_get_status");
+  return s;
+}
+
+int64_t pick_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t seq_len, int64_t num_sms) {
+  return gqa_decode_pick_splits(static_cast<int>(B), static_cast<int>(Hq), static_cast<int>(Hkv),
+                                static_cast<int>(seq_len), static_cast<int>(num_sms));
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("gqa_decode_v0", &gqa_decode_v0, "GQA decode v0: CUDA-core grouped scan (paged KV, bf16)");
+  m.def("gqa_decode_v1", &gqa_decode_v1,
+        "GQA decode v1: pipelined TMA + tensor-core scan, unsplit (paged KV, bf16)");
+  m.def("gqa_decode_v2", &gqa_decode_v2, "GQA decode v2: split-KV scan + merge (paged KV, bf16)",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("scale"), py::arg("num_splits") = 8);
+  m.def("gqa_decode", &gqa_decode, "GQA decode, balanced (num_splits=0) or fixed splits",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("scale"), py::arg("num_splits"), py::arg("workspace"),
+        py::arg("check_blocks") = true, py::arg("out") = py::none());
+  m.def("gqa_decode_partial", &gqa_decode_partial, "unnormalised softmax states (m, l, acc)",
+        py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("scale"), py::arg("workspace"),
+        py::arg("check_blocks") = true);
+  m.def("merge_states", &merge_states, "merge per-shard softmax states into bf16 output");
+  m.def("workspace_bytes", &workspace_bytes, "workspace bytes for gqa_decode on this device");
+  m.def("get_status", &get_status, "device status word", py::arg("clear") = false);
+  m.def("pick_splits", &pick_splits, "fixed split count heuristic");
+}

@@ -1,0 +1,110 @@
+"""Multi-GPU decode: one process per GPU, torch.distributed for the plumbing.
+
+Two partitionings (the reference itself is single-GPU; its split-KV merge
+identity, kernels/gqa_decode/v2_splitkv.cu:97-107, is what crosses GPUs):
+
+* Batch sharding - independent requests are dealt to ranks (longest first,
+  to the rank with the least total tokens), each rank decodes its own
+  requests from its own KV pages.  No communication on the data path.
+
+* KV-range sharding - one long request's pages are cut into contiguous
+  ranges, one per rank.  Every rank computes the unnormalised softmax state
+  (m, l, acc) of its range with gqa_decode_partial, the states are
+  all-gathered in one packed fp32 buffer (Hq * 130 floats per request per
+  rank: 16.6 KB at Hq = 32) and every rank merges them with the CUDA merge
+  kernel, so all ranks end with the same output.
+"""
+
+import datetime
+import heapq
+
+import torch
+import torch.distributed as dist
+
+
+def lpt_shards(seq_lens, world):
+    """Request indices per rank, balancing the sum of seq_lens (LPT greedy).
+
+    Deterministic: ties are broken by request index and rank index.  Each
+    rank's list is sorted ascending.
+    """
+    seq_lens = [int(s) for s in seq_lens]
+    order = sorted(range(len(seq_lens)), key=lambda i: (-seq_lens[i], i))
+    heap = [(0, r) for r in range(world)]
+    shards = [[] for _ in range(world)]
+    for i in order:
+        load, r = heapq.heappop(heap)
+        shards[r].append(i)
+        heapq.heappush(heap, (load + seq_lens[i], r))
+    return [sorted(s) for s in shards]
+
+
+def kv_range(seq_len, block_size, rank, world):
+    """Token range [t0, t1) of `rank` when one request's pages are cut into
+    `world` contiguous page ranges of near-equal size (page boundaries keep
+    every rank's pages whole)."""
+    n_pages = (seq_len + block_size - 1) // block_size
+    p0 = n_pages * rank // world
+    p1 = n_pages * (rank + 1) // world
+    return min(seq_len, p0 * block_size), min(seq_len, p1 * block_size)
+
+
+def pack_states(m, l, acc):
+    """[m | l | acc] of one rank as a flat fp32 buffer of rows * 130 floats."""
+    rows = m.numel()
+    buf = torch.empty(rows * 130, dtype=torch.float32, device=m.device)
+    buf[:rows].copy_(m.reshape(-1))
+    buf[rows:2 * rows].copy_(l.reshape(-1))
+    buf[2 * rows:].copy_(acc.reshape(-1))
+    return buf
+
+
+def unpack_states(gathered, rows):
+    """Inverse of pack_states for gathered [world, rows * 130] buffers:
+    m, l [world, rows] and acc [world, rows, 128], all contiguous."""
+    world = gathered.shape[0]
+    m = gathered[:, :rows].contiguous()
+    l = gathered[:, rows:2 * rows].contiguous()
+    acc = gathered[:, 2 * rows:].contiguous().view(world, rows, 128)
+    return m, l, acc
+
+
+def init_process_group(backend, timeout_s=60):
+    """Process group from the torchrun environment with a short timeout, so a
+    rank that never arrives ends the others' collectives with an error."""
+    if not dist.is_initialized():
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=timeout_s))
+    return dist.group.WORLD
+
+
+class KVRangeDecoder:
+    """Decode requests whose KV range is split across the ranks of `group`.
+
+    Each rank passes only its own pages (local k/v caches, block table and
+    local token counts); decode() returns the full [B, Hq, 128] bf16 output
+    on every rank.
+    """
+
+    def __init__(self, group=None):
+        from binding import gqa_decode_partial, merge_states  # CUDA extension
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self._partial = gqa_decode_partial
+        self._merge = merge_states
+        self._gathered = None
+
+    def decode(self, q, k_local, v_local, block_table_local, seq_lens_local, scale):
+        m, l, acc = self._partial(q, k_local, v_local, block_table_local, seq_lens_local, scale)
+        B, Hq = q.shape[0], q.shape[1]
+        rows = B * Hq
+        if self.world == 1:
+            out = self._merge(m.view(1, rows), l.view(1, rows), acc.view(1, rows, 128))
+            return out.view(B, Hq, 128)
+        buf = pack_states(m, l, acc)
+        if self._gathered is None or self._gathered.shape != (self.world, buf.numel()):
+            self._gathered = torch.empty(self.world, buf.numel(), dtype=torch.float32,
+                                         device=buf.device)
+        dist.all_gather_into_tensor(self._gathered, buf, group=self.group)
+        mm, ll, aa = unpack_states(self._gathered, rows)
+        return self._merge(mm, ll, aa).view(B, Hq, 128)

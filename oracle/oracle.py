@@ -1,0 +1,154 @@
+"""ctypes front end of the CPU oracle (gqa_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg as the checker.  It restates the reference's
+python/reference.py (gather_kv :7-18, attention_ref :21-40) in C; its
+outputs are pinned against reference.py itself through the fixtures in
+tests/golden/.
+"""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import torch
+
+ORACLE_DIR = os.path.dirname(os.path.abspath(__file__))
+BUILD_DIR = os.path.join(ORACLE_DIR, "_build")
+REF_LIB = os.path.join(ORACLE_DIR, "_ref", "libref_gqa.so")
+
+
+def _cpu_has_avx2_fma():
+    try:
+        with open("/proc/cpuinfo") as f:
+            flags = f.read()
+        return " avx2" in flags and " fma" in flags
+    except OSError:
+        return False
+
+
+def build(reference_dir=None):
+    """make the oracle (and, with a reference checkout, the _ref kernels)."""
+    subprocess.run(["make", "-s", "-C", ORACLE_DIR], check=True)
+    if reference_dir and os.path.isdir(reference_dir):
+        subprocess.run(["make", "-s", "-C", ORACLE_DIR, "ref", f"REF={reference_dir}"], check=True)
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        name = "liboracle_avx2.so" if _cpu_has_avx2_fma() else "liboracle_base.so"
+        path = os.path.join(BUILD_DIR, name)
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        p = ctypes.c_void_p
+        i = ctypes.c_int
+        f = ctypes.c_float
+        L.oracle_attention_ref.argtypes = [p, p, p, p, p, i, i, i, i, i, f, p, i]
+        L.oracle_attention_ref.restype = None
+        L.oracle_attention_state.argtypes = [p, p, p, p, p, i, i, i, i, i, f, p, p, p, i]
+        L.oracle_attention_state.restype = None
+        L.oracle_online_softmax.argtypes = [p, p, i, i, p, p, p]
+        L.oracle_online_softmax.restype = None
+        L.oracle_merge_states.argtypes = [p, p, p, i, i, p, p, p]
+        L.oracle_merge_states.restype = None
+        i64 = ctypes.c_int64
+        L.oracle_nhd_index.argtypes = [i64, i64, i64, i64, i64, i64]
+        L.oracle_nhd_index.restype = i64
+        _lib = L
+    return _lib
+
+
+def default_threads():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def _bits(t):
+    """CPU contiguous uint16 numpy view of a bf16 tensor."""
+    t = t.detach().to("cpu").contiguous()
+    assert t.dtype == torch.bfloat16
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+def _i32(t):
+    return np.ascontiguousarray(t.detach().to("cpu").numpy().astype(np.int32, copy=False))
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def attention_ref(q, k_cache, v_cache, block_table, seq_lens, scale, nthreads=None):
+    """fp32 out [B, Hq, 128] (torch CPU tensor), reference.py semantics."""
+    B, Hq, D = q.shape
+    assert D == 128
+    Hkv, bs = k_cache.shape[2], k_cache.shape[1]
+    qb, kb, vb = _bits(q), _bits(k_cache), _bits(v_cache)
+    bt, sl = _i32(block_table), _i32(seq_lens)
+    out = np.empty((B, Hq, D), dtype=np.float32)
+    lib().oracle_attention_ref(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(bt), _ptr(sl), B, Hq, Hkv, bs,
+                               bt.shape[1], float(scale), _ptr(out),
+                               nthreads or default_threads())
+    return torch.from_numpy(out)
+
+
+def attention_state(q, k_cache, v_cache, block_table, seq_lens, scale, nthreads=None):
+    """Unnormalised (m, l, acc) in natural-log units: m, l [B, Hq], acc [B, Hq, 128]."""
+    B, Hq, D = q.shape
+    Hkv, bs = k_cache.shape[2], k_cache.shape[1]
+    qb, kb, vb = _bits(q), _bits(k_cache), _bits(v_cache)
+    bt, sl = _i32(block_table), _i32(seq_lens)
+    m = np.empty((B, Hq), dtype=np.float32)
+    l = np.empty((B, Hq), dtype=np.float32)
+    acc = np.empty((B, Hq, D), dtype=np.float32)
+    lib().oracle_attention_state(_ptr(qb), _ptr(kb), _ptr(vb), _ptr(bt), _ptr(sl), B, Hq, Hkv,
+                                 bs, bt.shape[1], float(scale), _ptr(m), _ptr(l), _ptr(acc),
+                                 nthreads or default_threads())
+    return torch.from_numpy(m), torch.from_numpy(l), torch.from_numpy(acc)
+
+
+def online_softmax(scores, values):
+    s = np.ascontiguousarray(scores, dtype=np.float32)
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    n, dv = v.shape
+    m = np.zeros(1, np.float32)
+    l = np.zeros(1, np.float32)
+    acc = np.zeros(dv, np.float32)
+    lib().oracle_online_softmax(_ptr(s), _ptr(v), n, dv, _ptr(m), _ptr(l), _ptr(acc))
+    return float(m[0]), float(l[0]), acc
+
+
+def merge_states(m, l, acc):
+    m = np.ascontiguousarray(m, dtype=np.float32)
+    l = np.ascontiguousarray(l, dtype=np.float32)
+    acc = np.ascontiguousarray(acc, dtype=np.float32)
+    n, dv = acc.shape
+    mo = np.zeros(1, np.float32)
+    lo = np.zeros(1, np.float32)
+    ao = np.zeros(dv, np.float32)
+    lib().oracle_merge_states(_ptr(m), _ptr(l), _ptr(acc), n, dv, _ptr(mo), _ptr(lo), _ptr(ao))
+    return float(mo[0]), float(lo[0]), ao
+
+
+def nhd_index(p, s, bs, Hkv, h, j):
+    return int(lib().oracle_nhd_index(p, s, bs, Hkv, h, j))
+
+
+def ref_kernels():
+    """The reference's own v1/v2 kernels built for sm_100a (oracle/_ref), or None."""
+    if not os.path.exists(REF_LIB):
+        return None
+    L = ctypes.CDLL(REF_LIB)
+    p = ctypes.c_void_p
+    i = ctypes.c_int
+    f = ctypes.c_float
+    L.ref_gqa_decode_v1.argtypes = [p, p, p, p, p, p, i, i, i, i, i, f, p]
+    L.ref_gqa_decode_v1.restype = i
+    L.ref_gqa_decode_v2.argtypes = [p, p, p, p, p, p, i, i, i, i, i, f, i, p, p, p, p]
+    L.ref_gqa_decode_v2.restype = i
+    return L

@@ -1,0 +1,128 @@
+"""CPU: the C-ABI library loads, exports every declared entry point, and its
+host-only planning functions behave.  No call here touches a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+import gqa_build as pkg_build
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "gqa_decode.h")
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [("group", ctypes.c_int), ("heads_per_row", ctypes.c_int),
+                ("consumer_warps", ctypes.c_int), ("threads", ctypes.c_int),
+                ("stages", ctypes.c_int), ("smem_bytes", ctypes.c_int), ("grid", ctypes.c_int),
+                ("workspace_bytes", ctypes.c_size_t)]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(pkg_build.LIB_PATH):
+        pkg_build.build_lib()
+    L = ctypes.CDLL(pkg_build.LIB_PATH)
+    L.gqa_decode_query_plan.argtypes = [ctypes.c_int] * 6 + [ctypes.POINTER(Plan)]
+    L.gqa_decode_query_plan.restype = ctypes.c_int
+    L.gqa_decode_pick_splits.argtypes = [ctypes.c_int] * 5
+    L.gqa_decode_pick_splits.restype = ctypes.c_int
+    L.gqa_decode_version.restype = ctypes.c_char_p
+    return L
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[\w]+\s*\*?\s+(gqa_decode_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_reference_launchers():
+    names = declared_functions()
+    for n in ["gqa_decode_v0_launch", "gqa_decode_v1_launch", "gqa_decode_v2_launch"]:
+        assert n in names
+    assert len(names) >= 13
+
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_symbol_exported(lib, name):
+    assert hasattr(lib, name), f"{name} declared in include/gqa_decode.h but not exported"
+
+
+def test_symbols_are_c_linkage():
+    # extern "C": the dynamic symbol table holds the plain names.
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg_build.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    syms = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    for name in declared_functions():
+        assert name in syms
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.gqa_decode_version()
+
+
+def plan(lib, B, Hq, Hkv, ns=0, sms=148, per_sm=1):
+    p = Plan()
+    rc = lib.gqa_decode_query_plan(B, Hq, Hkv, ns, sms, per_sm, ctypes.byref(p))
+    return rc, p
+
+
+def test_plan_rep_shape(lib):
+    rc, p = plan(lib, 32, 32, 8)
+    assert rc == 0
+    assert p.group == 4 and p.heads_per_row == 8 and p.consumer_warps == 8
+    assert p.threads == 288
+    assert p.stages == 3
+    assert p.smem_bytes <= 227 * 1024
+    assert p.grid == 148
+    # counters (32 rows x 8 warps) + m, l, acc for (148 + 32) slots x 32 heads
+    slots, qhr = 148 + 32, 32
+    expect = 1024 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4
+    assert p.workspace_bytes == expect
+
+
+@pytest.mark.parametrize("Hq,Hkv,hg,ncw", [(64, 8, 8, 8), (32, 8, 8, 8), (64, 4, 4, 8),
+                                           (128, 8, 4, 8), (32, 1, 1, 4), (8, 8, 8, 8),
+                                           (24, 8, 8, 8), (256, 2, 1, 16)])
+def test_plan_head_mapping(lib, Hq, Hkv, hg, ncw):
+    rc, p = plan(lib, 4, Hq, Hkv)
+    assert rc == 0
+    assert p.heads_per_row == hg and p.consumer_warps == ncw
+    assert p.threads == 32 * (ncw + 1)
+    assert 2 <= p.stages <= 8 and p.smem_bytes <= 227 * 1024
+
+
+def test_plan_rejects_bad_shapes(lib):
+    assert plan(lib, 4, 30, 8)[0] == -1   # Hq % Hkv != 0
+    assert plan(lib, 4, 0, 8)[0] == -1
+    assert plan(lib, 4, 129 * 8, 8)[0] == -2  # group of 129 heads
+    assert plan(lib, 4, 32, 8, ns=513)[0] == -1
+
+
+def test_plan_fixed_workspace_matches_reference_layout(lib):
+    # [B, Hq, ns, 128] + [B, Hq, ns] x 2, fp32 (python/gqa_decode_ext.cpp:106-109)
+    rc, p = plan(lib, 32, 32, 8, ns=8)
+    states = 32 * 32 * 8
+    assert p.workspace_bytes == states * 128 * 4 + 2 * ((states * 4 + 255) // 256 * 256)
+    assert p.grid == min(148, 32 * 8)
+    rc, p = plan(lib, 32, 32, 8, ns=1)
+    assert p.workspace_bytes == 0 and p.grid == 32
+
+
+def test_pick_splits(lib):
+    # rep shape: 32 rows; the chosen count fills the waves it uses to >= 90 %.
+    ns = lib.gqa_decode_pick_splits(32, 32, 8, 8192, 148)
+    assert 1 < ns <= 512
+    tasks = 32 * ns
+    waves = -(-tasks // 148)
+    assert tasks / (waves * 148) >= 0.9
+    # one long request: many splits
+    assert lib.gqa_decode_pick_splits(1, 32, 8, 262144, 148) >= 100
+    # a batch that already fills the GPU several times: no split
+    assert lib.gqa_decode_pick_splits(4096, 32, 8, 512, 148) == 1
+    assert lib.gqa_decode_pick_splits(0, 32, 8, 512, 148) == 1

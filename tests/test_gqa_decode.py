@@ -1,0 +1,355 @@
+"""GPU parity tests: every kernel against the CPU oracle and against the
+reference's own outputs (tests/golden), through the C ABI.
+
+Mirrors the reference's tests/test_gqa_decode.py (case table :89-98,
+NaN-poisoned pools :27-69, num_splits sweep and bitwise num_splits=1 == v1
+:109-121, len-1 with 8 splits :124-128, large logits :131-139) with the
+tolerance tightened to the north star's atol = rtol = 1e-2 (the reference
+used 2e-2): bf16 output rounding is ~2^-9 relative, P is rounded to bf16
+before the PV product (another ~2^-9 per weight), and the accumulation
+order differs from the oracle's.
+"""
+
+import ctypes
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import binding
+import cases
+import oracle
+from golden.make_golden import golden_cases, q_transform
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2
+RTOL = 1e-2
+SCALE = 1.0 / math.sqrt(128)
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
+KERNEL_NAMES = ["v0", "v1", "v2", "auto"]
+
+
+def to_gpu(case):
+    return tuple(t.cuda() for t in case)
+
+
+def assert_close(out, ref, what=""):
+    out_f = out.float().cpu()
+    ref = ref.float().cpu()
+    if not torch.allclose(out_f, ref, atol=ATOL, rtol=RTOL):
+        err = (out_f - ref).abs()
+        rel = err / ref.abs().clamp_min(1e-8)
+        pytest.fail(f"{what} mismatch: max-abs={err.max().item():.4e} "
+                    f"max-rel={rel.max().item():.4e}")
+
+
+def check_status():
+    assert binding.get_status(True) == 0, "device status word set (wait timeout / bad block id)"
+
+
+def run_and_check(kernel_fn, case_cpu, check_finite=False):
+    gpu = to_gpu(case_cpu)
+    out = kernel_fn(*gpu, SCALE)
+    torch.cuda.synchronize()
+    check_status()
+    if check_finite:
+        assert torch.isfinite(out.float()).all(), "kernel output has NaN/inf"
+    ref = oracle.attention_ref(*case_cpu, SCALE)
+    assert_close(out, ref)
+    return out
+
+
+# ---- the reference's case table ------------------------------------------------
+
+@pytest.mark.parametrize("kernel", KERNEL_NAMES)
+@pytest.mark.parametrize("name", list(cases.REF_CASES.keys()))
+def test_gqa_decode(kernel, name):
+    run_and_check(binding.KERNELS[kernel], cases.ref_case(name, seed=0))
+
+
+@pytest.mark.parametrize("num_splits", [1, 3, 8, 32, 512])
+def test_v2_num_splits(num_splits):
+    case = cases.ref_case("a_base", seed=0)
+    run_and_check(lambda *a: binding.gqa_decode_v2(*a, num_splits=num_splits), case)
+    if num_splits == 1:
+        # One split runs exactly the unsplit scan's arithmetic.
+        gpu = to_gpu(case)
+        out_v2 = binding.gqa_decode_v2(*gpu, SCALE, num_splits=1)
+        out_v1 = binding.gqa_decode_v1(*gpu, SCALE)
+        assert torch.equal(out_v2, out_v1), "v2(num_splits=1) != v1 bitwise"
+
+
+def test_v2_len1_splits8():
+    # S=1 with 8 splits: 7 empty segments must contribute nothing.
+    run_and_check(lambda *a: binding.gqa_decode_v2(*a, num_splits=8),
+                  cases.ref_case("c_len1", seed=0))
+
+
+@pytest.mark.parametrize("kernel", KERNEL_NAMES)
+def test_gqa_decode_large_logits(kernel):
+    q, k, v, bt, sl = cases.ref_case("a_base", seed=0)
+    q = (q.float() * 50.0).to(torch.bfloat16)
+    run_and_check(binding.KERNELS[kernel], (q, k, v, bt, sl), check_finite=True)
+
+
+@pytest.mark.parametrize("num_splits", [0, 1, 8, 64])
+def test_num_splits_through_extended_api(num_splits):
+    run_and_check(lambda *a: binding.gqa_decode(*a, num_splits=num_splits),
+                  cases.ref_case("i_8k", seed=0))
+
+
+# ---- against the reference's own outputs (tests/golden) ----------------------
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+@pytest.mark.parametrize("kernel", KERNEL_NAMES)
+@pytest.mark.parametrize("name", list(golden_cases().keys()))
+def test_matches_reference_py_outputs(golden, kernel, name):
+    builder, _ = golden_cases()[name]
+    q, k, v, bt, sl = builder()
+    q = q_transform(name, q)
+    out = binding.KERNELS[kernel](*to_gpu((q, k, v, bt, sl)), SCALE)
+    torch.cuda.synchronize()
+    check_status()
+    assert torch.isfinite(out.float()).all()
+    assert_close(out, torch.from_numpy(golden[name + "/out"]), f"{kernel}/{name}")
+
+
+def test_empty_request_gives_zero():
+    case = cases.make_case([50, 0, 17], 32, 8, 16, seed=17)
+    for kernel in KERNEL_NAMES:
+        out = binding.KERNELS[kernel](*to_gpu(case), SCALE)
+        torch.cuda.synchronize()
+        assert torch.all(out[1].float() == 0), kernel
+    check_status()
+
+
+def test_all_requests_empty():
+    case = cases.make_case([0, 0], 32, 8, 16, seed=18, pool_blocks=4)
+    for kernel in KERNEL_NAMES:
+        out = binding.KERNELS[kernel](*to_gpu(case), SCALE)
+        torch.cuda.synchronize()
+        assert torch.all(out.float() == 0), kernel
+    check_status()
+
+
+@pytest.mark.parametrize("Hq,Hkv,bs", [(8, 8, 16), (24, 8, 16), (64, 4, 16), (128, 8, 16),
+                                       (32, 1, 16), (32, 2, 1), (32, 8, 8), (32, 8, 32),
+                                       (16, 16, 16), (256, 2, 16)])
+def test_head_and_block_shapes(Hq, Hkv, bs):
+    case = cases.make_case([1, 15, 16, 17, 333, 1029], Hq, Hkv, bs, seed=19, value_scale=0.5)
+    for kernel in KERNEL_NAMES:
+        run_and_check(binding.KERNELS[kernel], case)
+
+
+def test_determinism():
+    gpu = to_gpu(cases.ref_case("i_8k", seed=1))
+    for kernel in KERNEL_NAMES:
+        a = binding.KERNELS[kernel](*gpu, SCALE)
+        b = binding.KERNELS[kernel](*gpu, SCALE)
+        assert torch.equal(a, b), kernel
+
+
+# ---- BASELINE configurations at full size --------------------------------------
+
+def check_subset(out, case_gpu, requests):
+    sub = cases.subset(case_gpu, requests)
+    ref = oracle.attention_ref(*sub, SCALE)
+    assert_close(out[list(requests)], ref)
+
+
+def test_config1():
+    run_and_check(binding.gqa_decode, cases.config1())
+
+
+def test_config2_rep_full_size():
+    case = cases.config2(device="cuda")
+    outs = {}
+    for ns in ["auto", 1, 8, 16, 32]:
+        outs[ns] = binding.gqa_decode_v2(*case, SCALE, num_splits=ns)
+    torch.cuda.synchronize()
+    check_status()
+    for ns, out in outs.items():
+        check_subset(out, case, [0, 17, 31])
+        assert torch.isfinite(out.float()).all()
+    assert torch.equal(outs[1], binding.gqa_decode_v1(*case, SCALE))
+    # Size-independent cross-check: every schedule agrees on every request.
+    for ns in [8, 16, 32]:
+        assert_close(outs[ns], outs["auto"], f"splits {ns} vs auto")
+
+
+def test_config3_wide_group():
+    case = cases.config3(device="cuda", B=16)
+    out = binding.gqa_decode(*case, SCALE)
+    torch.cuda.synchronize()
+    check_status()
+    check_subset(out, case, [0, 15])
+    assert_close(binding.gqa_decode_v2(*case, SCALE, num_splits=16), out)
+
+
+def test_config4_ragged():
+    case = cases.config4(device="cuda")
+    out = binding.gqa_decode(*case, SCALE)
+    torch.cuda.synchronize()
+    check_status()
+    assert torch.isfinite(out.float()).all()
+    sl = case[4].cpu()
+    pick = {int(sl.argmin()), int(sl.argmax()), 0, 128, 255}
+    check_subset(out, case, sorted(pick))
+    assert_close(binding.gqa_decode_v2(*case, SCALE, num_splits=8), out)
+
+
+@pytest.mark.parametrize("k_scale", [1.0, 8.0])
+def test_config5_long_context(k_scale):
+    case = cases.config5(device="cuda", k_scale=k_scale)
+    out = binding.gqa_decode(*case, SCALE)
+    torch.cuda.synchronize()
+    check_status()
+    assert torch.isfinite(out.float()).all()
+    check_subset(out, case, [0])
+
+
+# ---- KV-range sharding (emulated on one GPU) and partial states ---------------
+
+def test_partial_states_match_oracle():
+    case_cpu = cases.make_case([700, 1, 2049], 32, 8, 16, seed=23)
+    m, l, acc = binding.gqa_decode_partial(*to_gpu(case_cpu), SCALE)
+    torch.cuda.synchronize()
+    om, ol, oacc = oracle.attention_state(*case_cpu, SCALE)
+    # kernel m is in log2 units
+    np.testing.assert_allclose((m.cpu() / math.log2(math.e)).numpy(), om.numpy(), atol=1e-3,
+                               rtol=1e-3)
+    np.testing.assert_allclose(l.cpu().numpy(), ol.numpy(), rtol=1e-2)
+    np.testing.assert_allclose(acc.cpu().numpy(), oacc.numpy(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("nshards", [2, 4, 8])
+@pytest.mark.parametrize("k_scale", [1.0, 8.0])
+def test_kv_range_sharding_emulated(nshards, k_scale):
+    import sharding
+
+    S, bs = 65536, 64
+    case = cases.make_case([S], 32, 8, bs, seed=24, pool_factor=1.0, k_scale=k_scale,
+                           device="cuda")
+    q, k, v, bt, sl = case
+    states = []
+    for r in range(nshards):
+        t0, t1 = sharding.kv_range(S, bs, r, nshards)
+        bt_r = bt[:, t0 // bs:(t1 + bs - 1) // bs].contiguous()
+        sl_r = torch.tensor([t1 - t0], dtype=torch.int32, device="cuda")
+        states.append(binding.gqa_decode_partial(q, k, v, bt_r, sl_r, SCALE))
+    packed = torch.stack([sharding.pack_states(*s) for s in states])
+    mm, ll, aa = sharding.unpack_states(packed, 32)
+    out = binding.merge_states(mm, ll, aa).view(1, 32, 128)
+    torch.cuda.synchronize()
+    check_status()
+    full = binding.gqa_decode(*case, SCALE)
+    assert_close(out, full, "sharded vs single")
+    check_subset(out, case, [0])
+
+
+def test_merge_states_all_empty_shards():
+    m = torch.full((3, 5), -float("inf"), device="cuda")
+    l = torch.zeros(3, 5, device="cuda")
+    acc = torch.zeros(3, 5, 128, device="cuda")
+    out = binding.merge_states(m, l, acc)
+    torch.cuda.synchronize()
+    assert torch.all(out.float() == 0)
+
+
+# ---- guards ---------------------------------------------------------------------
+
+def test_bad_block_id_sets_status_without_fault():
+    # The kernel's own range check turns an out-of-range block id into status
+    # bit 1 and reads block 0 instead; the launch itself stays in bounds.
+    q, k, v, bt, sl = cases.make_case([40, 40], 32, 8, 16, seed=25)
+    bt = bt.clone()
+    bt[1, 1] = k.shape[0] + 7
+    binding.get_status(True)
+    out = binding.gqa_decode(*to_gpu((q, k, v, bt, sl)), SCALE, check_blocks=True)
+    torch.cuda.synchronize()
+    assert binding.get_status(True) & 2
+    ref = oracle.attention_ref(q[:1], k, v, bt[:1], sl[:1], SCALE)
+    assert_close(out[:1], ref)
+
+
+def test_cuda_graph_replay():
+    q, k, v, bt, sl = to_gpu(cases.ref_case("a_base", seed=3))
+    eager = binding.gqa_decode(q, k, v, bt, sl, SCALE)
+    out = torch.empty_like(q)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        binding.gqa_decode(q, k, v, bt, sl, SCALE, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        binding.gqa_decode(q, k, v, bt, sl, SCALE, out=out)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+
+
+def test_raw_c_abi_v2_launch():
+    # The reference launcher signature called straight through ctypes with a
+    # caller-owned workspace on torch's stream.
+    lib = ctypes.CDLL(binding.LIB_PATH)
+    case = to_gpu(cases.ref_case("a_base", seed=4))
+    q, k, v, bt, sl = case
+    B, Hq = q.shape[:2]
+    ns = 8
+    out = torch.empty_like(q)
+    ws_acc = torch.empty(B, Hq, ns, 128, device="cuda")
+    ws_m = torch.empty(B, Hq, ns, device="cuda")
+    ws_l = torch.empty(B, Hq, ns, device="cuda")
+    p = ctypes.c_void_p
+    i = ctypes.c_int
+    lib.gqa_decode_v2_launch.argtypes = [p] * 6 + [i] * 5 + [ctypes.c_float, i, p, p, p, p]
+    lib.gqa_decode_v2_launch.restype = None
+    lib.gqa_decode_last_error.restype = ctypes.c_int
+    lib.gqa_decode_v2_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), bt.data_ptr(),
+                             sl.data_ptr(), out.data_ptr(), B, Hq, k.shape[2], k.shape[1],
+                             bt.shape[1], SCALE, ns, ws_acc.data_ptr(), ws_m.data_ptr(),
+                             ws_l.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert lib.gqa_decode_last_error() == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, binding.gqa_decode_v2(*case, SCALE, num_splits=ns))
+    # invalid split count: nothing launched, error reported
+    lib.gqa_decode_v2_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), bt.data_ptr(),
+                             sl.data_ptr(), out.data_ptr(), B, Hq, k.shape[2], k.shape[1],
+                             bt.shape[1], SCALE, 0, ws_acc.data_ptr(), ws_m.data_ptr(),
+                             ws_l.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert lib.gqa_decode_last_error() != 0
+
+
+def test_v2_rejects_bad_num_splits():
+    case = to_gpu(cases.ref_case("c_len1", seed=0))
+    with pytest.raises(RuntimeError, match=r"num_splits must be in \[1, 512\]"):
+        binding.gqa_decode_v2(*case, SCALE, num_splits=513)
+
+
+def test_reference_kernels_built_for_sm100_agree():
+    # The reference's own v1/v2 kernels, compiled from their sources for
+    # sm_100a (oracle/_ref), as an independent GPU-side checker.
+    ref = oracle.ref_kernels()
+    if ref is None:
+        pytest.skip("oracle/_ref not built (needs the reference checkout at build time)")
+    case_cpu = cases.ref_case("a_base", seed=0)
+    q, k, v, bt, sl = to_gpu(case_cpu)
+    B, Hq = q.shape[:2]
+    out_ref = torch.empty_like(q)
+    rc = ref.ref_gqa_decode_v1(q.data_ptr(), k.data_ptr(), v.data_ptr(), bt.data_ptr(),
+                               sl.data_ptr(), out_ref.data_ptr(), B, Hq, k.shape[2], k.shape[1],
+                               bt.shape[1], SCALE, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ours = binding.gqa_decode(q, k, v, bt, sl, SCALE)
+    assert_close(out_ref, oracle.attention_ref(*case_cpu, SCALE), "reference v1 (sm_100a)")
+    assert_close(ours, out_ref, "ours vs reference v1 (sm_100a)")

@@ -1,0 +1,158 @@
+"""CPU: the oracle pinned against the reference's own outputs and worked examples.
+
+* golden.npz holds python/reference.py:attention_ref outputs (made by
+  tests/golden/make_golden.py from the unmodified reference);
+* known-answer traces from docs/k1/notes_w1.md (online softmax :74-86,
+  split merge :88-95, NHD index :55-68);
+* the SDPA cross-check of tests/test_reference.py:13-23.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import cases
+import oracle
+from golden.make_golden import golden_cases, input_digest, q_transform
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
+SCALE = 1.0 / math.sqrt(128)
+# fp32 vs fp32 with a different summation order (the reference's own
+# oracle-vs-SDPA check uses 1e-5 max-abs, tests/test_reference.py:23).
+PIN_ATOL = 2e-5
+PIN_RTOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return np.load(GOLDEN)
+
+
+@pytest.mark.parametrize("name", list(golden_cases().keys()))
+def test_oracle_matches_reference_outputs(golden, name):
+    builder, _ = golden_cases()[name]
+    q, k, v, bt, sl = builder()
+    q = q_transform(name, q)
+    assert input_digest((q, k, v, bt, sl)) == str(golden[name + "/digest"]), \
+        "regenerated inputs differ from the ones the fixture was made from"
+    out = oracle.attention_ref(q, k, v, bt, sl, SCALE).numpy()
+    ref = golden[name + "/out"]
+    assert np.isfinite(ref).all()
+    np.testing.assert_allclose(out, ref, atol=PIN_ATOL, rtol=PIN_RTOL)
+
+
+def test_empty_request_is_zero(golden):
+    # reference.py returns zeros for seq_len == 0 (softmax of an empty row).
+    ref = golden["empty_request/out"]
+    assert np.all(ref[1] == 0.0)
+
+
+def test_online_softmax_trace():
+    # docs/k1/notes_w1.md:74-86: scores [2,5,1,6], 2-d values.
+    scores = [2.0, 5.0, 1.0, 6.0]
+    values = [[1, 0], [0, 1], [1, 1], [2, 0]]
+    m, l, acc = oracle.online_softmax(scores, values)
+    assert m == 6.0
+    assert l == pytest.approx(1.392933, abs=1e-6)
+    np.testing.assert_allclose(acc, [2.025054, 0.374618], atol=1e-6)
+    np.testing.assert_allclose(acc / l, [1.4538, 0.2689], atol=1e-4)
+
+
+def test_split_merge_trace():
+    # docs/k1/notes_w1.md:88-95: split {t0,t1} and {t2,t3}, merged.
+    values = np.array([[1, 0], [0, 1], [1, 1], [2, 0]], dtype=np.float32)
+    m1, l1, a1 = oracle.online_softmax([2.0, 5.0], values[:2])
+    m2, l2, a2 = oracle.online_softmax([1.0, 6.0], values[2:])
+    assert (m1, m2) == (5.0, 6.0)
+    assert l1 == pytest.approx(1.049787, abs=1e-6)
+    assert l2 == pytest.approx(1.006738, abs=1e-6)
+    np.testing.assert_allclose(a1, [0.049787, 1.0], atol=1e-6)
+    np.testing.assert_allclose(a2, [2.006738, 0.006738], atol=1e-6)
+    M, L, A = oracle.merge_states([m1, m2], [l1, l2], np.stack([a1, a2]))
+    assert M == 6.0
+    assert L == pytest.approx(1.392933, abs=1e-6)
+    np.testing.assert_allclose(A, [2.025054, 0.374617], atol=2e-6)
+    np.testing.assert_allclose(A / L, [1.4538, 0.2689], atol=1e-4)
+
+
+def test_merge_all_empty_is_neutral():
+    M, L, A = oracle.merge_states([-np.inf, -np.inf], [0.0, 0.0], np.zeros((2, 3)))
+    assert M == -np.inf and L == 0.0 and np.all(A == 0)
+
+
+def test_nhd_index_worked_example():
+    # docs/k1/notes_w1.md:59-68: bs=16, Hkv=8, h=3, t=20, block_table=[9,2,14].
+    bt = [9, 2, 14]
+    t, bs = 20, 16
+    idx = oracle.nhd_index(bt[t // bs], t % bs, bs, 8, 3, 0)
+    assert idx == 37248
+    assert idx * 2 == 74496
+    # int32 overflow point noted at notes_w1.md:70-72: 2^32 elements.
+    assert oracle.nhd_index(128 * 32768 // 16, 0, 16, 8, 0, 0) == 2 ** 32
+
+
+@pytest.mark.parametrize("B,S,Hq,Hkv", [(2, [37, 100], 32, 8), (1, [1], 32, 8),
+                                        (3, [16, 17, 64], 64, 8)])
+def test_oracle_matches_sdpa(B, S, Hq, Hkv):
+    # Shapes of tests/test_reference.py:14-20, identity block table.
+    g = torch.Generator().manual_seed(0)
+    bs = 16
+    max_blocks = (max(S) + bs - 1) // bs
+    nblk = B * max_blocks
+    q = torch.randn(B, Hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(nblk, bs, Hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(nblk, bs, Hkv, 128, generator=g).to(torch.bfloat16)
+    bt = torch.arange(nblk, dtype=torch.int32).reshape(B, max_blocks)
+    sl = torch.tensor(S, dtype=torch.int32)
+    out = oracle.attention_ref(q, k, v, bt, sl, SCALE)
+    grp = Hq // Hkv
+    for b in range(B):
+        Kb = k.float()[bt[b].long()].reshape(-1, Hkv, 128)[:S[b]]
+        Vb = v.float()[bt[b].long()].reshape(-1, Hkv, 128)[:S[b]]
+        Ke = Kb.permute(1, 0, 2).repeat_interleave(grp, dim=0)
+        Ve = Vb.permute(1, 0, 2).repeat_interleave(grp, dim=0)
+        o = F.scaled_dot_product_attention(q[b].float().unsqueeze(1), Ke, Ve, scale=SCALE)
+        assert (o.squeeze(1) - out[b]).abs().max().item() < 1e-5
+
+
+def test_state_split_merge_equals_full():
+    # Splitting one request's tokens into page ranges and merging the states
+    # reproduces the full softmax (the identity the GPU merge relies on).
+    q, k, v, bt, sl = cases.make_case([1000], 32, 8, 16, seed=21, poison=False)
+    full = oracle.attention_ref(q, k, v, bt, sl, SCALE)
+    parts = []
+    for t0, t1 in [(0, 320), (320, 656), (656, 1000)]:
+        p0, p1 = t0 // 16, (t1 + 15) // 16
+        bt_part = bt[:, p0:p1].contiguous()
+        parts.append(oracle.attention_state(q, k, v, bt_part,
+                                            torch.tensor([t1 - t0], dtype=torch.int32), SCALE))
+    for h in range(32):
+        M, L, A = oracle.merge_states([p[0][0, h] for p in parts], [p[1][0, h] for p in parts],
+                                      np.stack([p[2][0, h].numpy() for p in parts]))
+        np.testing.assert_allclose(A / L, full[0, h].numpy(), atol=1e-5, rtol=1e-5)
+
+
+def test_case_recipe_poisons_unused_storage():
+    q, k, v, bt, sl = cases.make_case([17, 65], 32, 8, 16, seed=0)
+    used = set(int(x) for x in bt.flatten() if x >= 0)
+    for p in range(k.shape[0]):
+        if p not in used:
+            assert torch.isnan(k[p].float()).all() and torch.isnan(v[p].float()).all()
+    last = int(bt[0, 1])
+    assert torch.isnan(k[last, 1:].float()).all() and not torch.isnan(k[last, 0].float()).any()
+
+
+def test_config_recipes():
+    sl1 = cases.config1_seq_lens()
+    assert len(sl1) == 4 and all(1 <= s <= 512 for s in sl1)
+    q, k, v, bt, sl = cases.config1()
+    assert k.shape[0] == sum((s + 15) // 16 for s in sl1) + 16
+    sl4 = cases.config4_seq_lens()
+    assert len(sl4) == 256 and min(sl4) >= 64 and max(sl4) <= 32768
+    assert cases.kv_bytes([8192] * 32, 8) == 1 << 30
+    assert cases.kv_bytes([262144], 8) == 1 << 30
+    assert cases.kv_bytes([32768] * 128, 8) == 16 << 30
