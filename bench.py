@@ -57,8 +57,8 @@ PROFILE_SUMMARY = os.path.join(REPO, "profiles", "gqa_decode_scan_kernel_rep.md"
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="rep",
                     choices=["rep", "wide", "ragged", "long", "long_peaked"])

@@ -44,8 +44,20 @@ thread_local cudaError_t t_last_error = cudaSuccess;
 constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
+// Workspace layout.  The first kCounterSlots ints hold the balanced
+// schedule's arrival counters for every shape: every launch leaves them at
+// zero and no partial state of any shape or schedule is ever stored there, so
+// one zeroing (gqa_decode_workspace_init) keeps them valid across launches of
+// different shapes.  A batch needing more counters than that gets a larger
+// counter region that the launcher clears before each launch.
+constexpr size_t kCounterSlots = 65536;
+
+size_t counter_region(size_t counters) {
+  return align_up(std::max(counters, kCounterSlots) * sizeof(int));
+}
+
 struct BalancedLayout {
-  size_t counters, m, l, acc, total;
+  size_t counters, ncounters, m, l, acc, total;
 };
 
 BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
@@ -54,16 +66,20 @@ BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
   const size_t slots = static_cast<size_t>(grid) + rows;
   BalancedLayout L;
   L.counters = 0;
-  L.m = align_up(rows * sp.ncw * sizeof(int));
+  L.ncounters = rows * sp.ncw;
+  L.m = counter_region(L.ncounters);
   L.l = L.m + align_up(slots * qhr * sizeof(float));
   L.acc = L.l + align_up(slots * qhr * sizeof(float));
   L.total = L.acc + align_up(slots * qhr * gqa::kHeadDim * sizeof(float));
   return L;
 }
 
+// Fixed splits through gqa_decode_launch: the reference's [B, Hq, ns](,128)
+// partial arrays, placed after the standard counter region.
 size_t fixed_ws_bytes(int B, int Hq, int ns) {
   const size_t states = static_cast<size_t>(B) * Hq * ns;
-  return align_up(states * gqa::kHeadDim * sizeof(float)) + 2 * align_up(states * sizeof(float));
+  return counter_region(0) + align_up(states * gqa::kHeadDim * sizeof(float)) +
+         2 * align_up(states * sizeof(float));
 }
 
 // Per-device facts, cached: SM count and resident CTAs for a (threads, smem).
@@ -212,6 +228,10 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
   const BalancedLayout lay = balanced_layout(B, sp, grid);
   if (!ws || ws_bytes < lay.total || !aligned16(ws)) return cudaErrorInvalidValue;
   unsigned char* w = static_cast<unsigned char*>(ws);
+  if (lay.ncounters > kCounterSlots) {
+    e = cudaMemsetAsync(w + lay.counters, 0, lay.ncounters * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
   gqa::ScanParams p =
       base_params(q, k, v, bt, sl, B, Hq, Hkv, bs, max_blocks, num_blocks, scale, sp);
   p.out = out;
@@ -344,7 +364,7 @@ cudaError_t gqa_decode_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
     const size_t need = fixed_ws_bytes(B, Hq, num_splits);
     if (!workspace || workspace_bytes < need || !aligned16(workspace)) return cudaErrorInvalidValue;
     const size_t states = static_cast<size_t>(B) * Hq * num_splits;
-    unsigned char* w = static_cast<unsigned char*>(workspace);
+    unsigned char* w = static_cast<unsigned char*>(workspace) + counter_region(0);
     acc = reinterpret_cast<float*>(w);
     m = reinterpret_cast<float*>(w + align_up(states * gqa::kHeadDim * sizeof(float)));
     l = reinterpret_cast<float*>(w + align_up(states * gqa::kHeadDim * sizeof(float)) +

@@ -82,7 +82,8 @@ def test_plan_rep_shape(lib):
     assert p.grid == 148
     # counters (32 rows x 8 warps) + m, l, acc for (148 + 32) slots x 32 heads
     slots, qhr = 148 + 32, 32
-    expect = 1024 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4
+    counters = 65536 * 4  # fixed counter region shared by every shape
+    expect = counters + 2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4
     assert p.workspace_bytes == expect
 
 
@@ -108,7 +109,8 @@ def test_plan_fixed_workspace_matches_reference_layout(lib):
     # [B, Hq, ns, 128] + [B, Hq, ns] x 2, fp32 (python/gqa_decode_ext.cpp:106-109)
     rc, p = plan(lib, 32, 32, 8, ns=8)
     states = 32 * 32 * 8
-    assert p.workspace_bytes == states * 128 * 4 + 2 * ((states * 4 + 255) // 256 * 256)
+    assert p.workspace_bytes == (65536 * 4 + states * 128 * 4 +
+                                 2 * ((states * 4 + 255) // 256 * 256))
     assert p.grid == min(148, 32 * 8)
     rc, p = plan(lib, 32, 32, 8, ns=1)
     assert p.workspace_bytes == 0 and p.grid == 32
@@ -126,3 +128,12 @@ def test_pick_splits(lib):
     # a batch that already fills the GPU several times: no split
     assert lib.gqa_decode_pick_splits(4096, 32, 8, 512, 148) == 1
     assert lib.gqa_decode_pick_splits(0, 32, 8, 512, 148) == 1
+
+
+def test_counter_region_grows_for_huge_batches(lib):
+    # 16384 requests x 8 warps = 131072 counters > the 65536 standard slots.
+    rc, p = plan(lib, 16384, 32, 8)
+    slots, qhr = 148 + 16384, 32
+    expect = (131072 * 4 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
+              slots * qhr * 128 * 4)
+    assert rc == 0 and p.workspace_bytes == expect

@@ -19,6 +19,7 @@ import pytest
 import torch
 
 import binding
+import capi
 import cases
 import oracle
 from golden.make_golden import golden_cases, q_transform
@@ -47,7 +48,7 @@ def assert_close(out, ref, what=""):
 
 
 def check_status():
-    assert binding.get_status(True) == 0, "device status word set (wait timeout / bad block id)"
+    assert capi.status() == 0, "device status word set (wait timeout / bad block id)"
 
 
 def run_and_check(kernel_fn, case_cpu, check_finite=False):
@@ -67,38 +68,36 @@ def run_and_check(kernel_fn, case_cpu, check_finite=False):
 @pytest.mark.parametrize("kernel", KERNEL_NAMES)
 @pytest.mark.parametrize("name", list(cases.REF_CASES.keys()))
 def test_gqa_decode(kernel, name):
-    run_and_check(binding.KERNELS[kernel], cases.ref_case(name, seed=0))
+    run_and_check(capi.KERNELS[kernel], cases.ref_case(name, seed=0))
 
 
 @pytest.mark.parametrize("num_splits", [1, 3, 8, 32, 512])
 def test_v2_num_splits(num_splits):
     case = cases.ref_case("a_base", seed=0)
-    run_and_check(lambda *a: binding.gqa_decode_v2(*a, num_splits=num_splits), case)
+    run_and_check(lambda *a: capi.v2(*a, num_splits=num_splits), case)
     if num_splits == 1:
         # One split runs exactly the unsplit scan's arithmetic.
         gpu = to_gpu(case)
-        out_v2 = binding.gqa_decode_v2(*gpu, SCALE, num_splits=1)
-        out_v1 = binding.gqa_decode_v1(*gpu, SCALE)
+        out_v2 = capi.v2(*gpu, SCALE, num_splits=1)
+        out_v1 = capi.v1(*gpu, SCALE)
         assert torch.equal(out_v2, out_v1), "v2(num_splits=1) != v1 bitwise"
 
 
 def test_v2_len1_splits8():
     # S=1 with 8 splits: 7 empty segments must contribute nothing.
-    run_and_check(lambda *a: binding.gqa_decode_v2(*a, num_splits=8),
-                  cases.ref_case("c_len1", seed=0))
+    run_and_check(lambda *a: capi.v2(*a, num_splits=8), cases.ref_case("c_len1", seed=0))
 
 
 @pytest.mark.parametrize("kernel", KERNEL_NAMES)
 def test_gqa_decode_large_logits(kernel):
     q, k, v, bt, sl = cases.ref_case("a_base", seed=0)
     q = (q.float() * 50.0).to(torch.bfloat16)
-    run_and_check(binding.KERNELS[kernel], (q, k, v, bt, sl), check_finite=True)
+    run_and_check(capi.KERNELS[kernel], (q, k, v, bt, sl), check_finite=True)
 
 
 @pytest.mark.parametrize("num_splits", [0, 1, 8, 64])
 def test_num_splits_through_extended_api(num_splits):
-    run_and_check(lambda *a: binding.gqa_decode(*a, num_splits=num_splits),
-                  cases.ref_case("i_8k", seed=0))
+    run_and_check(lambda *a: capi.auto(*a, num_splits=num_splits), cases.ref_case("i_8k", seed=0))
 
 
 # ---- against the reference's own outputs (tests/golden) ----------------------
@@ -114,7 +113,7 @@ def test_matches_reference_py_outputs(golden, kernel, name):
     builder, _ = golden_cases()[name]
     q, k, v, bt, sl = builder()
     q = q_transform(name, q)
-    out = binding.KERNELS[kernel](*to_gpu((q, k, v, bt, sl)), SCALE)
+    out = capi.KERNELS[kernel](*to_gpu((q, k, v, bt, sl)), SCALE)
     torch.cuda.synchronize()
     check_status()
     assert torch.isfinite(out.float()).all()
@@ -124,7 +123,7 @@ def test_matches_reference_py_outputs(golden, kernel, name):
 def test_empty_request_gives_zero():
     case = cases.make_case([50, 0, 17], 32, 8, 16, seed=17)
     for kernel in KERNEL_NAMES:
-        out = binding.KERNELS[kernel](*to_gpu(case), SCALE)
+        out = capi.KERNELS[kernel](*to_gpu(case), SCALE)
         torch.cuda.synchronize()
         assert torch.all(out[1].float() == 0), kernel
     check_status()
@@ -133,7 +132,7 @@ def test_empty_request_gives_zero():
 def test_all_requests_empty():
     case = cases.make_case([0, 0], 32, 8, 16, seed=18, pool_blocks=4)
     for kernel in KERNEL_NAMES:
-        out = binding.KERNELS[kernel](*to_gpu(case), SCALE)
+        out = capi.KERNELS[kernel](*to_gpu(case), SCALE)
         torch.cuda.synchronize()
         assert torch.all(out.float() == 0), kernel
     check_status()
@@ -145,14 +144,14 @@ def test_all_requests_empty():
 def test_head_and_block_shapes(Hq, Hkv, bs):
     case = cases.make_case([1, 15, 16, 17, 333, 1029], Hq, Hkv, bs, seed=19, value_scale=0.5)
     for kernel in KERNEL_NAMES:
-        run_and_check(binding.KERNELS[kernel], case)
+        run_and_check(capi.KERNELS[kernel], case)
 
 
 def test_determinism():
     gpu = to_gpu(cases.ref_case("i_8k", seed=1))
     for kernel in KERNEL_NAMES:
-        a = binding.KERNELS[kernel](*gpu, SCALE)
-        b = binding.KERNELS[kernel](*gpu, SCALE)
+        a = capi.KERNELS[kernel](*gpu, SCALE)
+        b = capi.KERNELS[kernel](*gpu, SCALE)
         assert torch.equal(a, b), kernel
 
 
@@ -165,20 +164,20 @@ def check_subset(out, case_gpu, requests):
 
 
 def test_config1():
-    run_and_check(binding.gqa_decode, cases.config1())
+    run_and_check(capi.auto, cases.config1())
 
 
 def test_config2_rep_full_size():
     case = cases.config2(device="cuda")
     outs = {}
     for ns in ["auto", 1, 8, 16, 32]:
-        outs[ns] = binding.gqa_decode_v2(*case, SCALE, num_splits=ns)
+        outs[ns] = capi.auto(*case, SCALE) if ns == "auto" else capi.v2(*case, SCALE, ns)
     torch.cuda.synchronize()
     check_status()
     for ns, out in outs.items():
         check_subset(out, case, [0, 17, 31])
         assert torch.isfinite(out.float()).all()
-    assert torch.equal(outs[1], binding.gqa_decode_v1(*case, SCALE))
+    assert torch.equal(outs[1], capi.v1(*case, SCALE))
     # Size-independent cross-check: every schedule agrees on every request.
     for ns in [8, 16, 32]:
         assert_close(outs[ns], outs["auto"], f"splits {ns} vs auto")
@@ -186,29 +185,29 @@ def test_config2_rep_full_size():
 
 def test_config3_wide_group():
     case = cases.config3(device="cuda", B=16)
-    out = binding.gqa_decode(*case, SCALE)
+    out = capi.auto(*case, SCALE)
     torch.cuda.synchronize()
     check_status()
     check_subset(out, case, [0, 15])
-    assert_close(binding.gqa_decode_v2(*case, SCALE, num_splits=16), out)
+    assert_close(capi.v2(*case, SCALE, num_splits=16), out)
 
 
 def test_config4_ragged():
     case = cases.config4(device="cuda")
-    out = binding.gqa_decode(*case, SCALE)
+    out = capi.auto(*case, SCALE)
     torch.cuda.synchronize()
     check_status()
     assert torch.isfinite(out.float()).all()
     sl = case[4].cpu()
     pick = {int(sl.argmin()), int(sl.argmax()), 0, 128, 255}
     check_subset(out, case, sorted(pick))
-    assert_close(binding.gqa_decode_v2(*case, SCALE, num_splits=8), out)
+    assert_close(capi.v2(*case, SCALE, num_splits=8), out)
 
 
 @pytest.mark.parametrize("k_scale", [1.0, 8.0])
 def test_config5_long_context(k_scale):
     case = cases.config5(device="cuda", k_scale=k_scale)
-    out = binding.gqa_decode(*case, SCALE)
+    out = capi.auto(*case, SCALE)
     torch.cuda.synchronize()
     check_status()
     assert torch.isfinite(out.float()).all()
@@ -219,7 +218,7 @@ def test_config5_long_context(k_scale):
 
 def test_partial_states_match_oracle():
     case_cpu = cases.make_case([700, 1, 2049], 32, 8, 16, seed=23)
-    m, l, acc = binding.gqa_decode_partial(*to_gpu(case_cpu), SCALE)
+    m, l, acc = capi.partial(*to_gpu(case_cpu), SCALE)
     torch.cuda.synchronize()
     om, ol, oacc = oracle.attention_state(*case_cpu, SCALE)
     # kernel m is in log2 units
@@ -243,13 +242,13 @@ def test_kv_range_sharding_emulated(nshards, k_scale):
         t0, t1 = sharding.kv_range(S, bs, r, nshards)
         bt_r = bt[:, t0 // bs:(t1 + bs - 1) // bs].contiguous()
         sl_r = torch.tensor([t1 - t0], dtype=torch.int32, device="cuda")
-        states.append(binding.gqa_decode_partial(q, k, v, bt_r, sl_r, SCALE))
+        states.append(capi.partial(q, k, v, bt_r, sl_r, SCALE))
     packed = torch.stack([sharding.pack_states(*s) for s in states])
     mm, ll, aa = sharding.unpack_states(packed, 32)
-    out = binding.merge_states(mm, ll, aa).view(1, 32, 128)
+    out = capi.merge(mm, ll, aa).view(1, 32, 128)
     torch.cuda.synchronize()
     check_status()
-    full = binding.gqa_decode(*case, SCALE)
+    full = capi.auto(*case, SCALE)
     assert_close(out, full, "sharded vs single")
     check_subset(out, case, [0])
 
@@ -258,7 +257,7 @@ def test_merge_states_all_empty_shards():
     m = torch.full((3, 5), -float("inf"), device="cuda")
     l = torch.zeros(3, 5, device="cuda")
     acc = torch.zeros(3, 5, 128, device="cuda")
-    out = binding.merge_states(m, l, acc)
+    out = capi.merge(m, l, acc)
     torch.cuda.synchronize()
     assert torch.all(out.float() == 0)
 
@@ -271,10 +270,10 @@ def test_bad_block_id_sets_status_without_fault():
     q, k, v, bt, sl = cases.make_case([40, 40], 32, 8, 16, seed=25)
     bt = bt.clone()
     bt[1, 1] = k.shape[0] + 7
-    binding.get_status(True)
-    out = binding.gqa_decode(*to_gpu((q, k, v, bt, sl)), SCALE, check_blocks=True)
+    capi.status()
+    out = capi.auto(*to_gpu((q, k, v, bt, sl)), SCALE, check_blocks=True)
     torch.cuda.synchronize()
-    assert binding.get_status(True) & 2
+    assert capi.status() & 2
     ref = oracle.attention_ref(q[:1], k, v, bt[:1], sl[:1], SCALE)
     assert_close(out[:1], ref)
 
@@ -350,6 +349,32 @@ def test_reference_kernels_built_for_sm100_agree():
                                bt.shape[1], SCALE, torch.cuda.current_stream().cuda_stream)
     assert rc == 0
     torch.cuda.synchronize()
-    ours = binding.gqa_decode(q, k, v, bt, sl, SCALE)
+    ours = capi.auto(q, k, v, bt, sl, SCALE)
     assert_close(out_ref, oracle.attention_ref(*case_cpu, SCALE), "reference v1 (sm_100a)")
     assert_close(ours, out_ref, "ours vs reference v1 (sm_100a)")
+
+
+# ---- the PyTorch binding (reference python/binding.py surface) ------------------
+
+@pytest.mark.parametrize("name", ["a_base", "f_bs64", "g_hq64"])
+def test_binding_matches_c_abi(name):
+    gpu = to_gpu(cases.ref_case(name, seed=5))
+    for kernel in ["v0", "v1", "v2"]:
+        assert torch.equal(binding.KERNELS[kernel](*gpu, SCALE), capi.KERNELS[kernel](*gpu, SCALE))
+    assert torch.equal(binding.gqa_decode_v2(*gpu, SCALE, num_splits=32),
+                       capi.v2(*gpu, SCALE, num_splits=32))
+    assert torch.equal(binding.gqa_decode_v2(*gpu, SCALE, num_splits="auto"),
+                       capi.auto(*gpu, SCALE))
+    check_status()
+
+
+def test_binding_validation_messages():
+    q, k, v, bt, sl = to_gpu(cases.ref_case("c_len1", seed=0))
+    with pytest.raises(RuntimeError, match="q must be bf16"):
+        binding.gqa_decode_v1(q.float(), k, v, bt, sl, SCALE)
+    with pytest.raises(RuntimeError, match="block_table must be int32"):
+        binding.gqa_decode_v1(q, k, v, bt.long(), sl, SCALE)
+    with pytest.raises(RuntimeError, match="Hq must be divisible by Hkv"):
+        binding.gqa_decode_v1(q[:, :30].contiguous(), k, v, bt, sl, SCALE)
+    with pytest.raises(RuntimeError, match="k_cache and v_cache must have the same shape"):
+        binding.gqa_decode_v1(q, k, v[:-1].contiguous(), bt, sl, SCALE)
