@@ -102,9 +102,9 @@ class KVRangeDecoder:
             out = self._merge(m.view(1, rows), l.view(1, rows), acc.view(1, rows, 128))
             return out.view(B, Hq, 128)
         buf = pack_states(m, l, acc)
-        if self._gathered is None or self._gathered.shape != (self.world, buf.numel()):
-            self._gathered = torch.empty(self.world, buf.numel(), dtype=torch.float32,
-                                         device=buf.device)
+        n = buf.numel()
+        if self._gathered is None or self._gathered.numel() != self.world * n:
+            self._gathered = torch.empty(self.world * n, dtype=torch.float32, device=buf.device)
         dist.all_gather_into_tensor(self._gathered, buf, group=self.group)
-        mm, ll, aa = unpack_states(self._gathered, rows)
+        mm, ll, aa = unpack_states(self._gathered.view(self.world, n), rows)
         return self._merge(mm, ll, aa).view(B, Hq, 128)
