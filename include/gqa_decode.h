@@ -146,6 +146,37 @@ cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
                                     const float* state_acc, int nshards, int rows, gqa_bf16* out,
                                     cudaStream_t stream);
 
+/* Size of the device scratch array behind gqa_decode_launch_noalloc. */
+#define GQA_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* gqa_decode_launch (num_splits == 0, balanced schedule) for callers that
+ * cannot allocate device memory - e.g. an engine that gives all of HBM to
+ * its own KV-cache pool and forbids later allocations, or a plain C / cgo /
+ * JNI binding with no device allocator to hand over a workspace.  No
+ * counterpart in the reference (its extension allocates a workspace on every
+ * call, python/gqa_decode_ext.cpp:106-109).
+ * - The scratch (arrival counters and split states) is a file-scope
+ *   GQA_DECODE_NOALLOC_SCRATCH_BYTES (16 MiB) device array that every GPU
+ *   loading this library holds until the process exits.  This call allocates
+ *   nothing: no cudaMalloc, no cudaFree.
+ * - Shapes whose scratch need exceeds it are rejected with
+ *   cudaErrorInvalidValue before anything is launched.  The need is about
+ *   (grid / rows_per_request + B) * Hq * 520 bytes (grid = one CTA per SM,
+ *   rows_per_request = Hkv / heads_per_row of gqa_decode_plan): on a 148-SM
+ *   B200 with Hkv = 8, up to ~860 requests at Hq = 32 or ~350 at Hq = 64.
+ * - The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture.
+ * - All calls on a device share the array and it keeps the previous call's
+ *   contents; each call clears the counters it needs on `stream` before its
+ *   kernel.  Calls that overlap on the GPU (other streams, other threads)
+ *   race on the array and must be serialised by the caller. */
+cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                      const gqa_bf16* v_cache, const int* block_table,
+                                      const int* seq_lens, gqa_bf16* out, int B, int Hq,
+                                      int Hkv, int block_size, int max_blocks, int num_blocks,
+                                      float scale, cudaStream_t stream);
+
 /* Fixed split count for the v2 schedule at a nominal seq_len: the count
  * (1..512) that minimises the estimated makespan over num_sms SMs.  The
  * reference picks it by offline sweep (bench/run_matrix.py:84-88). */

@@ -1,0 +1,157 @@
+// Decode entry point for callers that cannot allocate device memory.
+//
+// gqa_decode_launch needs a caller-provided workspace for the balanced
+// schedule's arrival counters and split partial states.  Some callers have
+// no way to provide one: a host engine that hands all of HBM to its own
+// KV-cache pool at start-up and treats any later device allocation as a bug
+// (cudaMalloc would synchronise the device mid-step and can fail once the
+// pool holds the memory), or a thin foreign-function binding (C, cgo, JNI)
+// that has no device allocator to draw a workspace from.  For them,
+// gqa_decode_launch_noalloc keeps that scratch in the file-scope array
+// below, which the CUDA module reserves on every GPU that loads this library
+// and keeps until the process exits.  The entry point itself calls no
+// cudaMalloc, cudaFree or other allocating routine.
+#include <algorithm>
+#include <cstdint>
+#include <mutex>
+
+#include "gqa_decode.h"
+#include "gqa_internal.h"
+
+namespace {
+
+constexpr size_t kScratchBytes = GQA_DECODE_NOALLOC_SCRATCH_BYTES;
+constexpr size_t kAlign = 256;
+
+// Scratch shared by every gqa_decode_launch_noalloc call on a device:
+// [arrival counters | m | l | acc], laid out per call for its shape.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+struct DeviceState {
+  std::once_flag once;
+  cudaError_t setup_error = cudaSuccess;
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  int sms = 0;
+  int smem_attr = 0;
+  int occ_threads = 0, occ_smem = 0, occ = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceState g_state[kMaxDevices];
+std::mutex g_mu;
+
+// One-time set-up for the current device: the scratch array's device address
+// (in host code its name is only a stand-in, so it must be looked up) and the
+// SM count.
+void setup_device(DeviceState* st, int dev) {
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess) {
+    st->setup_error = e;
+    return;
+  }
+  e = cudaDeviceGetAttribute(&st->sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    st->setup_error = e;
+    return;
+  }
+  st->scratch = static_cast<unsigned char*>(ptr);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                                 const gqa_bf16* v_cache, const int* block_table,
+                                                 const int* seq_lens, gqa_bf16* out, int B,
+                                                 int Hq, int Hkv, int block_size, int max_blocks,
+                                                 int num_blocks, float scale,
+                                                 cudaStream_t stream) {
+  gqa::ShapePlan sp;
+  if (B < 0 || block_size <= 0 || max_blocks <= 0 || num_blocks < 0 ||
+      gqa::make_shape_plan(Hq, Hkv, &sp) != 0)
+    return cudaErrorInvalidValue;
+  if (B == 0) return cudaSuccess;
+  if (!q || !k_cache || !v_cache || !block_table || !seq_lens || !out)
+    return cudaErrorInvalidValue;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return cudaErrorMisalignedAddress;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  DeviceState* st = &g_state[dev];
+  std::call_once(st->once, setup_device, st, dev);
+  if (st->setup_error != cudaSuccess) return st->setup_error;
+
+  int grid = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (st->smem_attr < sp.smem_bytes) {
+      e = gqa::scan_kernel_set_smem(sp.smem_bytes);
+      if (e != cudaSuccess) return e;
+      st->smem_attr = sp.smem_bytes;
+    }
+    if (st->occ_threads != sp.threads || st->occ_smem != sp.smem_bytes) {
+      int o = 0;
+      e = gqa::scan_kernel_occupancy(sp.threads, sp.smem_bytes, &o);
+      if (e != cudaSuccess) return e;
+      if (o < 1) return cudaErrorInvalidConfiguration;
+      st->occ_threads = sp.threads;
+      st->occ_smem = sp.smem_bytes;
+      st->occ = o;
+    }
+    grid = st->sms * st->occ;
+  }
+
+  // Balanced-schedule layout inside the static scratch.
+  const size_t rows = static_cast<size_t>(B) * sp.NHG;
+  const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
+  const size_t slots = static_cast<size_t>(grid) + rows;
+  const size_t counters_bytes = rows * sp.ncw * sizeof(int);
+  const size_t off_m = align_up(counters_bytes);
+  const size_t off_l = off_m + align_up(slots * qhr * sizeof(float));
+  const size_t off_acc = off_l + align_up(slots * qhr * sizeof(float));
+  const size_t need = off_acc + align_up(slots * qhr * gqa::kHeadDim * sizeof(float));
+  if (need > kScratchBytes) return cudaErrorInvalidValue;  // shape too large for the scratch
+
+  // The arrival counters must start at zero; the scratch keeps whatever the
+  // previous call left, so clear them on the same stream first.
+  e = cudaMemsetAsync(st->scratch, 0, counters_bytes, stream);
+  if (e != cudaSuccess) return e;
+
+  gqa::ScanParams p{};
+  p.q = q;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.block_table = block_table;
+  p.seq_lens = seq_lens;
+  p.out = out;
+  p.counters = reinterpret_cast<int*>(st->scratch);
+  p.part_m = reinterpret_cast<float*>(st->scratch + off_m);
+  p.part_l = reinterpret_cast<float*>(st->scratch + off_l);
+  p.part_acc = reinterpret_cast<float*>(st->scratch + off_acc);
+  p.B = B;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.bs = block_size;
+  p.max_blocks = max_blocks;
+  p.num_blocks = num_blocks;
+  p.G = sp.G;
+  p.NT = sp.NT;
+  p.HG = sp.HG;
+  p.NHG = sp.NHG;
+  p.ncw = sp.ncw;
+  p.row_bytes = sp.row_bytes;
+  p.row_stride = sp.row_stride;
+  p.stage_bytes = sp.stage_bytes;
+  p.nstages = sp.nstages;
+  p.schedule = gqa::kBalanced;
+  p.num_splits = 0;
+  p.out_partial = 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+}

@@ -25,7 +25,7 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build")
 EXT_NAME = "gqa_decode_ext"
 EXT_PATH = os.path.join(BUILD_DIR, EXT_NAME + ".so")
 
-CU_SOURCES = ["gqa_scan.cu", "gqa_simt.cu", "gqa_api.cu"]
+CU_SOURCES = ["gqa_scan.cu", "gqa_simt.cu", "gqa_api.cu", "gqa_noalloc.cu"]
 CU_HEADERS = ["gqa_internal.h", "gqa_ptx.cuh"]
 
 NVCC_FLAGS = [
