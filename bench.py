@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--ref-seconds", type=float, default=90.0,
                     help="total budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="requests per GPU for rep / wide (smaller cases for profiling)")
     return ap.parse_args()
 
 
@@ -179,20 +181,23 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- workloads
 
-def build_workload(name, rank, world, device):
+def build_workload(name, rank, world, device, batch=None):
     """Returns (case on device, description dict, kv bytes of this rank,
     decode function factory kind)."""
     import cases
 
     if name == "rep":
-        case = cases.config2(device=device, seed=2 + rank)
-        cfg = {"workload": "config2_rep", "B_per_gpu": 32, "seq_len": 8192, "Hq": 32, "Hkv": 8,
-               "block_size": 16, "num_blocks_per_gpu": 16384, "global_batch": 32 * world}
+        B = batch or 32
+        case = cases.config2(device=device, seed=2 + rank, B=B)
+        cfg = {"workload": "config2_rep" if B == 32 else f"config2_rep_B{B}", "B_per_gpu": B,
+               "seq_len": 8192, "Hq": 32, "Hkv": 8, "block_size": 16,
+               "num_blocks_per_gpu": B * 512, "global_batch": B * world}
         kind = "batch"
     elif name == "wide":
-        case = cases.config3(device=device, seed=3 + rank, B=16)
-        cfg = {"workload": "config3_wide", "B_per_gpu": 16, "seq_len": 32768, "Hq": 64,
-               "Hkv": 8, "block_size": 64, "global_batch": 16 * world}
+        B = batch or 16
+        case = cases.config3(device=device, seed=3 + rank, B=B)
+        cfg = {"workload": "config3_wide", "B_per_gpu": B, "seq_len": 32768, "Hq": 64,
+               "Hkv": 8, "block_size": 64, "global_batch": B * world}
         kind = "batch"
     elif name == "ragged":
         import sharding
@@ -243,9 +248,10 @@ def sum_over_ranks(x, world, device):
     return float(t.item())
 
 
-def time_loop(step, K, world, stream):
+def time_loop(step, K, world, stream, finish=None):
     """Mean ms per step over exactly K steps, CUDA events on `stream`,
-    barrier + synchronize on both sides."""
+    barrier + synchronize on both sides.  `finish` joins any side streams
+    into `stream` before the end event."""
     barrier(world)
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
@@ -253,10 +259,66 @@ def time_loop(step, K, world, stream):
     start.record(stream)
     for _ in range(K):
         step()
+    if finish is not None:
+        finish()
     end.record(stream)
     torch.cuda.synchronize()
     barrier(world)
     return start.elapsed_time(end) / K
+
+
+class E2ELoop:
+    """Double-buffered host<->device traffic around the decode: H2D of the
+    next step's inputs on one copy stream, D2H of each output on another, the
+    decode on the compute stream, ordered by events."""
+
+    def __init__(self, q, bt, sl, out, stream):
+        self.compute = stream
+        self.h2d_stream = torch.cuda.Stream(device=q.device)
+        self.d2h_stream = torch.cuda.Stream(device=q.device)
+        self.host_in = [(q.cpu().pin_memory(), bt.cpu().pin_memory(), sl.cpu().pin_memory())
+                        for _ in range(2)]
+        self.dev_in = [(torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl))
+                       for _ in range(2)]
+        self.dev_out = [torch.empty_like(out) for _ in range(2)]
+        self.host_out = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+                         for _ in range(2)]
+        self.uploaded = [torch.cuda.Event() for _ in range(2)]
+        self.decoded = [torch.cuda.Event() for _ in range(2)]
+        self.downloaded = [torch.cuda.Event() for _ in range(2)]
+        self.i = 0
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host_in[0])
+        self.d2h_bytes = out.numel() * out.element_size()
+        self._upload(0)
+
+    def _upload(self, j):
+        with torch.cuda.stream(self.h2d_stream):
+            # buffer j was last read by the decode two steps ago
+            self.h2d_stream.wait_event(self.decoded[j])
+            for d, h in zip(self.dev_in[j], self.host_in[j]):
+                d.copy_(h, non_blocking=True)
+            self.uploaded[j].record(self.h2d_stream)
+
+    def step(self, decode):
+        j = self.i % 2
+        self._upload(1 - j)  # next step's inputs, overlapping this decode
+        self.compute.wait_event(self.uploaded[j])
+        self.compute.wait_event(self.downloaded[j])  # out buffer j is free again
+        decode(*self.dev_in[j], self.dev_out[j])
+        self.decoded[j].record(self.compute)
+        with torch.cuda.stream(self.d2h_stream):
+            self.d2h_stream.wait_event(self.decoded[j])
+            self.host_out[j].copy_(self.dev_out[j], non_blocking=True)
+            self.downloaded[j].record(self.d2h_stream)
+        self.i += 1
+
+    def drain(self):
+        self.compute.wait_stream(self.d2h_stream)
+        self.compute.wait_stream(self.h2d_stream)
+
+    def last_output(self):
+        torch.cuda.synchronize()
+        return self.host_out[(self.i - 1) % 2].to(self.dev_out[0].device)
 
 
 def per_step_median_us(step, n, stream):
@@ -366,7 +428,7 @@ def run_ours(args, world, rank, local):
         import sharding
 
         sharding.init_process_group("nccl", timeout_s=120)
-    case, cfg, kv_local, kind = build_workload(args.workload, rank, world, device)
+    case, cfg, kv_local, kind = build_workload(args.workload, rank, world, device, args.batch)
     q, k, v, bt, sl = case
     ns = 0 if args.num_splits == "auto" else int(args.num_splits)
 
@@ -429,31 +491,26 @@ def run_ours(args, world, rank, local):
     median_us = per_step_median_us(step, min(args.steps, 200), stream)
     median_us = max_over_ranks(median_us, world, device)
 
-    # e2e through the public API with host buffers: per step, q, block_table
-    # and seq_lens go H2D from pinned memory and out comes back D2H.
-    q_h = q.cpu().pin_memory()
-    bt_h = bt.cpu().pin_memory()
-    sl_h = sl.cpu().pin_memory()
-    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    q_d, bt_d, sl_d = torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl)
-    h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + sl_h.numel() * 4
-    d2h = out_h.numel() * out_h.element_size()
+    # e2e through the public API with host buffers: every step copies its q,
+    # block_table and seq_lens H2D from pinned memory and its out back D2H.
+    # As in a serving loop, step i+1's inputs are uploaded (copy stream) while
+    # step i decodes, and step i's output is downloaded (second copy stream)
+    # while step i+1 decodes; buffers are double-buffered.
+    e2e = E2ELoop(q, bt, sl, out, stream)
     if kind == "batch":
-        def e2e_step():
-            q_d.copy_(q_h, non_blocking=True)
-            bt_d.copy_(bt_h, non_blocking=True)
-            sl_d.copy_(sl_h, non_blocking=True)
-            binding.gqa_decode(q_d, k, v, bt_d, sl_d, SCALE, num_splits=ns, out=out)
-            out_h.copy_(out, non_blocking=True)
+        def decode(q_d, bt_d, sl_d, out_d):
+            binding.gqa_decode(q_d, k, v, bt_d, sl_d, SCALE, num_splits=ns, out=out_d)
     else:
-        def e2e_step():
-            q_d.copy_(q_h, non_blocking=True)
-            bt_d.copy_(bt_h, non_blocking=True)
-            sl_d.copy_(sl_h, non_blocking=True)
-            out_h.copy_(dec.decode(q_d, k, v, bt_d, sl_d, SCALE), non_blocking=True)
+        def decode(q_d, bt_d, sl_d, out_d):
+            out_d.copy_(dec.decode(q_d, k, v, bt_d, sl_d, SCALE))
     for _ in range(max(3, args.warmup // 4)):
-        e2e_step()
-    ms_e2e = max_over_ranks(time_loop(e2e_step, args.steps, world, stream), world, device)
+        e2e.step(decode)
+    e2e.drain()
+    h2d, d2h = e2e.h2d_bytes, e2e.d2h_bytes
+    ms_e2e = max_over_ranks(time_loop(lambda: e2e.step(decode), args.steps, world, stream,
+                                      finish=e2e.drain), world, device)
+    if not torch.equal(e2e.last_output(), out):
+        raise SystemExit("e2e output differs from the device-resident output")
     status = binding.get_status(True)
     if status:
         raise SystemExit(f"device status {status} after timing")
@@ -481,8 +538,9 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": round(kv_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": int(h2d * world),
                 "d2h_bytes_per_step": int(d2h * world),
-                "path": "binding.gqa_decode -> C ABI gqa_decode_launch, host pinned q/bt/sl in, "
-                        "out back"},
+                "path": "binding.gqa_decode -> C ABI gqa_decode_launch; every step q/bt/sl "
+                        "H2D from pinned host memory and out D2H, double-buffered on two copy "
+                        "streams overlapping the previous / next decode"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": profiled_traffic(kv_local), "peak_source": peak_src,

@@ -66,7 +66,7 @@ BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
   const size_t slots = static_cast<size_t>(grid) + rows;
   BalancedLayout L;
   L.counters = 0;
-  L.ncounters = rows * sp.ncw;
+  L.ncounters = (static_cast<size_t>(grid) + 2 * rows) * sp.ncw;
   L.m = counter_region(L.ncounters);
   L.l = L.m + align_up(slots * qhr * sizeof(float));
   L.acc = L.l + align_up(slots * qhr * sizeof(float));

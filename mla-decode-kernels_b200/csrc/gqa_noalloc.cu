@@ -111,7 +111,7 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   const size_t rows = static_cast<size_t>(B) * sp.NHG;
   const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
   const size_t slots = static_cast<size_t>(grid) + rows;
-  const size_t counters_bytes = rows * sp.ncw * sizeof(int);
+  const size_t counters_bytes = (static_cast<size_t>(grid) + 2 * rows) * sp.ncw * sizeof(int);
   const size_t off_m = align_up(counters_bytes);
   const size_t off_l = off_m + align_up(slots * qhr * sizeof(float));
   const size_t off_acc = off_l + align_up(slots * qhr * sizeof(float));

@@ -213,47 +213,153 @@ __device__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int 
   }
 }
 
-// Last-arriving warp of a cut row: merge the row's partial slots for the q
-// heads of this warp in slot order (deterministic) and write the result.
-__device__ void merge_row_unit(const ScanParams& p, const Seg& s, int hl, int j0, int cnt,
-                               int lane) {
+// Partial states merged in one step.  Rows cut into more parts than this are
+// merged in two levels: the last warp of every group of kMergeGroup
+// consecutive CTAs merges the group into the group's first slot, and the
+// last of those merges the groups.
+constexpr int kMergeGroup = 16;
+constexpr int kMergeHeads = 4;  // q heads merged together (register budget)
+constexpr int kMergeBatch = 2;  // parts per batch of acc loads
+
+// Merge n unnormalised states of this warp's q heads [jj0, jj0 + cnt),
+// stored in slots first, first + stride, ...  With `final_` the result goes
+// to the output (normalised bf16, or unnormalised to res_* with
+// out_partial) of q heads bh0 + i; otherwise it overwrites slot `first`.
+// Loads are batched so that the whole merge costs a few L2 round trips:
+// lanes hold one part each for (m, l), and every lane accumulates 4 output
+// dims of all kMergeHeads heads over kMergeBatch parts per batch.
+__device__ __forceinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n, int jj0,
+                            int cnt, int lane, bool final_, size_t bh0) {
   const int QHR = p.HG * p.G;
-  const long long slot0 = s.cfirst + s.row;
-  const int hk = s.hg * p.HG + hl;
-  for (int n = 0; n < cnt; ++n) {
-    const int jj = hl * p.G + j0 + n;
-    float M = -INFINITY;
-    for (int k = 0; k < s.nparts; ++k)
-      M = fmaxf(M, __ldcg(p.part_m + (slot0 + k) * QHR + jj));
-    float L = 0.f;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < s.nparts; ++k) {
-      const size_t st = static_cast<size_t>(slot0 + k) * QHR + jj;
-      const float f = exp2f(__ldcg(p.part_m + st) - M);
-      L += __ldcg(p.part_l + st) * f;
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(p.part_acc + st * kHeadDim) + lane);
-      a.x += x.x * f;
-      a.y += x.y * f;
-      a.z += x.z * f;
-      a.w += x.w * f;
+  for (int i0 = 0; i0 < cnt; i0 += kMergeHeads) {
+    float M[kMergeHeads], L[kMergeHeads], m0[kMergeHeads], l0[kMergeHeads];
+    #pragma unroll
+    for (int i = 0; i < kMergeHeads; ++i) {
+      M[i] = -INFINITY;
+      L[i] = 0.f;
+      m0[i] = -INFINITY;
+      l0[i] = 0.f;
     }
-    const size_t bh = static_cast<size_t>(s.b) * p.Hq + hk * p.G + j0 + n;
-    if (p.out_partial) {
-      if (lane == 0) {
-        p.res_m[bh] = M;
-        p.res_l[bh] = L;
+    // pass 1: M per head over all parts (the first 32 parts stay in registers)
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      #pragma unroll
+      for (int i = 0; i < kMergeHeads; ++i) {
+        float mk = -INFINITY, lk = 0.f;
+        if (i0 + i < cnt && c0 + lane < n) {
+          const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + lane) * stride) *
+                                QHR + jj0 + i0 + i;
+          mk = __ldcg(p.part_m + st);
+          lk = __ldcg(p.part_l + st);
+        }
+        if (c0 == 0) {
+          m0[i] = mk;
+          l0[i] = lk;
+        }
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, off));
+        M[i] = fmaxf(M[i], mk);
       }
-      *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) = a;
-    } else {
-      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a.x / L, a.y / L, a.z / L, a.w / L);
+    }
+    // pass 2: weights, L and acc
+    float4 a[kMergeHeads];
+    #pragma unroll
+    for (int i = 0; i < kMergeHeads; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      float w[kMergeHeads];
+      #pragma unroll
+      for (int i = 0; i < kMergeHeads; ++i) {
+        float mk = m0[i], lk = l0[i];
+        if (c0 > 0) {
+          mk = -INFINITY;
+          lk = 0.f;
+          if (i0 + i < cnt && c0 + lane < n) {
+            const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + lane) *
+                                                              stride) * QHR + jj0 + i0 + i;
+            mk = __ldcg(p.part_m + st);
+            lk = __ldcg(p.part_l + st);
+          }
+        }
+        w[i] = (c0 + lane < n && i0 + i < cnt) ? exp2f(mk - M[i]) : 0.f;
+        float lw = lk * w[i];
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(kFull, lw, off);
+        L[i] += lw;
+      }
+      const int nc = min(32, n - c0);
+      for (int k0 = 0; k0 < nc; k0 += kMergeBatch) {
+        float4 x[kMergeHeads][kMergeBatch];
+        #pragma unroll
+        for (int i = 0; i < kMergeHeads; ++i) {
+          #pragma unroll
+          for (int kk = 0; kk < kMergeBatch; ++kk) {
+            x[i][kk] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i0 + i < cnt && k0 + kk < nc) {
+              const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + k0 + kk) *
+                                                                stride) * QHR + jj0 + i0 + i;
+              x[i][kk] = __ldcg(reinterpret_cast<const float4*>(p.part_acc + st * kHeadDim) + lane);
+            }
+          }
+        }
+        #pragma unroll
+        for (int i = 0; i < kMergeHeads; ++i) {
+          #pragma unroll
+          for (int kk = 0; kk < kMergeBatch; ++kk) {
+            const float f = __shfl_sync(kFull, w[i], (k0 + kk) & 31);
+            a[i].x += x[i][kk].x * f;
+            a[i].y += x[i][kk].y * f;
+            a[i].z += x[i][kk].z * f;
+            a[i].w += x[i][kk].w * f;
+          }
+        }
+      }
+    }
+    #pragma unroll
+    for (int i = 0; i < kMergeHeads; ++i) {
+      if (i0 + i >= cnt) continue;
+      if (final_) {
+        const size_t bh = bh0 + i0 + i;
+        if (p.out_partial) {
+          if (lane == 0) {
+            p.res_m[bh] = M[i];
+            p.res_l[bh] = L[i];
+          }
+          *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) = a[i];
+        } else {
+          store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a[i].x / L[i], a[i].y / L[i],
+                       a[i].z / L[i], a[i].w / L[i]);
+        }
+      } else {
+        const size_t st = static_cast<size_t>(first) * QHR + jj0 + i0 + i;
+        if (lane == 0) {
+          p.part_m[st] = M[i];
+          p.part_l[st] = L[i];
+        }
+        *reinterpret_cast<float4*>(p.part_acc + st * kHeadDim + 4 * lane) = a[i];
+      }
     }
   }
 }
 
+// Count one arrival on *ctr; true (on every lane) for the warp whose arrival
+// completes `total`.  That warp also re-arms the counter for the next launch
+// after it has used the data (see callers).
+__device__ __forceinline__ bool arrive_last(int* ctr, int total, int lane) {
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(ctr, 1) == total - 1;
+  last = __shfl_sync(kFull, last, 0);
+  if (last) __threadfence();
+  return last != 0;
+}
+
 }  // namespace
 
-__global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
-    gqa_decode_scan_kernel(const ScanParams p) {
+// kMaxWarps bounds the CTA (consumer warps + the copy warp) so the register
+// budget fits it: 9 warps for groups of up to 8 heads per kv head (the common
+// shapes, no spills), 17 for the widest groups.
+template <int kMaxWarps>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(const ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ long long sh_warp[32];
   __shared__ long long sh_info[8];
@@ -543,17 +649,38 @@ __global__ void __launch_bounds__((kMaxConsumerWarps + 1) * 32, 1)
       }
     }
     if (s.kind == kPartial && p.schedule == kBalanced) {
-      // Count this warp's partial; the warp that completes the row merges it.
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      int* ctr = p.counters + static_cast<size_t>(s.row) * p.ncw + warp;
-      if (lane == 0) last = atomicAdd(ctr, 1) == s.nparts - 1;
-      last = __shfl_sync(kFull, last, 0);
-      if (last) {
-        __threadfence();
-        merge_row_unit(p, s, hl, j0, cnt, lane);
-        if (lane == 0) *ctr = 0;  // leave the counter ready for the next launch
+      // Count this warp's partial; the warp that completes a group / the row
+      // merges it.  Counters: [group counters by first slot | row counters],
+      // (grid + rows) and rows entries of ncw each.
+      const long long rows = static_cast<long long>(p.B) * p.NHG;
+      const long long grid = gridDim.x;
+      int* row_ctr = p.counters + static_cast<size_t>(grid + rows + s.row) * p.ncw + warp;
+      const int jj0 = hl * p.G + j0;
+      const size_t bh0 = static_cast<size_t>(s.b) * p.Hq + hbase;
+      if (s.nparts <= kMergeGroup) {
+        if (arrive_last(row_ctr, s.nparts, lane)) {
+          merge_parts(p, s.cfirst + s.row, 1, s.nparts, jj0, cnt, lane, true, bh0);
+          if (lane == 0) *row_ctr = 0;
+        }
+      } else {
+        const long long gi = (static_cast<long long>(blockIdx.x) - s.cfirst) / kMergeGroup;
+        const long long g0 = s.cfirst + gi * kMergeGroup;
+        const long long clast = s.cfirst + s.nparts - 1;
+        const int gsz = static_cast<int>(min(static_cast<long long>(kMergeGroup), clast - g0 + 1));
+        const int ngroups = (s.nparts + kMergeGroup - 1) / kMergeGroup;
+        bool group_done = true;
+        if (gsz > 1) {
+          int* grp_ctr = p.counters + static_cast<size_t>(g0 + s.row) * p.ncw + warp;
+          group_done = arrive_last(grp_ctr, gsz, lane);
+          if (group_done) {
+            merge_parts(p, g0 + s.row, 1, gsz, jj0, cnt, lane, false, 0);
+            if (lane == 0) *grp_ctr = 0;
+          }
+        }
+        if (group_done && arrive_last(row_ctr, ngroups, lane)) {
+          merge_parts(p, s.cfirst + s.row, kMergeGroup, ngroups, jj0, cnt, lane, true, bh0);
+          if (lane == 0) *row_ctr = 0;
+        }
       }
     }
   }
@@ -622,8 +749,14 @@ __global__ void __launch_bounds__(128) gqa_decode_shard_merge_kernel(const Shard
   store_bf16x4(o, a.x / Lsum, a.y / Lsum, a.z / Lsum, a.w / Lsum);
 }
 
+constexpr int kSmallWarps = 9;
+constexpr int kLargeWarps = kMaxConsumerWarps + 1;
+
 cudaError_t launch_scan(const ScanParams& p, int grid, int threads, int smem, cudaStream_t s) {
-  gqa_decode_scan_kernel<<<grid, threads, smem, s>>>(p);
+  if (threads <= kSmallWarps * 32)
+    gqa_decode_scan_kernel<kSmallWarps><<<grid, threads, smem, s>>>(p);
+  else
+    gqa_decode_scan_kernel<kLargeWarps><<<grid, threads, smem, s>>>(p);
   return cudaGetLastError();
 }
 
@@ -641,13 +774,19 @@ cudaError_t launch_shard_merge(const ShardMergeParams& p, cudaStream_t s) {
 }
 
 cudaError_t scan_kernel_set_smem(int smem_bytes) {
-  return cudaFuncSetAttribute(gqa_decode_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              smem_bytes);
+  cudaError_t e = cudaFuncSetAttribute(gqa_decode_scan_kernel<kSmallWarps>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gqa_decode_scan_kernel<kLargeWarps>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
 }
 
 cudaError_t scan_kernel_occupancy(int threads, int smem_bytes, int* blocks_per_sm) {
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, gqa_decode_scan_kernel,
-                                                       threads, smem_bytes);
+  if (threads <= kSmallWarps * 32)
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        blocks_per_sm, gqa_decode_scan_kernel<kSmallWarps>, threads, smem_bytes);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      blocks_per_sm, gqa_decode_scan_kernel<kLargeWarps>, threads, smem_bytes);
 }
 
 cudaError_t read_status(int* status, int clear) {

@@ -131,9 +131,10 @@ def test_pick_splits(lib):
 
 
 def test_counter_region_grows_for_huge_batches(lib):
-    # 16384 requests x 8 warps = 131072 counters > the 65536 standard slots.
+    # (148 CTAs + 2 x 16384 rows) x 8 warps counters > the 65536 standard slots.
     rc, p = plan(lib, 16384, 32, 8)
     slots, qhr = 148 + 16384, 32
-    expect = (131072 * 4 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
+    counters = (148 + 2 * 16384) * 8
+    expect = ((counters * 4 + 255) // 256 * 256 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
               slots * qhr * 128 * 4)
     assert rc == 0 and p.workspace_bytes == expect
