@@ -64,6 +64,9 @@ def parse_args():
                     choices=["rep", "wide", "ragged", "long", "long_peaked"])
     ap.add_argument("--num-splits", default="auto",
                     help="auto = balanced schedule; an integer = fixed splits (v2)")
+    ap.add_argument("--kernel", default="auto", choices=["auto", "v0", "v1", "v2"],
+                    help="entry point timed: auto = gqa_decode (C ABI gqa_decode_launch); "
+                         "v0/v1/v2 = the reference-compatible binding functions")
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU-baseline budget (our arm, rank 0, N=1)")
     ap.add_argument("--ref-seconds", type=float, default=90.0,
@@ -433,7 +436,19 @@ def run_ours(args, world, rank, local):
     ns = 0 if args.num_splits == "auto" else int(args.num_splits)
 
     out = torch.empty_like(q)
-    if kind == "batch":
+    if kind == "batch" and args.kernel != "auto":
+        if args.kernel == "v2":
+            ns2 = 8 if ns == 0 else ns
+            fn = lambda *a: binding.gqa_decode_v2(*a, num_splits=ns2)  # noqa: E731
+            launches_per_step = 1 if ns2 == 1 else 2
+        else:
+            fn = binding.KERNELS[args.kernel]
+            launches_per_step = 1
+
+        def step():
+            out.copy_(fn(q, k, v, bt, sl, SCALE))
+        launches_per_step += 1  # the copy into the step's output buffer
+    elif kind == "batch":
         def step():
             binding.gqa_decode(q, k, v, bt, sl, SCALE, num_splits=ns, out=out)
         launches_per_step = 1 if ns in (0, 1) else 2
@@ -497,7 +512,10 @@ def run_ours(args, world, rank, local):
     # step i decodes, and step i's output is downloaded (second copy stream)
     # while step i+1 decodes; buffers are double-buffered.
     e2e = E2ELoop(q, bt, sl, out, stream)
-    if kind == "batch":
+    if kind == "batch" and args.kernel != "auto":
+        def decode(q_d, bt_d, sl_d, out_d):
+            out_d.copy_(fn(q_d, k, v, bt_d, sl_d, SCALE))
+    elif kind == "batch":
         def decode(q_d, bt_d, sl_d, out_d):
             binding.gqa_decode(q_d, k, v, bt_d, sl_d, SCALE, num_splits=ns, out=out_d)
     else:
@@ -532,7 +550,7 @@ def run_ours(args, world, rank, local):
                              "1.1426 ms per GiB = 939.7 GB/s",
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 q/K/V, cases.py recipe)",
         "config": dict(cfg, parallelism=f"dp{world}" if kind == "batch" else f"kv{world}",
-                       num_splits=args.num_splits,
+                       num_splits=args.num_splits, kernel=args.kernel,
                        l2="inputs > 126 MB L2 (1+ GiB KV per GPU); no flush needed",
                        kv_bytes_per_step=int(kv_total)),
         "e2e": {"value": round(kv_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",

@@ -110,7 +110,8 @@ cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
  * selects the balanced schedule: one persistent CTA per SM, each streaming
  * an equal share of all requests' KV, with partial rows merged in the same
  * launch.  num_blocks > 0 makes the kernel check every block id against
- * [0, num_blocks) (a bad id sets status bit 2 and reads block 0 instead).
+ * [0, num_blocks) (a bad id sets status bit 1, value 2, and reads block 0
+ * instead).
  * Workspace: gqa_decode_workspace_bytes, zeroed once with
  * gqa_decode_workspace_init.  Concurrent launches must not share one
  * workspace.  Additive to the reference API (its extension exposes
@@ -186,6 +187,14 @@ int gqa_decode_pick_splits(int B, int Hq, int Hkv, int seq_len, int num_sms);
  * out, bit 1 = a block id was out of range.  clear != 0 resets it.
  * Synchronous. */
 cudaError_t gqa_decode_get_status(int* status, int clear);
+
+/* Failure-detection self-test: launches one warp that waits on a pipeline
+ * barrier nothing will complete, with a limit of limit_us microseconds
+ * (1..2,000,000).  The wait gives up and sets status bit 0 exactly as a
+ * stuck pipeline in the decode kernels would; read it with
+ * gqa_decode_get_status.  No reference counterpart (the reference has no
+ * bounded waits). */
+cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream);
 
 /* Library version string. */
 const char* gqa_decode_version(void);

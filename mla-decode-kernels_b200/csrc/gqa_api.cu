@@ -434,6 +434,11 @@ cudaError_t gqa_decode_get_status(int* status, int clear) {
   return gqa::read_status(status, clear);
 }
 
+cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream) {
+  if (limit_us <= 0 || limit_us > 2000000) return cudaErrorInvalidValue;
+  return gqa::launch_wait_selftest(static_cast<unsigned long long>(limit_us) * 1000ull, stream);
+}
+
 const char* gqa_decode_version(void) { return "gqa_decode_b200 0.1.0 (sm_100a)"; }
 
 }  // extern "C"

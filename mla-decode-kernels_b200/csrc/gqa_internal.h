@@ -121,5 +121,6 @@ cudaError_t launch_shard_merge(const ShardMergeParams& p, cudaStream_t s);
 cudaError_t scan_kernel_set_smem(int smem_bytes);
 cudaError_t scan_kernel_occupancy(int threads, int smem_bytes, int* blocks_per_sm);
 cudaError_t read_status(int* status, int clear);
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t s);
 
 }  // namespace gqa

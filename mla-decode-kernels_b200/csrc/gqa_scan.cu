@@ -789,6 +789,27 @@ cudaError_t scan_kernel_occupancy(int threads, int smem_bytes, int* blocks_per_s
       blocks_per_sm, gqa_decode_scan_kernel<kLargeWarps>, threads, smem_bytes);
 }
 
+// Self-test of the bounded wait: one warp waits on an mbarrier phase that
+// nothing completes.  The wait must give up after limit_ns and report
+// kStatusWaitTimeout through the device status word, exactly as a stuck
+// pipeline in the scan kernel would, instead of hanging the GPU.
+__global__ void __launch_bounds__(32) gqa_decode_wait_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (!__all_sync(kFull, mbar_wait(b, 0, limit_ns)) && threadIdx.x == 0)
+    raise_status(kStatusWaitTimeout);
+}
+
+cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t s) {
+  gqa_decode_wait_selftest_kernel<<<1, 32, 0, s>>>(limit_ns);
+  return cudaGetLastError();
+}
+
 cudaError_t read_status(int* status, int clear) {
   cudaError_t e = cudaMemcpyFromSymbol(status, g_status, sizeof(int));
   if (e != cudaSuccess || !clear) return e;

@@ -33,6 +33,8 @@ lib.gqa_decode_workspace_bytes.argtypes = [_I, _I, _I, _I]
 lib.gqa_decode_workspace_bytes.restype = _Z
 lib.gqa_decode_get_status.argtypes = [ctypes.POINTER(_I), _I]
 lib.gqa_decode_get_status.restype = _I
+lib.gqa_decode_selftest_wait_timeout.argtypes = [_I, _P]
+lib.gqa_decode_selftest_wait_timeout.restype = _I
 
 
 def stream():

@@ -278,6 +278,21 @@ def test_bad_block_id_sets_status_without_fault():
     assert_close(out[:1], ref)
 
 
+def test_bounded_wait_times_out_with_status():
+    # A pipeline barrier that nothing completes: the wait must give up after
+    # its limit (50 ms here) and report status bit 0; the context stays usable.
+    import time
+
+    capi.status()
+    t0 = time.perf_counter()
+    assert capi.lib.gqa_decode_selftest_wait_timeout(50000, capi.stream()) == 0
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert capi.status() == 1
+    assert 0.04 < elapsed < 5.0
+    run_and_check(capi.auto, cases.ref_case("e_partial_blocks", seed=0))
+
+
 def test_cuda_graph_replay():
     q, k, v, bt, sl = to_gpu(cases.ref_case("a_base", seed=3))
     eager = binding.gqa_decode(q, k, v, bt, sl, SCALE)
