@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--ref-seconds", type=float, default=90.0,
                     help="total budget of the --impl reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="long workloads at N > 1: fused peer-memory merge or NCCL all-gather")
     ap.add_argument("--batch", type=int, default=None,
                     help="requests per GPU for rep / wide (smaller cases for profiling)")
     return ap.parse_args()
@@ -455,11 +457,16 @@ def run_ours(args, world, rank, local):
     else:
         import sharding
 
-        dec = sharding.KVRangeDecoder()
+        if args.exchange == "p2p":
+            dec = sharding.P2PKVRangeDecoder(q.shape[0], q.shape[1], k.shape[2], device)
+            launches_per_step = 1
+        else:
+            dec = sharding.KVRangeDecoder()
+            launches_per_step = 2
 
         def step():
             out.copy_(dec.decode(q, k, v, bt, sl, SCALE))
-        launches_per_step = 2
+        launches_per_step += 1  # the copy into the step's output buffer
 
     # correctness spot check before timing (bench/common.py:75-89): the first
     # two requests (or the whole shard) against the CPU oracle.
@@ -533,6 +540,8 @@ def run_ours(args, world, rank, local):
     if status:
         raise SystemExit(f"device status {status} after timing")
 
+    if kind == "kvrange" and hasattr(dec, "close"):
+        dec.close()
     if rank != 0:
         return
     peak, peak_src = measured_hbm_peak()
@@ -551,6 +560,7 @@ def run_ours(args, world, rank, local):
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 q/K/V, cases.py recipe)",
         "config": dict(cfg, parallelism=f"dp{world}" if kind == "batch" else f"kv{world}",
                        num_splits=args.num_splits, kernel=args.kernel,
+                       exchange=args.exchange if kind == "kvrange" else None,
                        l2="inputs > 126 MB L2 (1+ GiB KV per GPU); no flush needed",
                        kv_bytes_per_step=int(kv_total)),
         "e2e": {"value": round(kv_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",

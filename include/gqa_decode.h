@@ -139,6 +139,35 @@ cudaError_t gqa_decode_partial_launch(const gqa_bf16* q, const gqa_bf16* k_cache
                                       void* workspace, size_t workspace_bytes,
                                       cudaStream_t stream);
 
+/* Bytes of one rank's exchange buffer for gqa_decode_kvshard_launch with
+ * world ranks (1..8); 0 for invalid dims. */
+size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world);
+
+/* KV-range sharded decode with the cross-rank merge fused into the kernel
+ * (one launch per rank, no collective library).  Every rank holds the same
+ * q, block_table rows for its own contiguous page range of each request,
+ * and seq_lens = its tokens per request.  peer_buffers[r] is rank r's
+ * exchange buffer (gqa_decode_kvshard_buffer_bytes, zeroed once before the
+ * first call, 16-byte aligned) as mapped into this process (CUDA IPC;
+ * peer_buffers[rank] is this rank's own buffer).  The warp that finishes a
+ * request's state on this rank stores it into every rank's buffer with
+ * plain peer stores, publishes it with a system-scope release flag, waits
+ * (bounded, 4 s; on timeout status bit 2, value 4, and that output is left
+ * unwritten) for every rank's state and merges them into out, identical on
+ * all ranks.  epoch: non-zero, the same on every rank for one decode, +1 per
+ * decode (states are double-buffered by its parity).  Each rank must run on
+ * its own GPU: the ranks' kernels wait for one another.  The reference has no
+ * multi-GPU path; the merge is its split identity
+ * (kernels/gqa_decode/v2_splitkv.cu:97-107). */
+cudaError_t gqa_decode_kvshard_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                      const gqa_bf16* v_cache, const int* block_table,
+                                      const int* seq_lens, gqa_bf16* out, int B, int Hq, int Hkv,
+                                      int block_size, int max_blocks, int num_blocks,
+                                      float scale, int rank, int world,
+                                      void* const* peer_buffers, unsigned epoch,
+                                      void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream);
+
 /* Merge nshards states per row (state i of row r at index i * rows + r, acc
  * at (i * rows + r) * 128) into bf16 out [rows, 128] with the online-softmax
  * identity of kernels/gqa_decode/v2_splitkv.cu:97-107 (reference); rows whose
@@ -184,7 +213,8 @@ cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf16* k_cache
 int gqa_decode_pick_splits(int B, int Hq, int Hkv, int seq_len, int num_sms);
 
 /* Device status word of the current device: bit 0 = a pipeline wait timed
- * out, bit 1 = a block id was out of range.  clear != 0 resets it.
+ * out, bit 1 = a block id was out of range, bit 2 = a peer rank's state
+ * never arrived (gqa_decode_kvshard_launch).  clear != 0 resets it.
  * Synchronous. */
 cudaError_t gqa_decode_get_status(int* status, int clear);
 

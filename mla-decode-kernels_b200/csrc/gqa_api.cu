@@ -209,12 +209,28 @@ cudaError_t run_fixed(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v, c
   return gqa::launch_fixed_merge(mp, stream);
 }
 
-// BALANCED schedule, bf16 output or unnormalised states.
+// Peer-exchange arguments of the KV-range sharded decode.
+struct Exchange {
+  int world = 0, rank = 0;
+  unsigned epoch = 0;
+  void* const* peers = nullptr;
+};
+
+size_t exchange_flag_bytes(int B, const ShapePlan& sp, int world) {
+  return align_up(2ull * world * static_cast<size_t>(B) * sp.NHG * sp.ncw * sizeof(unsigned));
+}
+
+size_t exchange_bytes(int B, int Hq, const ShapePlan& sp, int world) {
+  return exchange_flag_bytes(B, sp, world) +
+         2ull * world * static_cast<size_t>(B) * Hq * gqa::kXStride * sizeof(float);
+}
+
+// BALANCED schedule: bf16 output, unnormalised states, or peer exchange.
 cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v, const int* bt,
                          const int* sl, gqa_bf16* out, float* res_m, float* res_l,
                          float* res_acc, int B, int Hq, int Hkv, int bs, int max_blocks,
                          int num_blocks, float scale, void* ws, size_t ws_bytes,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const Exchange* xchg = nullptr) {
   ShapePlan sp;
   const void* dst = out ? static_cast<const void*>(out) : static_cast<const void*>(res_acc);
   cudaError_t e = check_common(q, k, v, bt, sl, dst, B, Hq, Hkv, bs, max_blocks, &sp);
@@ -235,7 +251,22 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
   gqa::ScanParams p =
       base_params(q, k, v, bt, sl, B, Hq, Hkv, bs, max_blocks, num_blocks, scale, sp);
   p.out = out;
-  p.out_partial = out ? 0 : 1;
+  p.out_mode = out ? gqa::kOutBf16 : gqa::kOutState;
+  if (xchg) {
+    if (!out || xchg->world < 1 || xchg->world > gqa::kMaxPeers || xchg->rank < 0 ||
+        xchg->rank >= xchg->world || xchg->epoch == 0 || !xchg->peers)
+      return cudaErrorInvalidValue;
+    p.out_mode = gqa::kOutExchange;
+    p.xworld = xchg->world;
+    p.xrank = xchg->rank;
+    p.xepoch = xchg->epoch;
+    p.xunits = B * sp.NHG * sp.ncw;
+    p.xflag_bytes = static_cast<long long>(exchange_flag_bytes(B, sp, xchg->world));
+    for (int r = 0; r < xchg->world; ++r) {
+      if (!xchg->peers[r] || !aligned16(xchg->peers[r])) return cudaErrorInvalidValue;
+      p.xpeer[r] = static_cast<unsigned char*>(xchg->peers[r]);
+    }
+  }
   p.res_m = res_m;
   p.res_l = res_l;
   p.res_acc = res_acc;
@@ -385,6 +416,33 @@ cudaError_t gqa_decode_partial_launch(const gqa_bf16* q, const gqa_bf16* k_cache
   return run_balanced(q, k_cache, v_cache, block_table, seq_lens, nullptr, state_m, state_l,
                       state_acc, B, Hq, Hkv, block_size, max_blocks, num_blocks, scale,
                       workspace, workspace_bytes, stream);
+}
+
+size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world) {
+  ShapePlan sp;
+  if (gqa::make_shape_plan(Hq, Hkv, &sp) != 0 || B <= 0 || world < 1 ||
+      world > gqa::kMaxPeers)
+    return 0;
+  return exchange_bytes(B, Hq, sp, world);
+}
+
+cudaError_t gqa_decode_kvshard_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                      const gqa_bf16* v_cache, const int* block_table,
+                                      const int* seq_lens, gqa_bf16* out, int B, int Hq, int Hkv,
+                                      int block_size, int max_blocks, int num_blocks,
+                                      float scale, int rank, int world,
+                                      void* const* peer_buffers, unsigned epoch,
+                                      void* workspace, size_t workspace_bytes,
+                                      cudaStream_t stream) {
+  if (num_blocks < 0 || !out) return cudaErrorInvalidValue;
+  Exchange x;
+  x.world = world;
+  x.rank = rank;
+  x.epoch = epoch;
+  x.peers = peer_buffers;
+  return run_balanced(q, k_cache, v_cache, block_table, seq_lens, out, nullptr, nullptr, nullptr,
+                      B, Hq, Hkv, block_size, max_blocks, num_blocks, scale, workspace,
+                      workspace_bytes, stream, &x);
 }
 
 cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,

@@ -36,6 +36,19 @@ constexpr int kMaxStages = 8;
 
 enum Schedule : int { kFixed = 0, kBalanced = 1 };
 
+// Where a finished (request, q head) goes.
+enum OutMode : int {
+  kOutBf16 = 0,      // normalised bf16 `out`
+  kOutState = 1,     // unnormalised (m, l, acc) in res_* (KV shard, NCCL exchange)
+  kOutExchange = 2,  // state pushed to every rank's exchange buffer, merged in-kernel
+};
+
+// KV-range sharding over peer memory: every rank owns one exchange buffer
+// [flags: u32 [2][world][units] | states: f32 [2][world][B*Hq][kXStride]],
+// mapped into every other rank; [2] is the epoch parity.
+constexpr int kMaxPeers = 8;
+constexpr int kXStride = 132;  // floats per state: m, l, 2 pad, acc[128] (16-byte aligned)
+
 // Shape-only launch plan (no device state): how heads map to warps and how
 // large the stage ring is.
 struct ShapePlan {
@@ -61,14 +74,14 @@ struct ScanParams {
   const __nv_bfloat16* v;        // [num_blocks, bs, Hkv, 128]
   const int* block_table;        // [B, max_blocks]
   const int* seq_lens;           // [B]
-  __nv_bfloat16* out;            // [B, Hq, 128]; unused when out_partial
+  __nv_bfloat16* out;            // [B, Hq, 128]; unused with kOutState
   // Split partials.  FIXED: reference layout [B, Hq, num_splits](,128).
   // BALANCED: slot layout [slot, HG*G](,128), slot = cta + row.
   float* part_m;
   float* part_l;
   float* part_acc;
   int* counters;                 // BALANCED: [rows * ncw] arrival counters
-  // out_partial: the final per-(b, q-head) state is written unnormalised
+  // kOutState: the final per-(b, q-head) state is written unnormalised
   // here instead of bf16 `out` (KV-range sharding across GPUs).
   float* res_m;                  // [B, Hq]
   float* res_l;                  // [B, Hq]
@@ -79,8 +92,14 @@ struct ScanParams {
   int row_bytes, row_stride, stage_bytes, nstages;
   int schedule;                  // Schedule
   int num_splits;                // FIXED
-  int out_partial;               // 0/1
+  int out_mode;                  // OutMode
   float scale_log2;              // softmax scale * log2(e)
+  // kOutExchange
+  int xworld, xrank;
+  unsigned xepoch;               // != 0, identical on every rank for one decode
+  int xunits;                    // rows * ncw flags per (parity, source rank)
+  long long xflag_bytes;         // byte offset of the state area in a buffer
+  unsigned char* xpeer[kMaxPeers];  // exchange buffer of every rank ([xrank] = own)
 };
 
 struct MergeParams {

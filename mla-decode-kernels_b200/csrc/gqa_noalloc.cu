@@ -151,7 +151,7 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.nstages = sp.nstages;
   p.schedule = gqa::kBalanced;
   p.num_splits = 0;
-  p.out_partial = 0;
+  p.out_mode = gqa::kOutBf16;
   p.scale_log2 = scale * 1.4426950408889634f;
   return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
 }

@@ -20,6 +20,7 @@ constexpr unsigned long long kWaitLimitNs = 4000000000ull;
 // gqa_decode_get_status on the host).
 constexpr int kStatusWaitTimeout = 1;   // an mbarrier wait exceeded kWaitLimitNs
 constexpr int kStatusBadPage = 2;       // block_table entry outside [0, num_blocks)
+constexpr int kStatusPeerTimeout = 4;   // a peer rank's state never arrived
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -74,6 +75,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
       if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
+}
+
+// ---- system-scope flags (peer ranks over NVLink) ----------------------------
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ---- bulk copy (TMA, non-tensor) -----------------------------------------

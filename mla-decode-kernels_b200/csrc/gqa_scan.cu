@@ -194,23 +194,121 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float a, float 
   *reinterpret_cast<uint2*>(dst) = v;
 }
 
-// Zero output (or a neutral partial state) for the q heads [hbase, hbase+cnt)
-// of request b, which has no tokens.  The reference's kernels divide by
-// l = 0 there (docs/decisions/k1-004); python/reference.py yields 0.
-__device__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int lane) {
-  for (int n = 0; n < cnt; ++n) {
-    const size_t bh = static_cast<size_t>(b) * p.Hq + hbase + n;
-    if (p.out_partial) {
-      if (lane == 0) {
-        p.res_m[bh] = -INFINITY;
-        p.res_l[bh] = 0.f;
-      }
-      *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) =
-          make_float4(0.f, 0.f, 0.f, 0.f);
-    } else {
-      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, 0.f, 0.f, 0.f, 0.f);
+// ---- peer exchange (kOutExchange) -------------------------------------------
+//
+// The warp that owns the final state of a (row, warp unit) on this rank
+// stores it into slot `xrank` of every rank's exchange buffer (plain stores
+// to peer memory over NVLink), publishes it with a system-scope release
+// flag per destination, waits (bounded) for the flags of all ranks in its
+// own buffer, and merges the `xworld` states into `out`.  Flags and states
+// are double-buffered by epoch parity: a rank can only run one decode ahead
+// of a peer, so it never overwrites what the peer is still reading.
+
+__device__ __forceinline__ unsigned* xflag(const ScanParams& p, int owner, int src, int unit) {
+  return reinterpret_cast<unsigned*>(p.xpeer[owner]) +
+         (static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * p.xunits + unit);
+}
+
+__device__ __forceinline__ float* xstate(const ScanParams& p, int owner, int src, size_t bh) {
+  const size_t rows = static_cast<size_t>(p.B) * p.Hq;
+  return reinterpret_cast<float*>(p.xpeer[owner] + p.xflag_bytes) +
+         ((static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * rows + bh) * kXStride);
+}
+
+// Push one head's state, held lane-major (lane = 4 dims), to every rank.
+__device__ __forceinline__ void xput_lanes(const ScanParams& p, size_t bh, float m, float l,
+                                           float4 a, int lane) {
+  for (int o = 0; o < p.xworld; ++o) {
+    float* d = xstate(p, o, p.xrank, bh);
+    if (lane == 0) {
+      d[0] = m;
+      d[1] = l;
+    }
+    reinterpret_cast<float4*>(d + 4)[lane] = a;
+  }
+}
+
+// Publish this warp's states of unit `unit`, wait for every rank's, merge
+// heads [bh0, bh0 + cnt) and write bf16 out.  Rows empty on every rank give 0.
+__device__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
+  __threadfence_system();
+  __syncwarp();
+  if (lane < p.xworld) st_release_sys(xflag(p, lane, p.xrank, unit), p.xepoch);
+  bool ok = true;
+  if (lane < p.xworld) {
+    const unsigned* f = xflag(p, p.xrank, lane, unit);
+    ok = ld_acquire_sys(f) == p.xepoch;
+    if (!ok) {
+      const unsigned long long t0 = global_timer_ns();
+      while (!ok && global_timer_ns() - t0 < kWaitLimitNs) ok = ld_acquire_sys(f) == p.xepoch;
     }
   }
+  if (!__all_sync(kFull, ok)) {
+    if (lane == 0) raise_status(kStatusPeerTimeout);
+    return;
+  }
+  for (int i = 0; i < cnt; ++i) {
+    const size_t bh = bh0 + i;
+    float mk = -INFINITY, lk = 0.f;
+    if (lane < p.xworld) {
+      const float* st = xstate(p, p.xrank, lane, bh);
+      mk = __ldcg(st);
+      lk = __ldcg(st + 1);
+    }
+    float M = mk;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
+    const float w = (lane < p.xworld && M != -INFINITY) ? exp2f(mk - M) : 0.f;
+    float L = lk * w;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(kFull, L, off);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int o = 0; o < p.xworld; ++o) {
+      const float f = __shfl_sync(kFull, w, o);
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(xstate(p, p.xrank, o, bh) + 4) + lane);
+      a.x += x.x * f;
+      a.y += x.y * f;
+      a.z += x.z * f;
+      a.w += x.w * f;
+    }
+    if (M == -INFINITY) {
+      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, 0.f, 0.f, 0.f, 0.f);
+    } else {
+      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a.x / L, a.y / L, a.z / L, a.w / L);
+    }
+  }
+}
+
+// Final state of head bh, lane-major, to its destination by output mode
+// (kOutExchange: pushed to the ranks; the caller then runs xfinish).
+__device__ __forceinline__ void emit_final(const ScanParams& p, size_t bh, float M, float L,
+                                           float4 a, int lane) {
+  if (p.out_mode == kOutState) {
+    if (lane == 0) {
+      p.res_m[bh] = M;
+      p.res_l[bh] = L;
+    }
+    *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) = a;
+  } else if (p.out_mode == kOutExchange) {
+    xput_lanes(p, bh, M, L, a, lane);
+  } else {
+    store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a.x / L, a.y / L, a.z / L, a.w / L);
+  }
+}
+
+// Zero output (or a neutral state: m = -inf, l = 0, acc = 0) for the q heads
+// [hbase, hbase+cnt) of request b, which has no tokens on this rank.  The
+// reference's kernels divide by l = 0 there (docs/decisions/k1-004);
+// python/reference.py yields 0.  `unit` = row * ncw + warp (kOutExchange).
+__device__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int unit, int lane) {
+  const size_t bh0 = static_cast<size_t>(b) * p.Hq + hbase;
+  for (int n = 0; n < cnt; ++n) {
+    if (p.out_mode == kOutBf16)
+      store_bf16x4(p.out + (bh0 + n) * kHeadDim + 4 * lane, 0.f, 0.f, 0.f, 0.f);
+    else
+      emit_final(p, bh0 + n, -INFINITY, 0.f, make_float4(0.f, 0.f, 0.f, 0.f), lane);
+  }
+  if (p.out_mode == kOutExchange) xfinish(p, unit, bh0, cnt, lane);
 }
 
 // Partial states merged in one step.  Rows cut into more parts than this are
@@ -223,8 +321,8 @@ constexpr int kMergeBatch = 2;  // parts per batch of acc loads
 
 // Merge n unnormalised states of this warp's q heads [jj0, jj0 + cnt),
 // stored in slots first, first + stride, ...  With `final_` the result goes
-// to the output (normalised bf16, or unnormalised to res_* with
-// out_partial) of q heads bh0 + i; otherwise it overwrites slot `first`.
+// to the output of q heads bh0 + i (see emit_final); otherwise it overwrites
+// slot `first`.
 // Loads are batched so that the whole merge costs a few L2 round trips:
 // lanes hold one part each for (m, l), and every lane accumulates 4 output
 // dims of all kMergeHeads heads over kMergeBatch parts per batch.
@@ -317,17 +415,7 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
     for (int i = 0; i < kMergeHeads; ++i) {
       if (i0 + i >= cnt) continue;
       if (final_) {
-        const size_t bh = bh0 + i0 + i;
-        if (p.out_partial) {
-          if (lane == 0) {
-            p.res_m[bh] = M[i];
-            p.res_l[bh] = L[i];
-          }
-          *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) = a[i];
-        } else {
-          store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a[i].x / L[i], a[i].y / L[i],
-                       a[i].z / L[i], a[i].w / L[i]);
-        }
+        emit_final(p, bh0 + i0 + i, M[i], L[i], a[i], lane);
       } else {
         const size_t st = static_cast<size_t>(first) * QHR + jj0 + i0 + i;
         if (lane == 0) {
@@ -489,7 +577,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (eff_len(p.seq_lens, b, cap) != 0) continue;
       for (int hg = 0; hg < p.NHG; ++hg)
-        write_empty(p, b, (hg * p.HG + hl) * p.G + j0, cnt, lane);
+        write_empty(p, b, (hg * p.HG + hl) * p.G + j0, cnt, (b * p.NHG + hg) * p.ncw + warp,
+                    lane);
     }
   }
 
@@ -500,7 +589,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     const int hk = s.hg * p.HG + hl;
     const int hbase = hk * p.G + j0;
     if (s.kind == kZero) {
-      write_empty(p, s.b, hbase, cnt, lane);
+      write_empty(p, s.b, hbase, cnt, s.row * p.ncw + warp, lane);
       continue;
     }
     uint32_t qf[8][2];
@@ -593,7 +682,29 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
       l1 += __shfl_xor_sync(kFull, l1, off);
     }
     const int n0 = 2 * tig, n1 = 2 * tig + 1;
-    if (s.kind == kDirect && !p.out_partial) {
+    if (s.kind == kDirect && p.out_mode == kOutExchange) {
+      // Row finished inside this CTA: push the fragments' state to the ranks.
+      for (int o = 0; o < p.xworld; ++o) {
+        #pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          const int head = n ? n1 : n0;
+          if (head >= cnt) continue;
+          float* d = xstate(p, o, p.xrank, static_cast<size_t>(s.b) * p.Hq + hbase + head);
+          if (g == 0) {
+            d[0] = n ? m1 : m0;
+            d[1] = n ? l1 : l0;
+          }
+          #pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            d[4 + mt * 16 + g] = acc[mt][n];
+            d[4 + mt * 16 + g + 8] = acc[mt][2 + n];
+          }
+        }
+      }
+      xfinish(p, s.row * p.ncw + warp, static_cast<size_t>(s.b) * p.Hq + hbase, cnt, lane);
+      continue;
+    }
+    if (s.kind == kDirect && p.out_mode == kOutBf16) {
       #pragma unroll
       for (int n = 0; n < 2; ++n) {
         const int head = n ? n1 : n0;
@@ -608,7 +719,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
       }
       continue;
     }
-    // Unnormalised state: the CTA's partial slot, or (out_partial) the
+    // Unnormalised state: the CTA's partial slot, or (kOutState) the
     // request's final shard state.
     float* dm;
     float* dl;
@@ -661,6 +772,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
         if (arrive_last(row_ctr, s.nparts, lane)) {
           merge_parts(p, s.cfirst + s.row, 1, s.nparts, jj0, cnt, lane, true, bh0);
           if (lane == 0) *row_ctr = 0;
+          if (p.out_mode == kOutExchange) xfinish(p, s.row * p.ncw + warp, bh0, cnt, lane);
         }
       } else {
         const long long gi = (static_cast<long long>(blockIdx.x) - s.cfirst) / kMergeGroup;
@@ -680,6 +792,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
         if (group_done && arrive_last(row_ctr, ngroups, lane)) {
           merge_parts(p, s.cfirst + s.row, kMergeGroup, ngroups, jj0, cnt, lane, true, bh0);
           if (lane == 0) *row_ctr = 0;
+          if (p.out_mode == kOutExchange) xfinish(p, s.row * p.ncw + warp, bh0, cnt, lane);
         }
       }
     }

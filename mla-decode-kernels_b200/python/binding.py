@@ -113,6 +113,20 @@ def gqa_decode_partial(q, k_cache, v_cache, block_table, seq_lens, scale, check_
                                    bool(check_blocks))
 
 
+kvshard_buffer_bytes = _ext.kvshard_buffer_bytes
+
+
+def gqa_decode_kvshard(q, k_cache, v_cache, block_table, seq_lens, scale, rank, world,
+                       peer_ptrs, epoch, check_blocks=True):
+    """KV-range sharded decode with the cross-rank merge fused into the
+    kernel (peer stores + flags over NVLink); see sharding.P2PKVRangeDecoder."""
+    nbytes = _ext.workspace_bytes(q.shape[0], q.shape[1], k_cache.shape[2], 0)
+    ws = workspace(q.device, nbytes)
+    return _ext.gqa_decode_kvshard(q, k_cache, v_cache, block_table, seq_lens, float(scale),
+                                   int(rank), int(world), [int(x) for x in peer_ptrs], int(epoch),
+                                   ws, bool(check_blocks))
+
+
 # Reference registry (binding.py:31) plus the balanced schedule.
 KERNELS = {
     "v0": gqa_decode_v0,

@@ -200,6 +200,43 @@ std::vector<torch::Tensor> gqa_decode_partial(torch::Tensor q, torch::Tensor k_c
   return {m, l, acc};
 }
 
+// KV-range sharded decode with the cross-rank merge over peer memory; see
+// gqa_decode_kvshard_launch.  peer_ptrs[r] = rank r's exchange buffer as
+// mapped in this process.
+torch::Tensor gqa_decode_kvshard(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                 torch::Tensor block_table, torch::Tensor seq_lens, double scale,
+                                 int64_t rank, int64_t world, std::vector<int64_t> peer_ptrs,
+                                 int64_t epoch, torch::Tensor workspace, bool check_blocks) {
+  const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world,
+              "rank/world must satisfy 0 <= rank < world <= 8");
+  TORCH_CHECK(static_cast<int64_t>(peer_ptrs.size()) == world, "need one exchange buffer per rank");
+  TORCH_CHECK(epoch > 0 && epoch <= 0xffffffffLL, "epoch must be in [1, 2^32)");
+  TORCH_CHECK(workspace.is_cuda() && workspace.device() == q.device() && workspace.is_contiguous(),
+              "workspace must be a contiguous CUDA tensor on q's device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  void* peers[8] = {nullptr};
+  for (int64_t r = 0; r < world; ++r) peers[r] = reinterpret_cast<void*>(peer_ptrs[r]);
+  auto out = torch::empty_like(q);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(gqa_decode_kvshard_launch(
+                   bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache), block_table.data_ptr<int>(),
+                   seq_lens.data_ptr<int>(), reinterpret_cast<gqa_bf16*>(out.data_ptr()),
+                   static_cast<int>(d.B), static_cast<int>(d.Hq), static_cast<int>(d.Hkv),
+                   static_cast<int>(d.block_size), static_cast<int>(d.max_blocks),
+                   check_blocks ? static_cast<int>(d.num_blocks) : 0, static_cast<float>(scale),
+                   static_cast<int>(rank), static_cast<int>(world), peers,
+                   static_cast<unsigned>(epoch), workspace.data_ptr(), ws_bytes, stream),
+               "gqa_decode_kvshard");
+  return out;
+}
+
+int64_t kvshard_buffer_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t world) {
+  return static_cast<int64_t>(gqa_decode_kvshard_buffer_bytes(
+      static_cast<int>(B), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(world)));
+}
+
 // Merge states [nshards, rows] (+ acc [nshards, rows, 128]) into bf16 [rows, 128].
 torch::Tensor merge_states(torch::Tensor m, torch::Tensor l, torch::Tensor acc) {
   TORCH_CHECK(m.is_cuda() && l.is_cuda() && acc.is_cuda(), "states must be CUDA tensors");
@@ -254,6 +291,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("seq_lens"), py::arg("scale"), py::arg("workspace"),
         py::arg("check_blocks") = true);
+  m.def("gqa_decode_kvshard", &gqa_decode_kvshard,
+        "KV-range sharded decode, cross-rank merge over peer memory", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"), py::arg("seq_lens"),
+        py::arg("scale"), py::arg("rank"), py::arg("world"), py::arg("peer_ptrs"),
+        py::arg("epoch"), py::arg("workspace"), py::arg("check_blocks") = true);
+  m.def("kvshard_buffer_bytes", &kvshard_buffer_bytes, "exchange buffer bytes per rank");
   m.def("merge_states", &merge_states, "merge per-shard softmax states into bf16 output");
   m.def("workspace_bytes", &workspace_bytes, "workspace bytes for gqa_decode on this device");
   m.def("get_status", &get_status, "device status word", py::arg("clear") = false);

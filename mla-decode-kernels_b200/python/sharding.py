@@ -8,11 +8,16 @@ identity, kernels/gqa_decode/v2_splitkv.cu:97-107, is what crosses GPUs):
   requests from its own KV pages.  No communication on the data path.
 
 * KV-range sharding - one long request's pages are cut into contiguous
-  ranges, one per rank.  Every rank computes the unnormalised softmax state
-  (m, l, acc) of its range with gqa_decode_partial, the states are
-  all-gathered in one packed fp32 buffer (Hq * 130 floats per request per
-  rank: 16.6 KB at Hq = 32) and every rank merges them with the CUDA merge
-  kernel, so all ranks end with the same output.
+  ranges, one per rank.  Two exchanges of the per-rank softmax states:
+  - P2PKVRangeDecoder (default): one kernel per rank.  The warp that finishes
+    a request's state stores it straight into every rank's exchange buffer
+    (CUDA IPC mappings of one cudaMalloc per rank, plain peer stores over
+    NVLink), raises a release flag and merges all ranks' states once their
+    flags arrive (bounded wait), so the all-gather and the merge happen
+    inside the decode kernel.
+  - KVRangeDecoder: gqa_decode_partial, an NCCL all-gather of the packed
+    states (Hq * 130 floats per request per rank: 16.6 KB at Hq = 32) and the
+    merge kernel.  The collective-library baseline.
 """
 
 import datetime
@@ -108,3 +113,90 @@ class KVRangeDecoder:
         dist.all_gather_into_tensor(self._gathered, buf, group=self.group)
         mm, ll, aa = unpack_states(self._gathered.view(self.world, n), rows)
         return self._merge(mm, ll, aa).view(B, Hq, 128)
+
+
+def _cuda_check(err, what):
+    from cuda.bindings import runtime as rt
+
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"{what} failed: {err}")
+
+
+class P2PKVRangeDecoder:
+    """KV-range sharded decode with the cross-rank merge in the kernel.
+
+    Every rank allocates one exchange buffer (kvshard_buffer_bytes for the
+    batch shape) with cudaMalloc, exports it with CUDA IPC and maps every
+    peer's; the kernels then exchange states with plain peer stores.  Ranks
+    must sit on distinct GPUs of one node (their kernels wait for each
+    other).  decode() takes this rank's pages only and returns the full
+    [B, Hq, 128] bf16 output on every rank.  Call close() (collectively)
+    before the process group is destroyed.
+    """
+
+    def __init__(self, B, Hq, Hkv, device, group=None):
+        from cuda.bindings import runtime as rt
+
+        import binding
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("peer exchange supports up to 8 ranks")
+        self.device = torch.device(device)
+        self._binding = binding
+        self.nbytes = binding.kvshard_buffer_bytes(B, Hq, Hkv, self.world)
+        if self.nbytes <= 0:
+            raise ValueError("invalid shape for the peer exchange")
+        _cuda_check(rt.cudaSetDevice(self.device.index)[0], "cudaSetDevice")
+        err, self._own = rt.cudaMalloc(self.nbytes)
+        _cuda_check(err, "cudaMalloc")
+        _cuda_check(rt.cudaMemset(self._own, 0, self.nbytes)[0], "cudaMemset")
+        _cuda_check(rt.cudaDeviceSynchronize()[0], "cudaDeviceSynchronize")
+        self._opened = []
+        peers = [int(self._own)]
+        if self.world > 1:
+            err, handle = rt.cudaIpcGetMemHandle(self._own)
+            _cuda_check(err, "cudaIpcGetMemHandle")
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            info = [None] * self.world
+            dist.all_gather_object(info, (bytes(handle.reserved), uuid), group=group)
+            if len({u for _, u in info}) != self.world:
+                raise RuntimeError("every rank of a peer exchange needs its own GPU")
+            peers = []
+            for r, (hb, _) in enumerate(info):
+                if r == self.rank:
+                    peers.append(int(self._own))
+                    continue
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = hb
+                err, ptr = rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess)
+                _cuda_check(err, "cudaIpcOpenMemHandle")
+                self._opened.append(ptr)
+                peers.append(int(ptr))
+            dist.barrier(group=group)
+        self.peers = peers
+        self.epoch = 0
+
+    def decode(self, q, k_local, v_local, block_table_local, seq_lens_local, scale):
+        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFFF else 1
+        return self._binding.gqa_decode_kvshard(q, k_local, v_local, block_table_local,
+                                                seq_lens_local, scale, self.rank, self.world,
+                                                self.peers, self.epoch)
+
+    def close(self):
+        from cuda.bindings import runtime as rt
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for ptr in self._opened:
+            rt.cudaIpcCloseMemHandle(ptr)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        rt.cudaFree(self._own)
+        self._own = None

@@ -253,6 +253,27 @@ def test_kv_range_sharding_emulated(nshards, k_scale):
     check_subset(out, case, [0])
 
 
+@pytest.mark.parametrize("seq_lens", [[65536], [3000, 0, 17, 40000]])
+def test_kvshard_peer_exchange_single_rank(seq_lens):
+    # world = 1: the kernel pushes each state into its own exchange buffer,
+    # raises and reads its own flag and merges one state; two decodes in a row
+    # exercise both epoch parities.
+    import sharding
+
+    case = cases.make_case(seq_lens, 32, 8, 64, seed=26, pool_factor=1.0, device="cuda")
+    dec = sharding.P2PKVRangeDecoder(len(seq_lens), 32, 8, torch.device("cuda", 0))
+    try:
+        expect = capi.auto(*case, SCALE)
+        for _ in range(2):
+            out = dec.decode(*case, SCALE)
+            torch.cuda.synchronize()
+            check_status()
+            assert_close(out, expect, "peer exchange, one rank")
+        check_subset(out, case, [0])
+    finally:
+        dec.close()
+
+
 def test_merge_states_all_empty_shards():
     m = torch.full((3, 5), -float("inf"), device="cuda")
     l = torch.zeros(3, 5, device="cuda")

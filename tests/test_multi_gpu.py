@@ -1,10 +1,10 @@
 """GPU, 2+ devices: the two multi-GPU partitionings on real NCCL ranks.
 
 * KV-range sharding (config-5 recipe, shortened): every rank holds one
-  contiguous page range of a single request, KVRangeDecoder computes the
-  local softmax state, all-gathers the packed states over NCCL and merges
-  them; every rank's output must match the single-GPU decode of the whole
-  request (within the suite's tolerance) and the CPU oracle.
+  contiguous page range of a single request; KVRangeDecoder (local state,
+  NCCL all-gather, merge kernel) and P2PKVRangeDecoder (one kernel per rank,
+  states exchanged with peer stores + flags over NVLink) must both match the
+  single-GPU decode of the whole request on every rank.
 * Batch sharding: every rank decodes its LPT share of a ragged batch with
   the unsplit scan (v1), whose arithmetic for a request does not depend on
   the other requests in the launch; each output must equal, bitwise, the
@@ -49,7 +49,7 @@ def _worker(rank, world, port, mode, k_scale, result_dir):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     sharding.init_process_group("nccl", timeout_s=60)
-    if mode == "kvrange":
+    if mode in ("kvrange", "kvrange_p2p"):
         S, bs = 40000, 64
         # same request on every rank (same seed), each keeps its own page range
         q, k, v, bt, sl = cases.make_case([S], 32, 8, bs, seed=50, pool_factor=1.0,
@@ -57,10 +57,17 @@ def _worker(rank, world, port, mode, k_scale, result_dir):
         t0, t1 = sharding.kv_range(S, bs, rank, world)
         bt_r = bt[:, t0 // bs:(t1 + bs - 1) // bs].contiguous()
         sl_r = torch.tensor([t1 - t0], dtype=torch.int32, device=dev)
-        out = sharding.KVRangeDecoder().decode(q, k, v, bt_r, sl_r, SCALE)
+        if mode == "kvrange":
+            out = sharding.KVRangeDecoder().decode(q, k, v, bt_r, sl_r, SCALE)
+        else:
+            dec = sharding.P2PKVRangeDecoder(1, 32, 8, dev)
+            for _ in range(3):  # several epochs: both parities, reused buffers
+                out = dec.decode(q, k, v, bt_r, sl_r, SCALE)
+            torch.cuda.synchronize()
+            dec.close()
         full = binding.gqa_decode(q, k, v, bt, sl, SCALE)
         torch.cuda.synchronize()
-        np.save(os.path.join(result_dir, f"kv_{rank}.npy"),
+        np.save(os.path.join(result_dir, f"{mode}_{rank}.npy"),
                 np.stack([out.float().cpu().numpy(), full.float().cpu().numpy()]))
     else:
         sl_all = cases.config4_seq_lens(seed=1, B=24)
@@ -92,12 +99,13 @@ def _world():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["kvrange", "kvrange_p2p"])
 @pytest.mark.parametrize("k_scale", [1.0, 8.0])
-def test_kv_range_sharding_nccl(tmp_path, k_scale):
+def test_kv_range_sharding(tmp_path, mode, k_scale):
     world = _world()
-    _spawn(world, "kvrange", k_scale, tmp_path)
+    _spawn(world, mode, k_scale, tmp_path)
     for r in range(world):
-        out, full = np.load(tmp_path / f"kv_{r}.npy")
+        out, full = np.load(tmp_path / f"{mode}_{r}.npy")
         assert np.isfinite(out).all()
         np.testing.assert_allclose(out, full, atol=1e-2, rtol=1e-2)
 
