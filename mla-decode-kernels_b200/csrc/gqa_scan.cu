@@ -467,6 +467,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     }
     fence_mbar_init();
   }
+
   if (p.schedule == kBalanced) {
     balanced_start(p, cap, sh_warp, sh_info);  // contains __syncthreads
   } else {
@@ -801,7 +802,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
 
 // Merge for the FIXED schedule (reference workspace layout), one warp per
 // (b, q head), lane = 4 output dims.  Rows whose work fit in one split were
-// finished by the scan and are skipped.
+// finished by the scan and are skipped.  Lanes read the (m, l) of 32 splits
+// at once; acc rows are read 4 splits per batch so the loads overlap.
 __global__ void __launch_bounds__(128) gqa_decode_fixed_merge_kernel(const MergeParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long bh = static_cast<long long>(blockIdx.x) * 4 + warp;
@@ -812,23 +814,42 @@ __global__ void __launch_bounds__(128) gqa_decode_fixed_merge_kernel(const Merge
   const int L = (S + kStageTokens - 1) / kStageTokens;
   if (L == 0) return;
   const int chunk = (L + p.num_splits - 1) / p.num_splits;
-  const int nonempty = (L + chunk - 1) / chunk;
-  if (nonempty <= 1) return;
+  const int n = (L + chunk - 1) / chunk;
+  if (n <= 1) return;
   const size_t base = static_cast<size_t>(bh) * p.num_splits;
   float M = -INFINITY;
-  for (int i = lane; i < nonempty; i += 32) M = fmaxf(M, p.part_m[base + i]);
-  #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    float mk = c0 + lane < n ? __ldcg(p.part_m + base + c0 + lane) : -INFINITY;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, off));
+    M = fmaxf(M, mk);
+  }
   float Lsum = 0.f;
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i = 0; i < nonempty; ++i) {
-    const float f = exp2f(p.part_m[base + i] - M);
-    Lsum += p.part_l[base + i] * f;
-    const float4 x = reinterpret_cast<const float4*>(p.part_acc + (base + i) * kHeadDim)[lane];
-    a.x += x.x * f;
-    a.y += x.y * f;
-    a.z += x.z * f;
-    a.w += x.w * f;
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    const bool in = c0 + lane < n;
+    const float w = in ? exp2f(__ldcg(p.part_m + base + c0 + lane) - M) : 0.f;
+    float lw = in ? __ldcg(p.part_l + base + c0 + lane) * w : 0.f;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(kFull, lw, off);
+    Lsum += lw;
+    const int nc = min(32, n - c0);
+    for (int k0 = 0; k0 < nc; k0 += 4) {
+      float4 x[4];
+      #pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        x[kk] = k0 + kk < nc ? __ldcg(reinterpret_cast<const float4*>(
+                                   p.part_acc + (base + c0 + k0 + kk) * kHeadDim) + lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      #pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float f = __shfl_sync(kFull, w, (k0 + kk) & 31);
+        a.x += x[kk].x * f;
+        a.y += x[kk].y * f;
+        a.z += x[kk].z * f;
+        a.w += x[kk].w * f;
+      }
+    }
   }
   store_bf16x4(p.out + static_cast<size_t>(bh) * kHeadDim + 4 * lane, a.x / Lsum, a.y / Lsum,
                a.z / Lsum, a.w / Lsum);
