@@ -76,7 +76,7 @@ void gqa_decode_v2_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_
 cudaError_t gqa_decode_last_error(void);
 
 /* Shape plan of the pipelined kernel (no device access). */
-typedef struct gqa_decode_plan {
+typedef struct gqa_decode_plan_info {
   int group;             /* q heads per kv head, Hq / Hkv */
   int heads_per_row;     /* kv heads one CTA streams per token row */
   int consumer_warps;    /* tensor-core warps per CTA */
@@ -85,14 +85,14 @@ typedef struct gqa_decode_plan {
   int smem_bytes;        /* dynamic shared memory per CTA */
   int grid;              /* CTAs launched */
   size_t workspace_bytes;/* bytes gqa_decode_launch needs for these dims */
-} gqa_decode_plan;
+} gqa_decode_plan_info;
 
 /* Plan for the given dims on a GPU with num_sms SMs running ctas_per_sm CTAs
  * of this kernel each.  num_splits: 0 = balanced schedule, 1..512 = fixed
  * splits.  Returns 0, or -1 for invalid dims / -2 for Hq / Hkv > 128.
  * No reference counterpart (the reference sizes its grid in each launcher). */
 int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, int ctas_per_sm,
-                          gqa_decode_plan* plan);
+                          gqa_decode_plan_info* plan);
 
 /* Workspace bytes gqa_decode_launch / gqa_decode_partial_launch need on the
  * current device; 0 when none is needed.  No reference counterpart (the
@@ -138,6 +138,52 @@ cudaError_t gqa_decode_partial_launch(const gqa_bf16* q, const gqa_bf16* k_cache
                                       int max_blocks, int num_blocks, float scale,
                                       void* workspace, size_t workspace_bytes,
                                       cudaStream_t stream);
+
+/* Page table of a batch: dense (the reference's block_table [B, max_blocks]
+ * + seq_lens [B]) when block_table is non-NULL, else CSR (the FlashInfer
+ * paged layout the reference's baseline adapter converts to,
+ * bench/baselines/flashinfer_adapter.py:33-51): the pages of request b are
+ * kv_indices[kv_indptr[b] .. kv_indptr[b + 1]) and its last page holds
+ * kv_last_page_len[b] tokens.  num_blocks > 0 range-checks block ids. */
+typedef struct gqa_decode_pages {
+  const int* block_table;       /* dense [B, max_blocks], or NULL for CSR */
+  const int* seq_lens;          /* dense [B] */
+  int max_blocks;               /* dense: columns of block_table */
+  const int* kv_indptr;         /* CSR [B + 1] */
+  const int* kv_indices;        /* CSR [kv_indptr[B]] */
+  const int* kv_last_page_len;  /* CSR [B] */
+  int block_size;               /* tokens per page */
+  int num_blocks;               /* > 0: check block ids against [0, num_blocks) */
+} gqa_decode_pages;
+
+/* Convert a dense page table to CSR on the GPU (one small kernel), with the
+ * reference helper's arithmetic (bench/baselines/flashinfer_adapter.py:33-51):
+ * n_b = ceil(seq_lens[b] / page_size), kv_indptr = [0, prefix sums of n_b],
+ * kv_indices = the first n_b ids of every row, kv_last_page_len =
+ * seq_lens - (n_b - 1) * page_size.  kv_indices needs room for
+ * B * max_blocks ids. */
+cudaError_t gqa_decode_block_table_to_csr(const int* block_table, const int* seq_lens, int B,
+                                          int max_blocks, int page_size, int* kv_indptr,
+                                          int* kv_indices, int* kv_last_page_len,
+                                          cudaStream_t stream);
+
+/* Plan half of the plan/run split (the reference's FlashInfer baseline
+ * times only run(), docs/decisions/k1-007): computes on the GPU, into the
+ * workspace (gqa_decode_workspace_bytes(B, Hq, Hkv, 0), zeroed once), every
+ * CTA's share of the balanced schedule for this batch's lengths.  No host
+ * synchronisation.  The plan stays valid for any number of runs - e.g. all
+ * layers of a decode step - while the lengths, B, Hq and Hkv stay the same. */
+cudaError_t gqa_decode_plan(const gqa_decode_pages* pages, int B, int Hq, int Hkv,
+                            void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Run half: the balanced decode of gqa_decode_launch (num_splits = 0) reading
+ * its schedule from the workspace's plan instead of computing it, with a
+ * dense or CSR page table.  Launch-only on the host, so it can be captured in
+ * a CUDA graph. */
+cudaError_t gqa_decode_run(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                           const gqa_decode_pages* pages, gqa_bf16* out, int B, int Hq, int Hkv,
+                           float scale, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream);
 
 /* Bytes of one rank's exchange buffer for gqa_decode_kvshard_launch with
  * world ranks (1..8); 0 for invalid dims. */
@@ -192,7 +238,7 @@ cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
  * - Shapes whose scratch need exceeds it are rejected with
  *   cudaErrorInvalidValue before anything is launched.  The need is about
  *   (grid / rows_per_request + B) * Hq * 520 bytes (grid = one CTA per SM,
- *   rows_per_request = Hkv / heads_per_row of gqa_decode_plan): on a 148-SM
+ *   rows_per_request = Hkv / heads_per_row of gqa_decode_plan_info): on a 148-SM
  *   B200 with Hkv = 8, up to ~860 requests at Hq = 32 or ~350 at Hq = 64.
  * - The first call on a device looks up the array's device address
  *   (cudaGetSymbolAddress) with that device current; make that first call

@@ -57,9 +57,10 @@ size_t counter_region(size_t counters) {
 }
 
 struct BalancedLayout {
-  size_t counters, ncounters, m, l, acc, total;
+  size_t counters, ncounters, plan, prefix, m, l, acc, total;
 };
 
+// [counters | plan (header + one entry per CTA) | prefix [B + 1] | m | l | acc]
 BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
   const size_t rows = static_cast<size_t>(B) * sp.NHG;
   const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
@@ -67,7 +68,10 @@ BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
   BalancedLayout L;
   L.counters = 0;
   L.ncounters = (static_cast<size_t>(grid) + 2 * rows) * sp.ncw;
-  L.m = counter_region(L.ncounters);
+  L.plan = counter_region(L.ncounters);
+  L.prefix = L.plan + align_up((gqa::kPlanHeader + static_cast<size_t>(grid) * gqa::kPlanEntry) *
+                               sizeof(long long));
+  L.m = L.prefix + align_up((static_cast<size_t>(B) + 1) * sizeof(long long));
   L.l = L.m + align_up(slots * qhr * sizeof(float));
   L.acc = L.l + align_up(slots * qhr * sizeof(float));
   L.total = L.acc + align_up(slots * qhr * gqa::kHeadDim * sizeof(float));
@@ -147,6 +151,10 @@ gqa::ScanParams base_params(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16
   p.v = v;
   p.block_table = bt;
   p.seq_lens = sl;
+  // dense page table: the CSR pointers alias it (valid memory, never read)
+  p.kv_indptr = sl;
+  p.kv_indices = bt;
+  p.kv_last = sl;
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -207,6 +215,50 @@ cudaError_t run_fixed(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v, c
   mp.max_blocks = max_blocks;
   mp.num_splits = ns;
   return gqa::launch_fixed_merge(mp, stream);
+}
+
+// Page table of a launch, resolved from the C descriptor.
+struct Pages {
+  const int* bt = nullptr;
+  const int* sl = nullptr;
+  int max_blocks = 0;
+  const int* indptr = nullptr;
+  const int* indices = nullptr;
+  const int* last = nullptr;
+  int bs = 0;
+  int num_blocks = 0;
+  bool csr = false;
+};
+
+cudaError_t resolve_pages(const gqa_decode_pages* d, Pages* pg) {
+  if (!d || d->block_size <= 0 || d->num_blocks < 0) return cudaErrorInvalidValue;
+  pg->bs = d->block_size;
+  pg->num_blocks = d->num_blocks;
+  if (d->block_table) {
+    if (!d->seq_lens || d->max_blocks <= 0) return cudaErrorInvalidValue;
+    pg->bt = d->block_table;
+    pg->sl = d->seq_lens;
+    pg->max_blocks = d->max_blocks;
+    pg->csr = false;
+  } else {
+    if (!d->kv_indptr || !d->kv_indices || !d->kv_last_page_len) return cudaErrorInvalidValue;
+    pg->indptr = d->kv_indptr;
+    pg->indices = d->kv_indices;
+    pg->last = d->kv_last_page_len;
+    pg->max_blocks = 1;  // unused with CSR (lengths come from indptr)
+    pg->csr = true;
+  }
+  // The kernels read only the active table; the other one's pointers still
+  // point at valid device memory (the active arrays), never at null.
+  if (pg->csr) {
+    pg->bt = pg->indices;
+    pg->sl = pg->last;
+  } else {
+    pg->indptr = pg->sl;
+    pg->indices = pg->bt;
+    pg->last = pg->sl;
+  }
+  return cudaSuccess;
 }
 
 // Peer-exchange arguments of the KV-range sharded decode.
@@ -334,7 +386,7 @@ cudaError_t gqa_decode_last_error(void) {
 }
 
 int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, int ctas_per_sm,
-                          gqa_decode_plan* plan) {
+                          gqa_decode_plan_info* plan) {
   ShapePlan sp;
   const int rc = gqa::make_shape_plan(Hq, Hkv, &sp);
   if (rc != 0) return rc;
@@ -416,6 +468,90 @@ cudaError_t gqa_decode_partial_launch(const gqa_bf16* q, const gqa_bf16* k_cache
   return run_balanced(q, k_cache, v_cache, block_table, seq_lens, nullptr, state_m, state_l,
                       state_acc, B, Hq, Hkv, block_size, max_blocks, num_blocks, scale,
                       workspace, workspace_bytes, stream);
+}
+
+cudaError_t gqa_decode_block_table_to_csr(const int* block_table, const int* seq_lens, int B,
+                                          int max_blocks, int page_size, int* kv_indptr,
+                                          int* kv_indices, int* kv_last_page_len,
+                                          cudaStream_t stream) {
+  if (B < 0 || max_blocks <= 0 || page_size <= 0) return cudaErrorInvalidValue;
+  if (B == 0) return kv_indptr ? cudaMemsetAsync(kv_indptr, 0, sizeof(int), stream)
+                               : cudaErrorInvalidValue;
+  if (!block_table || !seq_lens || !kv_indptr || !kv_indices || !kv_last_page_len)
+    return cudaErrorInvalidValue;
+  return gqa::launch_block_table_to_csr(block_table, seq_lens, B, max_blocks, page_size, kv_indptr,
+                                        kv_indices, kv_last_page_len, stream);
+}
+
+cudaError_t gqa_decode_plan(const gqa_decode_pages* pages, int B, int Hq, int Hkv,
+                            void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  ShapePlan sp;
+  Pages pg;
+  cudaError_t e = resolve_pages(pages, &pg);
+  if (e != cudaSuccess) return e;
+  if (B <= 0 || gqa::make_shape_plan(Hq, Hkv, &sp) != 0) return cudaErrorInvalidValue;
+  int sms = 0, occ = 0;
+  e = device_facts(sp, &sms, &occ);
+  if (e != cudaSuccess) return e;
+  const int grid = sms * occ;
+  const BalancedLayout lay = balanced_layout(B, sp, grid);
+  if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
+    return cudaErrorInvalidValue;
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  gqa::ScanParams p{};
+  p.block_table = pg.bt;
+  p.seq_lens = pg.sl;
+  p.kv_indptr = pg.indptr;
+  p.kv_indices = pg.indices;
+  p.kv_last = pg.last;
+  p.csr = pg.csr ? 1 : 0;
+  p.B = B;
+  p.bs = pg.bs;
+  p.max_blocks = pg.max_blocks;
+  p.NHG = sp.NHG;
+  return gqa::launch_plan(p, reinterpret_cast<long long*>(w + lay.plan),
+                          reinterpret_cast<long long*>(w + lay.prefix), grid, stream);
+}
+
+cudaError_t gqa_decode_run(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                           const gqa_decode_pages* pages, gqa_bf16* out, int B, int Hq, int Hkv,
+                           float scale, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  ShapePlan sp;
+  Pages pg;
+  cudaError_t e = resolve_pages(pages, &pg);
+  if (e != cudaSuccess) return e;
+  e = check_common(q, k_cache, v_cache, pg.csr ? pg.indices : pg.bt,
+                   pg.csr ? pg.indptr : pg.sl, out, B, Hq, Hkv, pg.bs, pg.max_blocks, &sp);
+  if (e != cudaSuccess) return e;
+  if (B == 0) return cudaSuccess;
+  int sms = 0, occ = 0;
+  e = device_facts(sp, &sms, &occ);
+  if (e != cudaSuccess) return e;
+  const int grid = sms * occ;
+  const BalancedLayout lay = balanced_layout(B, sp, grid);
+  if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
+    return cudaErrorInvalidValue;
+  unsigned char* w = static_cast<unsigned char*>(workspace);
+  if (lay.ncounters > kCounterSlots) {
+    e = cudaMemsetAsync(w + lay.counters, 0, lay.ncounters * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+  }
+  gqa::ScanParams p = base_params(q, k_cache, v_cache, pg.bt, pg.sl, B, Hq, Hkv, pg.bs,
+                                  pg.max_blocks, pg.num_blocks, scale, sp);
+  p.kv_indptr = pg.indptr;
+  p.kv_indices = pg.indices;
+  p.kv_last = pg.last;
+  p.csr = pg.csr ? 1 : 0;
+  p.plan = reinterpret_cast<const long long*>(w + lay.plan);
+  p.out = out;
+  p.out_mode = gqa::kOutBf16;
+  p.counters = reinterpret_cast<int*>(w + lay.counters);
+  p.part_m = reinterpret_cast<float*>(w + lay.m);
+  p.part_l = reinterpret_cast<float*>(w + lay.l);
+  p.part_acc = reinterpret_cast<float*>(w + lay.acc);
+  p.schedule = gqa::kBalanced;
+  return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
 }
 
 size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world) {

@@ -72,8 +72,18 @@ struct ScanParams {
   const __nv_bfloat16* q;        // [B, Hq, 128]
   const __nv_bfloat16* k;        // [num_blocks, bs, Hkv, 128]
   const __nv_bfloat16* v;        // [num_blocks, bs, Hkv, 128]
-  const int* block_table;        // [B, max_blocks]
+  const int* block_table;        // [B, max_blocks] (dense page table)
   const int* seq_lens;           // [B]
+  // CSR page table (csr != 0): pages of request b are
+  // kv_indices[kv_indptr[b] .. kv_indptr[b+1]), its last page holding
+  // kv_last[b] tokens.
+  const int* kv_indptr;
+  const int* kv_indices;
+  const int* kv_last;
+  int csr;
+  // Precomputed BALANCED schedule (gqa_decode_plan), or null to compute the
+  // CTA's range in the kernel: [T, W, grid, ...(8)] then per CTA {g0, g1, b0, P0}.
+  const long long* plan;
   __nv_bfloat16* out;            // [B, Hq, 128]; unused with kOutState
   // Split partials.  FIXED: reference layout [B, Hq, num_splits](,128).
   // BALANCED: slot layout [slot, HG*G](,128), slot = cta + row.
@@ -141,5 +151,15 @@ cudaError_t scan_kernel_set_smem(int smem_bytes);
 cudaError_t scan_kernel_occupancy(int threads, int smem_bytes, int* blocks_per_sm);
 cudaError_t read_status(int* status, int clear);
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t s);
+// BALANCED plan for `grid` CTAs into plan (header + entries) using prefix
+// ([B + 1] int64 scratch); p supplies the page table and shape.
+cudaError_t launch_plan(const ScanParams& p, long long* plan, long long* prefix, int grid,
+                        cudaStream_t s);
+// block_table / seq_lens -> CSR (reference bench/baselines/flashinfer_adapter.py:33-51).
+cudaError_t launch_block_table_to_csr(const int* block_table, const int* seq_lens, int B,
+                                      int max_blocks, int page_size, int* indptr, int* indices,
+                                      int* last_page_len, cudaStream_t s);
+constexpr int kPlanHeader = 8;   // int64 header words of a plan
+constexpr int kPlanEntry = 4;    // int64 words per CTA entry
 
 }  // namespace gqa

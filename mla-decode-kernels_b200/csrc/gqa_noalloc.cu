@@ -129,6 +129,9 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.v = v_cache;
   p.block_table = block_table;
   p.seq_lens = seq_lens;
+  p.kv_indptr = seq_lens;  // dense page table; the CSR pointers are never read
+  p.kv_indices = block_table;
+  p.kv_last = seq_lens;
   p.out = out;
   p.counters = reinterpret_cast<int*>(st->scratch);
   p.part_m = reinterpret_cast<float*>(st->scratch + off_m);

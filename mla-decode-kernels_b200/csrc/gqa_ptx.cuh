@@ -77,6 +77,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// ---- loads that must stay inside their branch -------------------------------
+
+// Read-only 32-bit load that the compiler can never speculate: a volatile asm
+// is not executed outside the control flow that reaches it, so a load through
+// the unused page table's pointer cannot be hoisted above the test selecting
+// the page-table kind.
+__device__ __forceinline__ int ld_nc_s32(const int* p) {
+  int v;
+  asm volatile("ld.global.nc.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // ---- system-scope flags (peer ranks over NVLink) ----------------------------
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {

@@ -41,10 +41,28 @@ __device__ __forceinline__ void raise_status(int bits) { atomicOr(&g_status, bit
 // Tokens of request b that are read: seq_lens[b] clamped to the table's
 // capacity, so a bad length can never walk past the request's table row.
 __device__ __forceinline__ int eff_len(const int* seq_lens, int b, long long cap) {
-  long long s = __ldg(&seq_lens[b]);
+  long long s = ld_nc_s32(&seq_lens[b]);
   if (s < 0) s = 0;
   if (s > cap) s = cap;
   return static_cast<int>(s);
+}
+
+// Tokens of request b under the launch's page table.  CSR: (pages - 1) *
+// bs + tokens of the last page, clamped to the pages present.
+__device__ __forceinline__ int req_len(const ScanParams& p, int b, long long cap) {
+  if (!p.csr) return eff_len(p.seq_lens, b, cap);
+  const int n = ld_nc_s32(&p.kv_indptr[b + 1]) - ld_nc_s32(&p.kv_indptr[b]);
+  if (n <= 0) return 0;
+  long long s = static_cast<long long>(n - 1) * p.bs + ld_nc_s32(&p.kv_last[b]);
+  if (s < 0) s = 0;
+  if (s > static_cast<long long>(n) * p.bs) s = static_cast<long long>(n) * p.bs;
+  return static_cast<int>(s);
+}
+
+// Physical block ids of request b, indexed by logical block.
+__device__ __forceinline__ const int* page_row(const ScanParams& p, int b) {
+  if (p.csr) return p.kv_indices + ld_nc_s32(&p.kv_indptr[b]);
+  return p.block_table + static_cast<size_t>(b) * p.max_blocks;
 }
 
 struct Seg {
@@ -76,7 +94,7 @@ __device__ __forceinline__ bool iter_next(SegIter& it, const ScanParams& p, long
       const int split = t - row * ns;
       const int b = row / p.NHG;
       const int hg = row - b * p.NHG;
-      const int S = eff_len(p.seq_lens, b, cap);
+      const int S = req_len(p, b, cap);
       const int L = (S + kStageTokens - 1) / kStageTokens;
       if (L == 0) {
         if (split != 0) continue;
@@ -104,7 +122,7 @@ __device__ __forceinline__ bool iter_next(SegIter& it, const ScanParams& p, long
           it.g = it.g_end;
           return false;
         }
-        it.S = eff_len(p.seq_lens, it.b, cap);
+        it.S = req_len(p, it.b, cap);
         it.L = (it.S + kStageTokens - 1) / kStageTokens;
       }
       continue;
@@ -128,7 +146,7 @@ __device__ __forceinline__ bool iter_next(SegIter& it, const ScanParams& p, long
 
 // Block-wide start of the CTA's range in the BALANCED schedule.  Every
 // thread takes part; afterwards sh_* hold the range and its first request.
-__device__ void balanced_start(const ScanParams& p, long long cap, long long* sh_warp,
+__device__ __forceinline__ void balanced_start(const ScanParams& p, long long cap, long long* sh_warp,
                                long long* sh_info) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthr = blockDim.x, nwarps = nthr >> 5;
@@ -136,7 +154,7 @@ __device__ void balanced_start(const ScanParams& p, long long cap, long long* sh
   const int blo = min(p.B, tid * chunk), bhi = min(p.B, blo + chunk);
   long long local = 0;
   for (int b = blo; b < bhi; ++b)
-    local += (eff_len(p.seq_lens, b, cap) + kStageTokens - 1) / kStageTokens;
+    local += (req_len(p, b, cap) + kStageTokens - 1) / kStageTokens;
   long long x = local;
   #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
@@ -174,7 +192,7 @@ __device__ void balanced_start(const ScanParams& p, long long cap, long long* sh
   if (g0 < g1 && g0 >= excl * p.NHG && g0 < (excl + local) * p.NHG) {
     long long P = excl;
     for (int b = blo; b < bhi; ++b) {
-      const long long L = (eff_len(p.seq_lens, b, cap) + kStageTokens - 1) / kStageTokens;
+      const long long L = (req_len(p, b, cap) + kStageTokens - 1) / kStageTokens;
       if (g0 < (P + L) * p.NHG) {
         sh_info[3] = b;
         sh_info[4] = P;
@@ -230,7 +248,7 @@ __device__ __forceinline__ void xput_lanes(const ScanParams& p, size_t bh, float
 
 // Publish this warp's states of unit `unit`, wait for every rank's, merge
 // heads [bh0, bh0 + cnt) and write bf16 out.  Rows empty on every rank give 0.
-__device__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
+__device__ __forceinline__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
   __threadfence_system();
   __syncwarp();
   if (lane < p.xworld) st_release_sys(xflag(p, lane, p.xrank, unit), p.xepoch);
@@ -251,7 +269,8 @@ __device__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int 
     const size_t bh = bh0 + i;
     float mk = -INFINITY, lk = 0.f;
     if (lane < p.xworld) {
-      const float* st = xstate(p, p.xrank, lane, bh);
+      // source index clamped so the address is valid on every lane
+      const float* st = xstate(p, p.xrank, min(lane, p.xworld - 1), bh);
       mk = __ldcg(st);
       lk = __ldcg(st + 1);
     }
@@ -300,7 +319,7 @@ __device__ __forceinline__ void emit_final(const ScanParams& p, size_t bh, float
 // [hbase, hbase+cnt) of request b, which has no tokens on this rank.  The
 // reference's kernels divide by l = 0 there (docs/decisions/k1-004);
 // python/reference.py yields 0.  `unit` = row * ncw + warp (kOutExchange).
-__device__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int unit, int lane) {
+__device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int unit, int lane) {
   const size_t bh0 = static_cast<size_t>(b) * p.Hq + hbase;
   for (int n = 0; n < cnt; ++n) {
     if (p.out_mode == kOutBf16)
@@ -340,12 +359,15 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
     }
     // pass 1: M per head over all parts (the first 32 parts stay in registers)
     for (int c0 = 0; c0 < n; c0 += 32) {
+      // part index clamped into range: every address is valid on every lane
+      const size_t srow =
+          static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
+              QHR + jj0;
       #pragma unroll
       for (int i = 0; i < kMergeHeads; ++i) {
         float mk = -INFINITY, lk = 0.f;
         if (i0 + i < cnt && c0 + lane < n) {
-          const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + lane) * stride) *
-                                QHR + jj0 + i0 + i;
+          const size_t st = srow + min(i0 + i, cnt - 1);
           mk = __ldcg(p.part_m + st);
           lk = __ldcg(p.part_l + st);
         }
@@ -364,6 +386,9 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
     for (int i = 0; i < kMergeHeads; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int c0 = 0; c0 < n; c0 += 32) {
       float w[kMergeHeads];
+      const size_t srow =
+          static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
+              QHR + jj0;
       #pragma unroll
       for (int i = 0; i < kMergeHeads; ++i) {
         float mk = m0[i], lk = l0[i];
@@ -371,8 +396,7 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
           mk = -INFINITY;
           lk = 0.f;
           if (i0 + i < cnt && c0 + lane < n) {
-            const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + lane) *
-                                                              stride) * QHR + jj0 + i0 + i;
+            const size_t st = srow + min(i0 + i, cnt - 1);
             mk = __ldcg(p.part_m + st);
             lk = __ldcg(p.part_l + st);
           }
@@ -392,8 +416,9 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
           for (int kk = 0; kk < kMergeBatch; ++kk) {
             x[i][kk] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i0 + i < cnt && k0 + kk < nc) {
-              const size_t st = static_cast<size_t>(first + static_cast<long long>(c0 + k0 + kk) *
-                                                                stride) * QHR + jj0 + i0 + i;
+              const int kc = c0 + min(k0 + kk, nc - 1), ic = min(i0 + i, cnt - 1);
+              const size_t st =
+                  static_cast<size_t>(first + static_cast<long long>(kc) * stride) * QHR + jj0 + ic;
               x[i][kk] = __ldcg(reinterpret_cast<const float4*>(p.part_acc + st * kHeadDim) + lane);
             }
           }
@@ -447,7 +472,8 @@ __device__ __forceinline__ bool arrive_last(int* ctr, int total, int lane) {
 // budget fits it: 9 warps for groups of up to 8 heads per kv head (the common
 // shapes, no spills), 17 for the widest groups.
 template <int kMaxWarps>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+    gqa_decode_scan_kernel(const __grid_constant__ ScanParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ long long sh_warp[32];
   __shared__ long long sh_info[8];
@@ -468,7 +494,16 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     fence_mbar_init();
   }
 
-  if (p.schedule == kBalanced) {
+  if (p.schedule == kBalanced && p.plan) {
+    if (threadIdx.x < 4) {
+      const long long* e = p.plan + kPlanHeader + static_cast<size_t>(blockIdx.x) * kPlanEntry;
+      // entry {g0, g1, b0, P0} -> sh_info {g0, g1, W, b0, P0}
+      sh_info[threadIdx.x < 2 ? threadIdx.x : threadIdx.x + 1] = e[threadIdx.x];
+    } else if (threadIdx.x == 4) {
+      sh_info[2] = p.plan[1];
+    }
+    __syncthreads();
+  } else if (p.schedule == kBalanced) {
     balanced_start(p, cap, sh_warp, sh_info);  // contains __syncthreads
   } else {
     __syncthreads();
@@ -486,7 +521,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     it.b = static_cast<int>(sh_info[3]);
     it.row0 = sh_info[4] * p.NHG;
     it.hg = 0;
-    it.S = it.g < it.g_end ? eff_len(p.seq_lens, it.b, cap) : 0;
+    it.S = it.g < it.g_end ? req_len(p, it.b, cap) : 0;
     it.L = (it.S + kStageTokens - 1) / kStageTokens;
   }
 
@@ -506,7 +541,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
     Seg s;
     while (ok && iter_next(it, p, cap, s)) {
       if (s.kind == kZero) continue;
-      const int* bt_row = p.block_table + static_cast<size_t>(s.b) * p.max_blocks;
+      const int* bt_row = page_row(p, s.b);
       const size_t head_off = static_cast<size_t>(s.hg) * p.HG;
       for (int st = s.s0; st < s.s1; ++st) {
         const int tok0 = st * kStageTokens;
@@ -576,7 +611,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gqa_decode_scan_kernel(cons
   if (p.schedule == kBalanced) {
     // Requests without tokens occupy no stages; CTA (b mod grid) writes them.
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-      if (eff_len(p.seq_lens, b, cap) != 0) continue;
+      if (req_len(p, b, cap) != 0) continue;
       for (int hg = 0; hg < p.NHG; ++hg)
         write_empty(p, b, (hg * p.HG + hl) * p.G + j0, cnt, (b * p.NHG + hg) * p.ncw + warp,
                     lane);
@@ -819,7 +854,8 @@ __global__ void __launch_bounds__(128) gqa_decode_fixed_merge_kernel(const Merge
   const size_t base = static_cast<size_t>(bh) * p.num_splits;
   float M = -INFINITY;
   for (int c0 = 0; c0 < n; c0 += 32) {
-    float mk = c0 + lane < n ? __ldcg(p.part_m + base + c0 + lane) : -INFINITY;
+    const int kc = min(c0 + lane, n - 1);  // in range on every lane
+    float mk = c0 + lane < n ? __ldcg(p.part_m + base + kc) : -INFINITY;
     #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, off));
     M = fmaxf(M, mk);
@@ -828,8 +864,9 @@ __global__ void __launch_bounds__(128) gqa_decode_fixed_merge_kernel(const Merge
   float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int c0 = 0; c0 < n; c0 += 32) {
     const bool in = c0 + lane < n;
-    const float w = in ? exp2f(__ldcg(p.part_m + base + c0 + lane) - M) : 0.f;
-    float lw = in ? __ldcg(p.part_l + base + c0 + lane) * w : 0.f;
+    const int kc = min(c0 + lane, n - 1);
+    const float w = in ? exp2f(__ldcg(p.part_m + base + kc) - M) : 0.f;
+    float lw = in ? __ldcg(p.part_l + base + kc) * w : 0.f;
     #pragma unroll
     for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(kFull, lw, off);
     Lsum += lw;
@@ -838,9 +875,11 @@ __global__ void __launch_bounds__(128) gqa_decode_fixed_merge_kernel(const Merge
       float4 x[4];
       #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
-        x[kk] = k0 + kk < nc ? __ldcg(reinterpret_cast<const float4*>(
-                                   p.part_acc + (base + c0 + k0 + kk) * kHeadDim) + lane)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[kk] = k0 + kk < nc
+                    ? __ldcg(reinterpret_cast<const float4*>(
+                                 p.part_acc + (base + c0 + min(k0 + kk, nc - 1)) * kHeadDim) +
+                             lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
       #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const float f = __shfl_sync(kFull, w, (k0 + kk) & 31);
@@ -941,6 +980,128 @@ __global__ void __launch_bounds__(32) gqa_decode_wait_selftest_kernel(unsigned l
 
 cudaError_t launch_wait_selftest(unsigned long long limit_ns, cudaStream_t s) {
   gqa_decode_wait_selftest_kernel<<<1, 32, 0, s>>>(limit_ns);
+  return cudaGetLastError();
+}
+
+// Block-wide inclusive scan of one int64 per thread (blockDim.x <= 1024).
+__device__ long long block_inclusive_scan(long long x, long long* sh_warp, long long* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  #pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const long long y = __shfl_up_sync(kFull, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) sh_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    long long t = lane < nwarps ? sh_warp[lane] : 0;
+    #pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long y = __shfl_up_sync(kFull, t, off);
+      if (lane >= off) t += y;
+    }
+    if (lane < nwarps) sh_warp[lane] = t;
+  }
+  __syncthreads();
+  const long long r = x + (warp > 0 ? sh_warp[warp - 1] : 0);
+  *total = sh_warp[nwarps - 1];
+  __syncthreads();
+  return r;
+}
+
+// One CTA: stage prefix over the requests, then every CTA's range of the
+// BALANCED schedule - the same cut balanced_start computes inside the scan.
+__global__ void __launch_bounds__(1024)
+    gqa_decode_plan_kernel(const __grid_constant__ ScanParams p, long long* plan, long long* prefix,
+                           int grid) {
+  __shared__ long long sh_warp[32];
+  const long long cap = static_cast<long long>(p.max_blocks) * p.bs;
+  long long carry = 0;
+  if (threadIdx.x == 0) prefix[0] = 0;
+  for (int b0 = 0; b0 < p.B; b0 += blockDim.x) {
+    const int b = b0 + threadIdx.x;
+    const long long L = b < p.B ? (req_len(p, b, cap) + kStageTokens - 1) / kStageTokens : 0;
+    long long total;
+    const long long incl = block_inclusive_scan(L, sh_warp, &total);
+    if (b < p.B) prefix[b + 1] = carry + incl;
+    carry += total;
+  }
+  __syncthreads();
+  const long long T = carry * p.NHG;
+  long long W = (T + grid - 1) / grid;
+  if (W < 2) W = 2;
+  if (threadIdx.x == 0) {
+    plan[0] = T;
+    plan[1] = W;
+    plan[2] = grid;
+  }
+  for (int c = threadIdx.x; c < grid; c += blockDim.x) {
+    const long long g0 = min(T, static_cast<long long>(c) * W);
+    const long long g1 = min(T, g0 + W);
+    int b0 = 0;
+    if (g0 < g1) {
+      // last request whose stages start at or before g0 (an empty request
+      // never qualifies: the next one starts at the same stage)
+      int lo = 0, hi = p.B - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] * p.NHG <= g0) lo = mid; else hi = mid - 1;
+      }
+      b0 = lo;
+    }
+    long long* e = plan + kPlanHeader + static_cast<size_t>(c) * kPlanEntry;
+    e[0] = g0;
+    e[1] = g1;
+    e[2] = b0;
+    e[3] = prefix[b0];
+  }
+}
+
+// One CTA: block_table [B, max_blocks] + seq_lens -> CSR, with the reference
+// helper's arithmetic (bench/baselines/flashinfer_adapter.py:33-51):
+// n = ceil(S / page), indptr = prefix of n, indices = the first n ids of each
+// row, last_page_len = S - (n - 1) * page.
+__global__ void __launch_bounds__(1024) gqa_decode_block_table_to_csr_kernel(
+    const int* block_table, const int* seq_lens, int B, int max_blocks, int page, int* indptr,
+    int* indices, int* last_page_len) {
+  __shared__ long long sh_warp[32];
+  long long carry = 0;
+  if (threadIdx.x == 0) indptr[0] = 0;
+  for (int b0 = 0; b0 < B; b0 += blockDim.x) {
+    const int b = b0 + threadIdx.x;
+    long long n = 0;
+    if (b < B) {
+      const long long S = seq_lens[b];
+      const long long nb = (S + page - 1) / page;
+      last_page_len[b] = static_cast<int>(S - (nb - 1) * page);
+      n = nb < 0 ? 0 : (nb > max_blocks ? max_blocks : nb);
+    }
+    long long total;
+    const long long incl = block_inclusive_scan(n, sh_warp, &total);
+    if (b < B) indptr[b + 1] = static_cast<int>(carry + incl);
+    carry += total;
+  }
+  __syncthreads();
+  for (int b = 0; b < B; ++b) {
+    const int start = indptr[b];
+    const int n = indptr[b + 1] - start;
+    for (int j = threadIdx.x; j < n; j += blockDim.x)
+      indices[start + j] = block_table[static_cast<size_t>(b) * max_blocks + j];
+  }
+}
+
+cudaError_t launch_plan(const ScanParams& p, long long* plan, long long* prefix, int grid,
+                        cudaStream_t s) {
+  gqa_decode_plan_kernel<<<1, 1024, 0, s>>>(p, plan, prefix, grid);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_table_to_csr(const int* block_table, const int* seq_lens, int B,
+                                      int max_blocks, int page_size, int* indptr, int* indices,
+                                      int* last_page_len, cudaStream_t s) {
+  gqa_decode_block_table_to_csr_kernel<<<1, 1024, 0, s>>>(block_table, seq_lens, B, max_blocks,
+                                                          page_size, indptr, indices,
+                                                          last_page_len);
   return cudaGetLastError();
 }
 

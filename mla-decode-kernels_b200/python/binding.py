@@ -127,6 +127,63 @@ def gqa_decode_kvshard(q, k_cache, v_cache, block_table, seq_lens, scale, rank, 
                                    ws, bool(check_blocks))
 
 
+def block_table_to_paged(block_table, seq_lens, page_size):
+    """(kv_indptr [B+1], kv_indices [sum n_b], kv_last_page_len [B]) int32 on
+    block_table's device, from a dense page table: the reference's helper
+    (bench/baselines/flashinfer_adapter.py:33-51) computed by one GPU kernel.
+    Reads kv_indptr[B] back to size kv_indices (one host synchronisation)."""
+    indptr, indices, last = _ext.block_table_to_csr(block_table, seq_lens, int(page_size))
+    n = int(indptr[-1].item())
+    return indptr, indices[:n], last
+
+
+class BatchDecodeWithPagedKVCacheWrapper:
+    """plan() / run() over a CSR page table, shaped like the FlashInfer
+    wrapper the reference benchmarks against (bench/baselines/
+    flashinfer_adapter.py:24-66: NHD caches passed as (k_cache, v_cache),
+    plan() once per batch shape, run() per decode).  plan() runs on the GPU
+    without a host synchronisation; run() only launches, so it can be
+    captured in a CUDA graph and repeated (e.g. once per layer) while the
+    plan's lengths stay valid."""
+
+    def __init__(self, workspace_buffer=None, kv_layout="NHD"):
+        if kv_layout != "NHD":
+            raise ValueError("only the NHD page layout [num_blocks, page, Hkv, 128] is supported")
+        self._user_ws = workspace_buffer
+        self._ws = None
+        self._planned = None
+
+    def plan(self, indptr, indices, last_page_len, num_qo_heads, num_kv_heads, head_dim,
+             page_size, sm_scale=None, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+             num_blocks=0):
+        if head_dim != 128:
+            raise ValueError("head_dim must be 128")
+        if q_data_type != torch.bfloat16 or kv_data_type != torch.bfloat16:
+            raise ValueError("q and kv must be bf16")
+        B = last_page_len.shape[0]
+        nbytes = _ext.workspace_bytes(B, num_qo_heads, num_kv_heads, 0)
+        if self._user_ws is not None:
+            if self._user_ws.numel() * self._user_ws.element_size() < nbytes:
+                raise ValueError(f"workspace_buffer needs {nbytes} bytes")
+            self._ws = self._user_ws
+        else:
+            self._ws = workspace(indptr.device, nbytes)
+        _ext.plan_csr(indptr, indices, last_page_len, int(num_qo_heads), int(num_kv_heads),
+                      int(page_size), int(num_blocks), self._ws)
+        self._planned = (indptr, indices, last_page_len, num_qo_heads, num_kv_heads, page_size,
+                         1.0 / 128 ** 0.5 if sm_scale is None else float(sm_scale))
+
+    def run(self, q, paged_kv_cache, out=None, check_blocks=True):
+        if self._planned is None:
+            raise RuntimeError("plan() must be called before run()")
+        indptr, indices, last, Hq, Hkv, page_size, scale = self._planned
+        k_cache, v_cache = paged_kv_cache
+        if q.shape[1] != Hq or k_cache.shape[2] != Hkv or k_cache.shape[1] != page_size:
+            raise ValueError("q / cache shapes differ from the plan")
+        return _ext.run_csr(q, k_cache, v_cache, indptr, indices, last, scale, self._ws,
+                            bool(check_blocks), out)
+
+
 # Reference registry (binding.py:31) plus the balanced schedule.
 KERNELS = {
     "v0": gqa_decode_v0,

@@ -260,6 +260,152 @@ torch::Tensor merge_states(torch::Tensor m, torch::Tensor l, torch::Tensor acc) 
   return out;
 }
 
+// ---- CSR front end and plan/run ---------------------------------------------
+
+namespace {
+
+void check_i32(const torch::Tensor& t, const torch::Tensor& like, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.device() == like.device(), what, " must be on q's device");
+  TORCH_CHECK(t.scalar_type() == torch::kInt32 && t.is_contiguous(), what,
+              " must be a contiguous int32 tensor");
+}
+
+gqa_decode_pages dense_pages(const torch::Tensor& block_table, const torch::Tensor& seq_lens,
+                             int64_t page_size, int64_t num_blocks) {
+  gqa_decode_pages pg{};
+  pg.block_table = block_table.data_ptr<int>();
+  pg.seq_lens = seq_lens.data_ptr<int>();
+  pg.max_blocks = static_cast<int>(block_table.size(1));
+  pg.block_size = static_cast<int>(page_size);
+  pg.num_blocks = static_cast<int>(num_blocks);
+  return pg;
+}
+
+gqa_decode_pages csr_pages(const torch::Tensor& indptr, const torch::Tensor& indices,
+                           const torch::Tensor& last, int64_t page_size, int64_t num_blocks) {
+  gqa_decode_pages pg{};
+  pg.kv_indptr = indptr.data_ptr<int>();
+  pg.kv_indices = indices.data_ptr<int>();
+  pg.kv_last_page_len = last.data_ptr<int>();
+  pg.block_size = static_cast<int>(page_size);
+  pg.num_blocks = static_cast<int>(num_blocks);
+  return pg;
+}
+
+}  // namespace
+
+// block_table / seq_lens -> (kv_indptr [B+1], kv_indices [B*max_blocks]
+// (the first kv_indptr[B] are valid), kv_last_page_len [B]).
+std::vector<torch::Tensor> block_table_to_csr(torch::Tensor block_table, torch::Tensor seq_lens,
+                                              int64_t page_size) {
+  TORCH_CHECK(block_table.is_cuda() && block_table.scalar_type() == torch::kInt32 &&
+                  block_table.is_contiguous() && block_table.dim() == 2,
+              "block_table must be a contiguous int32 CUDA tensor [B, max_blocks]");
+  check_i32(seq_lens, block_table, "seq_lens");
+  TORCH_CHECK(seq_lens.dim() == 1 && seq_lens.size(0) == block_table.size(0),
+              "seq_lens must be [B]");
+  TORCH_CHECK(page_size >= 1, "page_size must be positive");
+  const c10::cuda::CUDAGuard guard(block_table.device());
+  const int64_t B = block_table.size(0), mb = block_table.size(1);
+  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(block_table.device());
+  auto indptr = torch::empty({B + 1}, i32);
+  auto indices = torch::empty({std::max<int64_t>(1, B * mb)}, i32);
+  auto last = torch::empty({B}, i32);
+  check_launch(gqa_decode_block_table_to_csr(
+                   block_table.data_ptr<int>(), seq_lens.data_ptr<int>(), static_cast<int>(B),
+                   static_cast<int>(std::max<int64_t>(1, mb)), static_cast<int>(page_size),
+                   indptr.data_ptr<int>(), indices.data_ptr<int>(), last.data_ptr<int>(),
+                   at::cuda::getCurrentCUDAStream()),
+               "gqa_decode_block_table_to_csr");
+  return {indptr, indices, last};
+}
+
+void plan_csr(torch::Tensor indptr, torch::Tensor indices, torch::Tensor last, int64_t Hq,
+              int64_t Hkv, int64_t page_size, int64_t num_blocks, torch::Tensor workspace) {
+  check_i32(indptr, workspace, "kv_indptr");
+  check_i32(indices, workspace, "kv_indices");
+  check_i32(last, workspace, "kv_last_page_len");
+  TORCH_CHECK(indptr.dim() == 1 && indptr.size(0) >= 1 && last.size(0) == indptr.size(0) - 1,
+              "kv_indptr must be [B + 1] and kv_last_page_len [B]");
+  const c10::cuda::CUDAGuard guard(workspace.device());
+  const gqa_decode_pages pg = csr_pages(indptr, indices, last, page_size, num_blocks);
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(gqa_decode_plan(&pg, static_cast<int>(last.size(0)), static_cast<int>(Hq),
+                               static_cast<int>(Hkv), workspace.data_ptr(), ws_bytes,
+                               at::cuda::getCurrentCUDAStream()),
+               "gqa_decode_plan");
+}
+
+void plan_dense(torch::Tensor block_table, torch::Tensor seq_lens, int64_t Hq, int64_t Hkv,
+                int64_t page_size, int64_t num_blocks, torch::Tensor workspace) {
+  check_i32(block_table, workspace, "block_table");
+  check_i32(seq_lens, workspace, "seq_lens");
+  TORCH_CHECK(block_table.dim() == 2 && seq_lens.dim() == 1 &&
+                  seq_lens.size(0) == block_table.size(0),
+              "block_table must be [B, max_blocks] and seq_lens [B]");
+  const c10::cuda::CUDAGuard guard(workspace.device());
+  const gqa_decode_pages pg = dense_pages(block_table, seq_lens, page_size, num_blocks);
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(gqa_decode_plan(&pg, static_cast<int>(seq_lens.size(0)), static_cast<int>(Hq),
+                               static_cast<int>(Hkv), workspace.data_ptr(), ws_bytes,
+                               at::cuda::getCurrentCUDAStream()),
+               "gqa_decode_plan");
+}
+
+torch::Tensor run_pages(const gqa_decode_pages& pg, const torch::Tensor& q,
+                        const torch::Tensor& k_cache, const torch::Tensor& v_cache, double scale,
+                        torch::Tensor workspace, c10::optional<torch::Tensor> out_opt) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() &&
+                  q.dim() == 3 && q.size(2) == 128,
+              "q must be a contiguous bf16 CUDA tensor [B, Hq, 128]");
+  TORCH_CHECK(k_cache.sizes() == v_cache.sizes() && k_cache.dim() == 4 && k_cache.size(3) == 128 &&
+                  k_cache.scalar_type() == torch::kBFloat16 &&
+                  v_cache.scalar_type() == torch::kBFloat16 && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous() && k_cache.device() == q.device() &&
+                  v_cache.device() == q.device(),
+              "k_cache/v_cache must be contiguous bf16 [num_blocks, block_size, Hkv, 128] on q's device");
+  TORCH_CHECK(k_cache.size(1) == pg.block_size, "page_size must match k_cache.size(1)");
+  TORCH_CHECK(workspace.is_cuda() && workspace.device() == q.device() && workspace.is_contiguous(),
+              "workspace must be a contiguous CUDA tensor on q's device");
+  const c10::cuda::CUDAGuard guard(q.device());
+  torch::Tensor out = out_opt.has_value() ? *out_opt : torch::empty_like(q);
+  TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == torch::kBFloat16 &&
+                  out.is_contiguous() && out.device() == q.device(),
+              "out must be a contiguous bf16 tensor shaped like q on q's device");
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  check_launch(gqa_decode_run(bf16_ptr(q), bf16_ptr(k_cache), bf16_ptr(v_cache), &pg,
+                              reinterpret_cast<gqa_bf16*>(out.data_ptr()),
+                              static_cast<int>(q.size(0)), static_cast<int>(q.size(1)),
+                              static_cast<int>(k_cache.size(2)), static_cast<float>(scale),
+                              workspace.data_ptr(), ws_bytes, at::cuda::getCurrentCUDAStream()),
+               "gqa_decode_run");
+  return out;
+}
+
+torch::Tensor run_csr(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                      torch::Tensor indptr, torch::Tensor indices, torch::Tensor last,
+                      double scale, torch::Tensor workspace, bool check_blocks,
+                      c10::optional<torch::Tensor> out) {
+  check_i32(indptr, q, "kv_indptr");
+  check_i32(indices, q, "kv_indices");
+  check_i32(last, q, "kv_last_page_len");
+  TORCH_CHECK(indptr.dim() == 1 && indptr.size(0) == q.size(0) + 1 && last.size(0) == q.size(0),
+              "kv_indptr must be [B + 1] and kv_last_page_len [B]");
+  const gqa_decode_pages pg = csr_pages(indptr, indices, last, k_cache.size(1),
+                                        check_blocks ? k_cache.size(0) : 0);
+  return run_pages(pg, q, k_cache, v_cache, scale, workspace, out);
+}
+
+torch::Tensor run_dense(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                        torch::Tensor block_table, torch::Tensor seq_lens, double scale,
+                        torch::Tensor workspace, bool check_blocks,
+                        c10::optional<torch::Tensor> out) {
+  check_inputs(q, k_cache, v_cache, block_table, seq_lens);
+  const gqa_decode_pages pg = dense_pages(block_table, seq_lens, k_cache.size(1),
+                                          check_blocks ? k_cache.size(0) : 0);
+  return run_pages(pg, q, k_cache, v_cache, scale, workspace, out);
+}
+
 int64_t workspace_bytes(int64_t B, int64_t Hq, int64_t Hkv, int64_t num_splits) {
   return static_cast<int64_t>(gqa_decode_workspace_bytes(
       static_cast<int>(B), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(num_splits)));
@@ -298,6 +444,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("epoch"), py::arg("workspace"), py::arg("check_blocks") = true);
   m.def("kvshard_buffer_bytes", &kvshard_buffer_bytes, "exchange buffer bytes per rank");
   m.def("merge_states", &merge_states, "merge per-shard softmax states into bf16 output");
+  m.def("block_table_to_csr", &block_table_to_csr, "dense page table -> CSR (GPU)");
+  m.def("plan_csr", &plan_csr, "balanced-schedule plan for a CSR page table");
+  m.def("plan_dense", &plan_dense, "balanced-schedule plan for a dense page table");
+  m.def("run_csr", &run_csr, "planned decode, CSR page table", py::arg("q"), py::arg("k_cache"),
+        py::arg("v_cache"), py::arg("kv_indptr"), py::arg("kv_indices"),
+        py::arg("kv_last_page_len"), py::arg("scale"), py::arg("workspace"),
+        py::arg("check_blocks") = true, py::arg("out") = py::none());
+  m.def("run_dense", &run_dense, "planned decode, dense page table", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"), py::arg("seq_lens"),
+        py::arg("scale"), py::arg("workspace"), py::arg("check_blocks") = true,
+        py::arg("out") = py::none());
   m.def("workspace_bytes", &workspace_bytes, "workspace bytes for gqa_decode on this device");
   m.def("get_status", &get_status, "device status word", py::arg("clear") = false);
   m.def("pick_splits", &pick_splits, "fixed split count heuristic");

@@ -139,6 +139,23 @@ def nhd_index(p, s, bs, Hkv, h, j):
     return int(lib().oracle_nhd_index(p, s, bs, Hkv, h, j))
 
 
+def block_table_to_paged(block_table, seq_lens, page_size):
+    """CSR form of a dense page table, restating the reference helper
+    (bench/baselines/flashinfer_adapter.py:33-51) in numpy:
+    n_b = ceil(S_b / page), indptr = [0, cumsum(n)], indices = the first n_b
+    ids of each row, last_page_len = S - (n - 1) * page."""
+    bt = np.asarray(block_table.detach().cpu().numpy() if hasattr(block_table, "detach")
+                    else block_table, dtype=np.int64)
+    sl = np.asarray(seq_lens.detach().cpu().numpy() if hasattr(seq_lens, "detach")
+                    else seq_lens, dtype=np.int64)
+    n = (sl + page_size - 1) // page_size
+    indptr = np.zeros(len(sl) + 1, dtype=np.int32)
+    indptr[1:] = np.cumsum(n)
+    indices = np.concatenate([bt[b, :n[b]] for b in range(len(sl))] or [np.zeros(0)])
+    last = (sl - (n - 1) * page_size).astype(np.int32)
+    return indptr, indices.astype(np.int32), last
+
+
 def ref_kernels():
     """The reference's own v1/v2 kernels built for sm_100a (oracle/_ref), or None."""
     if not os.path.exists(REF_LIB):

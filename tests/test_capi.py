@@ -66,6 +66,15 @@ def test_version(lib):
     assert b"sm_100a" in lib.gqa_decode_version()
 
 
+def align256(x):
+    return (x + 255) // 256 * 256
+
+
+def plan_bytes(grid, B):
+    # balanced-schedule plan: 8 header words + 4 per CTA, and the [B + 1] prefix
+    return align256((8 + 4 * grid) * 8) + align256((B + 1) * 8)
+
+
 def plan(lib, B, Hq, Hkv, ns=0, sms=148, per_sm=1):
     p = Plan()
     rc = lib.gqa_decode_query_plan(B, Hq, Hkv, ns, sms, per_sm, ctypes.byref(p))
@@ -83,7 +92,8 @@ def test_plan_rep_shape(lib):
     # counters (32 rows x 8 warps) + m, l, acc for (148 + 32) slots x 32 heads
     slots, qhr = 148 + 32, 32
     counters = 65536 * 4  # fixed counter region shared by every shape
-    expect = counters + 2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4
+    expect = (counters + plan_bytes(148, 32) + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
+              slots * qhr * 128 * 4)
     assert p.workspace_bytes == expect
 
 
@@ -135,6 +145,6 @@ def test_counter_region_grows_for_huge_batches(lib):
     rc, p = plan(lib, 16384, 32, 8)
     slots, qhr = 148 + 16384, 32
     counters = (148 + 2 * 16384) * 8
-    expect = ((counters * 4 + 255) // 256 * 256 + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
-              slots * qhr * 128 * 4)
+    expect = ((counters * 4 + 255) // 256 * 256 + plan_bytes(148, 16384) +
+              2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4)
     assert rc == 0 and p.workspace_bytes == expect

@@ -156,3 +156,13 @@ def test_config_recipes():
     assert cases.kv_bytes([8192] * 32, 8) == 1 << 30
     assert cases.kv_bytes([262144], 8) == 1 << 30
     assert cases.kv_bytes([32768] * 128, 8) == 16 << 30
+
+
+def test_block_table_to_paged_known_answer():
+    # tests/test_flashinfer_baseline.py:20-31 of the reference.
+    bt = np.array([[5, 1, 3], [0, 4, -1]], dtype=np.int32)
+    sl = np.array([37, 22], dtype=np.int32)
+    indptr, indices, last = oracle.block_table_to_paged(bt, sl, page_size=16)
+    assert indptr.tolist() == [0, 3, 5]
+    assert indices.tolist() == [5, 1, 3, 0, 4]
+    assert last.tolist() == [5, 6]
