@@ -345,7 +345,7 @@ constexpr int kMergeBatch = 2;  // parts per batch of acc loads
 // Loads are batched so that the whole merge costs a few L2 round trips:
 // lanes hold one part each for (m, l), and every lane accumulates 4 output
 // dims of all kMergeHeads heads over kMergeBatch parts per batch.
-__device__ __forceinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n, int jj0,
+__device__ __noinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n, int jj0,
                             int cnt, int lane, bool final_, size_t bh0) {
   const int QHR = p.HG * p.G;
   for (int i0 = 0; i0 < cnt; i0 += kMergeHeads) {
@@ -456,13 +456,16 @@ __device__ __forceinline__ void merge_parts(const ScanParams& p, long long first
 // Count one arrival on *ctr; true (on every lane) for the warp whose arrival
 // completes `total`.  That warp also re-arms the counter for the next launch
 // after it has used the data (see callers).
+// Ordering: __syncwarp (bar.warp.sync) orders every lane's partial-state
+// stores before lane 0's release-acquire add; release is cumulative, so the
+// last arriver's acquire sees every earlier warp's states, and the second
+// __syncwarp orders its lanes' reads after that acquire.
 __device__ __forceinline__ bool arrive_last(int* ctr, int total, int lane) {
-  __threadfence();
   __syncwarp();
   int last = 0;
-  if (lane == 0) last = atomicAdd(ctr, 1) == total - 1;
+  if (lane == 0) last = atom_add_acq_rel_gpu(ctr, 1) == total - 1;
   last = __shfl_sync(kFull, last, 0);
-  if (last) __threadfence();
+  __syncwarp();
   return last != 0;
 }
 
