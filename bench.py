@@ -8,6 +8,7 @@ traffic is excluded from the metric, as in the reference.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload rep|wide|ragged|long|long_peaked] [--num-splits auto|N]
+                  [--kernel auto|v0|v1|v2] [--api block_table|csr|csr_replan]
 
 N > 1 runs under torchrun, one rank per GPU.  Workloads (BASELINE.json
 configs; seeded synthetic data, cases.py):
@@ -51,7 +52,14 @@ SCALE = 1.0 / math.sqrt(128)
 # cell_32x8_S8192_B32_bs16.json) = 939.7 GB/s.
 BASELINE_GBS = (1 << 30) / 1.1426e-3 / 1e9
 FALLBACK_HBM_GBS = 6650.0
-PROFILE_SUMMARY = os.path.join(REPO, "profiles", "gqa_decode_scan_kernel_rep.md")
+E2E_PATHS = {
+    "block_table": "binding.gqa_decode -> C ABI gqa_decode_launch; every step q, block_table "
+                   "and seq_lens H2D from pinned host memory and out D2H",
+    "csr": "BatchDecodeWithPagedKVCacheWrapper plan + run -> C ABI gqa_decode_plan / "
+           "gqa_decode_run; every step q, indptr, indices and last_page_len H2D from pinned "
+           "host memory, a fresh plan, and out D2H",
+}
+E2E_PATHS["csr_replan"] = E2E_PATHS["csr"]
 
 
 def parse_args():
@@ -74,6 +82,11 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="long workloads at N > 1: fused peer-memory merge or NCCL all-gather")
+    ap.add_argument("--api", default="block_table", choices=["block_table", "csr", "csr_replan"],
+                    help="batch workloads, --kernel auto: block_table = gqa_decode (one call); "
+                         "csr = BatchDecodeWithPagedKVCacheWrapper.run on a CSR page table "
+                         "planned once (plan amortised over layers); csr_replan = plan + run "
+                         "every step")
     ap.add_argument("--batch", type=int, default=None,
                     help="requests per GPU for rep / wide (smaller cases for profiling)")
     return ap.parse_args()
@@ -98,29 +111,35 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
 
 
-def profiled_traffic(kv_bytes_per_launch):
-    """dram bytes per launch from the committed ncu summary (scaled to this
-    launch's KV bytes if the capture was a smaller case), else None."""
-    try:
-        with open(PROFILE_SUMMARY) as f:
-            text = f.read()
-    except OSError:
+# Archived ncu captures (profiles/<stem>.ncu.txt, written by ncu_report.py)
+# of the dominant kernel of each timed configuration, on a smaller case of
+# the same kernel; DRAM traffic scales with the KV bytes a launch processes.
+CAPTURES = {
+    ("rep", "auto"): ("gqa_decode_scan_kernel", "gqa_decode_scan_kernel_rep_b16"),
+    ("wide", "auto"): ("gqa_decode_scan_kernel", "gqa_decode_scan_kernel_wide_b4"),
+    ("rep", "v0"): ("gqa_decode_simt_kernel", "gqa_decode_simt_kernel_v0_b16"),
+    ("rep", "v1"): ("gqa_decode_scan_kernel", "gqa_decode_scan_kernel_v1_b16"),
+    ("rep", "v2"): ("gqa_decode_scan_kernel", "gqa_decode_scan_kernel_v2_ns8_b16"),
+}
+
+
+def dominant_kernel(args):
+    kernel = "auto" if args.kernel == "auto" else args.kernel
+    name, stem = CAPTURES.get((args.workload, kernel), ("gqa_decode_scan_kernel", None))
+    if kernel == "v2" and args.num_splits not in ("8", "auto"):
+        stem = None  # captured at num_splits=8 only
+    return name, stem
+
+
+def profiled_traffic(stem, kv_bytes_per_launch):
+    """DRAM bytes per launch: the capture's DRAM bytes / algorithmic bytes
+    ratio times this launch's KV bytes, or None without a capture."""
+    if stem is None:
         return None
-    vals = {}
-    for line in text.splitlines():
-        if ":" in line and line.strip().startswith(("traffic_bytes_per_launch", "kv_bytes_per_launch")):
-            k, v = line.split(":", 1)
-            try:
-                vals[k.strip()] = float(v.strip().split()[0])
-            except ValueError:
-                pass
-    if "traffic_bytes_per_launch" not in vals:
-        return None
-    t = vals["traffic_bytes_per_launch"]
-    kv = vals.get("kv_bytes_per_launch")
-    if kv:
-        t = t * kv_bytes_per_launch / kv
-    return int(t)
+    import ncu_report
+
+    r = ncu_report.traffic_ratio(stem)
+    return None if r is None else int(r * kv_bytes_per_launch)
 
 
 class ClockSampler:
@@ -277,14 +296,12 @@ class E2ELoop:
     next step's inputs on one copy stream, D2H of each output on another, the
     decode on the compute stream, ordered by events."""
 
-    def __init__(self, q, bt, sl, out, stream):
+    def __init__(self, inputs, out, stream):
         self.compute = stream
-        self.h2d_stream = torch.cuda.Stream(device=q.device)
-        self.d2h_stream = torch.cuda.Stream(device=q.device)
-        self.host_in = [(q.cpu().pin_memory(), bt.cpu().pin_memory(), sl.cpu().pin_memory())
-                        for _ in range(2)]
-        self.dev_in = [(torch.empty_like(q), torch.empty_like(bt), torch.empty_like(sl))
-                       for _ in range(2)]
+        self.h2d_stream = torch.cuda.Stream(device=out.device)
+        self.d2h_stream = torch.cuda.Stream(device=out.device)
+        self.host_in = [tuple(t.cpu().pin_memory() for t in inputs) for _ in range(2)]
+        self.dev_in = [tuple(torch.empty_like(t) for t in inputs) for _ in range(2)]
         self.dev_out = [torch.empty_like(out) for _ in range(2)]
         self.host_out = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
                          for _ in range(2)]
@@ -438,7 +455,27 @@ def run_ours(args, world, rank, local):
     ns = 0 if args.num_splits == "auto" else int(args.num_splits)
 
     out = torch.empty_like(q)
-    if kind == "batch" and args.kernel != "auto":
+    if args.api != "block_table" and (kind != "batch" or args.kernel != "auto"):
+        raise SystemExit("--api csr / csr_replan needs a batch workload and --kernel auto")
+    if args.api != "block_table":
+        page = k.shape[1]
+        csr = binding.block_table_to_paged(bt, sl, page)
+        wrapper = binding.BatchDecodeWithPagedKVCacheWrapper()
+
+        def plan(indptr, indices, last):
+            wrapper.plan(indptr, indices, last, q.shape[1], k.shape[2], 128, page,
+                         sm_scale=SCALE, num_blocks=k.shape[0])
+        plan(*csr)
+        if args.api == "csr":
+            def step():
+                wrapper.run(q, (k, v), out=out)
+            launches_per_step = 1
+        else:
+            def step():
+                plan(*csr)
+                wrapper.run(q, (k, v), out=out)
+            launches_per_step = 2
+    elif kind == "batch" and args.kernel != "auto":
         if args.kernel == "v2":
             ns2 = 8 if ns == 0 else ns
             fn = lambda *a: binding.gqa_decode_v2(*a, num_splits=ns2)  # noqa: E731
@@ -518,8 +555,12 @@ def run_ours(args, world, rank, local):
     # As in a serving loop, step i+1's inputs are uploaded (copy stream) while
     # step i decodes, and step i's output is downloaded (second copy stream)
     # while step i+1 decodes; buffers are double-buffered.
-    e2e = E2ELoop(q, bt, sl, out, stream)
-    if kind == "batch" and args.kernel != "auto":
+    e2e = E2ELoop((q, *csr) if args.api != "block_table" else (q, bt, sl), out, stream)
+    if args.api != "block_table":
+        def decode(q_d, indptr_d, indices_d, last_d, out_d):
+            plan(indptr_d, indices_d, last_d)
+            wrapper.run(q_d, (k, v), out=out_d)
+    elif kind == "batch" and args.kernel != "auto":
         def decode(q_d, bt_d, sl_d, out_d):
             out_d.copy_(fn(q_d, k, v, bt_d, sl_d, SCALE))
     elif kind == "batch":
@@ -545,6 +586,7 @@ def run_ours(args, world, rank, local):
     if rank != 0:
         return
     peak, peak_src = measured_hbm_peak()
+    kernel_name, capture = dominant_kernel(args)
     achieved = kv_local / (ms * 1e-3) / 1e9  # rank 0's kernel, per launch
     value = kv_total / (ms_max * 1e-3) / 1e9
     line = {
@@ -559,20 +601,20 @@ def run_ours(args, world, rank, local):
                              "1.1426 ms per GiB = 939.7 GB/s",
         "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16 q/K/V, cases.py recipe)",
         "config": dict(cfg, parallelism=f"dp{world}" if kind == "batch" else f"kv{world}",
-                       num_splits=args.num_splits, kernel=args.kernel,
+                       num_splits=args.num_splits, kernel=args.kernel, api=args.api,
                        exchange=args.exchange if kind == "kvrange" else None,
                        l2="inputs > 126 MB L2 (1+ GiB KV per GPU); no flush needed",
                        kv_bytes_per_step=int(kv_total)),
         "e2e": {"value": round(kv_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": int(h2d * world),
                 "d2h_bytes_per_step": int(d2h * world),
-                "path": "binding.gqa_decode -> C ABI gqa_decode_launch; every step q/bt/sl "
-                        "H2D from pinned host memory and out D2H, double-buffered on two copy "
-                        "streams overlapping the previous / next decode"},
+                "path": E2E_PATHS[args.api] + "; double-buffered on two copy streams "
+                        "overlapping the previous / next decode"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": profiled_traffic(kv_local), "peak_source": peak_src,
-                     "kernel": "gqa_decode_scan_kernel",
+                     "traffic": profiled_traffic(capture, kv_local), "peak_source": peak_src,
+                     "traffic_source": f"profiles/{capture}.ncu.txt" if capture else None,
+                     "kernel": kernel_name,
                      "algorithmic_bytes_per_launch": int(kv_local)},
         "gpu_launches": int(args.steps * launches_per_step),
         "gpu_launches_note": f"{launches_per_step} per step in the timed device-resident loop "

@@ -150,6 +150,7 @@ class BatchDecodeWithPagedKVCacheWrapper:
         if kv_layout != "NHD":
             raise ValueError("only the NHD page layout [num_blocks, page, Hkv, 128] is supported")
         self._user_ws = workspace_buffer
+        self._user_ws_zeroed = False
         self._ws = None
         self._planned = None
 
@@ -162,12 +163,20 @@ class BatchDecodeWithPagedKVCacheWrapper:
             raise ValueError("q and kv must be bf16")
         B = last_page_len.shape[0]
         nbytes = _ext.workspace_bytes(B, num_qo_heads, num_kv_heads, 0)
+        # The plan and the arrival counters live in the workspace, so every
+        # wrapper keeps its own: two wrappers planned for different batches
+        # (or run on different streams) never share one.  The counters must
+        # start at zero; each run leaves them at zero again.
         if self._user_ws is not None:
             if self._user_ws.numel() * self._user_ws.element_size() < nbytes:
                 raise ValueError(f"workspace_buffer needs {nbytes} bytes")
+            if not self._user_ws_zeroed:
+                self._user_ws.zero_()
+                self._user_ws_zeroed = True
             self._ws = self._user_ws
-        else:
-            self._ws = workspace(indptr.device, nbytes)
+        elif self._ws is None or self._ws.numel() < nbytes:
+            self._ws = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8,
+                                   device=indptr.device)
         _ext.plan_csr(indptr, indices, last_page_len, int(num_qo_heads), int(num_kv_heads),
                       int(page_size), int(num_blocks), self._ws)
         self._planned = (indptr, indices, last_page_len, num_qo_heads, num_kv_heads, page_size,

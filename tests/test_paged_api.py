@@ -144,3 +144,33 @@ def test_one_plan_many_runs_and_graph_replay():
     torch.cuda.synchronize()
     for lay, o in zip(layers, outs):
         assert torch.equal(o, capi.auto(*lay, SCALE))
+
+
+def test_two_wrappers_keep_their_own_plans():
+    # two batches planned up front, then run alternately: each wrapper's plan
+    # and counters live in its own workspace, so neither clobbers the other
+    a = to_gpu(cases.make_case([700, 5000, 64], 32, 8, 16, seed=61))
+    b = to_gpu(cases.make_case([3000] * 9, 32, 8, 16, seed=62))
+    wa, wb = binding.BatchDecodeWithPagedKVCacheWrapper(), binding.BatchDecodeWithPagedKVCacheWrapper()
+    wa.plan(*csr_of(a), 32, 8, 128, 16, sm_scale=SCALE, num_blocks=a[1].shape[0])
+    wb.plan(*csr_of(b), 32, 8, 128, 16, sm_scale=SCALE, num_blocks=b[1].shape[0])
+    for _ in range(2):
+        out_a = wa.run(a[0], (a[1], a[2]))
+        out_b = wb.run(b[0], (b[1], b[2]))
+    torch.cuda.synchronize()
+    assert capi.status() == 0
+    assert torch.equal(out_a, capi.auto(*a, SCALE))
+    assert torch.equal(out_b, capi.auto(*b, SCALE))
+
+
+def test_wrapper_user_workspace_starts_dirty():
+    # FlashInfer callers hand over an uninitialised byte buffer; the wrapper
+    # zeroes it once before the first plan
+    case = to_gpu(cases.make_case([2500, 17, 9000], 32, 8, 16, seed=63))
+    buf = torch.full((64 << 20,), 0xA5, dtype=torch.uint8, device="cuda")
+    w = binding.BatchDecodeWithPagedKVCacheWrapper(buf)
+    w.plan(*csr_of(case), 32, 8, 128, 16, sm_scale=SCALE, num_blocks=case[1].shape[0])
+    out = w.run(case[0], (case[1], case[2]))
+    torch.cuda.synchronize()
+    assert capi.status() == 0
+    assert torch.equal(out, capi.auto(*case, SCALE))
