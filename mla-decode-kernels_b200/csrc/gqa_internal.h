@@ -82,7 +82,8 @@ struct ScanParams {
   const int* kv_last;
   int csr;
   // Precomputed BALANCED schedule (gqa_decode_plan), or null to compute the
-  // CTA's range in the kernel: [T, W, grid, ...(8)] then per CTA {g0, g1, b0, P0}.
+  // CTA's range in the kernel: [T, E (ranges with work), grid, ...(8)] then per CTA
+  // {g0, g1, b0, P0}.
   const long long* plan;
   __nv_bfloat16* out;            // [B, Hq, 128]; unused with kOutState
   // Split partials.  FIXED: reference layout [B, Hq, num_splits](,128).

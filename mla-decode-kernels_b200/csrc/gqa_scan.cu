@@ -75,11 +75,29 @@ struct Seg {
   long long cfirst;  // BALANCED: index of the first CTA that holds this row
 };
 
+// BALANCED ranges: the T stages of all rows, in row order, are cut into E =
+// min(grid, T / 2) ranges with proportional boundaries [c T / E, (c+1) T / E)
+// - sizes differ by at most one stage, and every range holds at least two
+// stages so that no row is cut into single-stage parts.  CTAs c >= E idle.
+__device__ __forceinline__ long long range_parts(long long T, long long grid) {
+  return max(1LL, min(grid, T / 2));
+}
+
+__device__ __forceinline__ long long range_start(long long c, long long T, long long E) {
+  return c >= E ? T : c * T / E;
+}
+
+// The range that holds stage g (0 <= g < T): the largest c with
+// c T / E <= g, i.e. c T < (g + 1) E.
+__device__ __forceinline__ long long range_owner(long long g, long long T, long long E) {
+  return ((g + 1) * E - 1) / T;
+}
+
 struct SegIter {
   // FIXED
   int task, task_end, task_step;
   // BALANCED
-  long long g, g_end, W, row0;
+  long long g, g_end, T, E, row0;
   int b, hg, S, L;
 };
 
@@ -134,8 +152,8 @@ __device__ __forceinline__ bool iter_next(SegIter& it, const ScanParams& p, long
     s.S = it.S;
     s.s0 = static_cast<int>(it.g - rs);
     s.s1 = static_cast<int>(e - rs);
-    s.cfirst = rs / it.W;
-    s.nparts = static_cast<int>((re - 1) / it.W - s.cfirst + 1);
+    s.cfirst = range_owner(rs, it.T, it.E);
+    s.nparts = static_cast<int>(range_owner(re - 1, it.T, it.E) - s.cfirst + 1);
     s.kind = s.nparts == 1 ? kDirect : kPartial;
     s.slot = static_cast<int>(blockIdx.x) + s.row;
     it.g = e;
@@ -176,17 +194,16 @@ __device__ __forceinline__ void balanced_start(const ScanParams& p, long long ca
   const long long excl = x - local + (warp > 0 ? sh_warp[warp - 1] : 0);
   const long long total = sh_warp[nwarps - 1];
   const long long T = total * p.NHG;
-  const long long grid = gridDim.x;
-  long long W = (T + grid - 1) / grid;
-  if (W < 2) W = 2;  // at least 32 tokens per CTA before a row is cut
-  const long long g0 = min(T, static_cast<long long>(blockIdx.x) * W);
-  const long long g1 = min(T, g0 + W);
+  const long long E = range_parts(T, gridDim.x);
+  const long long g0 = range_start(blockIdx.x, T, E);
+  const long long g1 = range_start(blockIdx.x + 1LL, T, E);
   if (tid == 0) {
     sh_info[0] = g0;
     sh_info[1] = g1;
-    sh_info[2] = W;
+    sh_info[2] = E;
     sh_info[3] = 0;  // first request
     sh_info[4] = 0;  // stages before it
+    sh_info[5] = T;
   }
   __syncthreads();
   if (g0 < g1 && g0 >= excl * p.NHG && g0 < (excl + local) * p.NHG) {
@@ -500,10 +517,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   if (p.schedule == kBalanced && p.plan) {
     if (threadIdx.x < 4) {
       const long long* e = p.plan + kPlanHeader + static_cast<size_t>(blockIdx.x) * kPlanEntry;
-      // entry {g0, g1, b0, P0} -> sh_info {g0, g1, W, b0, P0}
       sh_info[threadIdx.x < 2 ? threadIdx.x : threadIdx.x + 1] = e[threadIdx.x];
     } else if (threadIdx.x == 4) {
       sh_info[2] = p.plan[1];
+    } else if (threadIdx.x == 5) {
+      sh_info[5] = p.plan[0];
     }
     __syncthreads();
   } else if (p.schedule == kBalanced) {
@@ -520,7 +538,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   } else {
     it.g = sh_info[0];
     it.g_end = sh_info[1];
-    it.W = sh_info[2];
+    it.E = sh_info[2];
+    it.T = sh_info[5];
     it.b = static_cast<int>(sh_info[3]);
     it.row0 = sh_info[4] * p.NHG;
     it.hg = 0;
@@ -1031,16 +1050,15 @@ __global__ void __launch_bounds__(1024)
   }
   __syncthreads();
   const long long T = carry * p.NHG;
-  long long W = (T + grid - 1) / grid;
-  if (W < 2) W = 2;
+  const long long E = range_parts(T, grid);
   if (threadIdx.x == 0) {
     plan[0] = T;
-    plan[1] = W;
+    plan[1] = E;
     plan[2] = grid;
   }
   for (int c = threadIdx.x; c < grid; c += blockDim.x) {
-    const long long g0 = min(T, static_cast<long long>(c) * W);
-    const long long g1 = min(T, g0 + W);
+    const long long g0 = range_start(c, T, E);
+    const long long g1 = range_start(c + 1LL, T, E);
     int b0 = 0;
     if (g0 < g1) {
       // last request whose stages start at or before g0 (an empty request

@@ -182,3 +182,75 @@ def config5(device="cuda", seed=5, S=262144, k_scale=1.0):
     k_scale=8 gives the peaked-softmax variant."""
     return make_case([S], 32, 8, 64, seed=seed, pool_factor=1.0, k_scale=k_scale,
                      device=device)
+
+
+# ---- MLA latent-cache cases (K2) -------------------------------------------
+#
+# Same recipe on FlashMLA's layouts: q [B, s_q, h_q, 576], one latent kv head
+# kv_cache [pool, page, 1, 576] (K = all 576 dims, V = the first 512), pages
+# of 64 tokens, a permuted page table and NaN-poisoned unused slots.
+
+MLA_D, MLA_DV = 576, 512
+
+
+def make_mla_case(seq_lens, s_q, h_q, page=64, *, seed=0, pool_factor=2.0, poison=True,
+                  value_scale=1.0, device="cpu", gen=None):
+    seq_lens = [int(s) for s in seq_lens]
+    B = len(seq_lens)
+    device = torch.device(device)
+    if gen is None:
+        gen = torch.Generator(device=device).manual_seed(seed)
+    n_blocks = [(s + page - 1) // page for s in seq_lens]
+    need = sum(n_blocks)
+    pool = max(need, int(math.ceil(need * pool_factor)), 1)
+    max_blocks = max(1, max(n_blocks) if n_blocks else 1)
+    q = _randn_bf16((B, s_q, h_q, MLA_D), gen, value_scale, device)
+    kv = _randn_bf16((pool, page, 1, MLA_D), gen, value_scale, device)
+    perm = torch.randperm(pool, generator=gen, device=device).to(torch.int32)
+    block_table = torch.full((B, max_blocks), -1, dtype=torch.int32, device=device)
+    off = 0
+    for b, n in enumerate(n_blocks):
+        block_table[b, :n] = perm[off:off + n]
+        off += n
+    if poison:
+        unused = perm[need:].long()
+        if unused.numel():
+            kv[unused] = float("nan")
+        for b, s in enumerate(seq_lens):
+            rem = s % page
+            if s > 0 and rem:
+                kv[int(block_table[b, n_blocks[b] - 1]), rem:] = float("nan")
+    return q, kv, block_table, torch.tensor(seq_lens, dtype=torch.int32, device=device)
+
+
+def mla_subset(case, requests):
+    """CPU copy of some requests of an MLA case with a compact page pool."""
+    q, kv, block_table, seq_lens = case
+    idx = torch.as_tensor(list(requests), dtype=torch.long, device=q.device)
+    sl = seq_lens[idx].to("cpu")
+    page = kv.shape[1]
+    n_blocks = [(int(s) + page - 1) // page for s in sl]
+    max_blocks = max(1, max(n_blocks))
+    bt = block_table[idx][:, :max_blocks].to("cpu")
+    blocks = torch.cat([bt[i, :n] for i, n in enumerate(n_blocks)]).long()
+    kv_small = kv[blocks.to(kv.device)].to("cpu")
+    bt_new = torch.full((len(n_blocks), max_blocks), -1, dtype=torch.int32)
+    off = 0
+    for i, n in enumerate(n_blocks):
+        bt_new[i, :n] = torch.arange(off, off + n, dtype=torch.int32)
+        off += n
+    return q[idx].to("cpu"), kv_small, bt_new, sl
+
+
+def mla_kv_bytes(seq_lens):
+    """Latent-cache bytes one decode step reads: sum_b S_b * 576 * 2 B (FlashMLA's
+    byte count without q and out, tests/test_flash_mla_dense_decoding.py:177-190
+    as quoted in docs/k1/notes_w1.md:107-113)."""
+    total = int(torch.as_tensor(seq_lens, dtype=torch.int64).clamp_min(0).sum())
+    return total * MLA_D * 2
+
+
+def mla_flops(seq_lens, s_q, h_q, causal=False):
+    """FlashMLA's FLOP count: per query row 2 * S * (576 + 512) (no causal discount)."""
+    total = int(torch.as_tensor(seq_lens, dtype=torch.int64).clamp_min(0).sum())
+    return total * s_q * h_q * 2 * (MLA_D + MLA_DV)

@@ -233,3 +233,82 @@ void oracle_merge_states(const float* m, const float* l, const float* acc, int n
   *m_out = M;
   *l_out = L;
 }
+
+/* ---- MLA absorbed-path decode (latent cache) -------------------------------
+ *
+ * The reference's roadmap kernel K2 (README.md "Roadmap": latent cache
+ * [num_blocks, 64, 576], baseline FlashMLA) has no code in the reference
+ * (kernels/mla_decode/ is empty), so this restates the operator FlashMLA's
+ * tests check (flash_mla_with_kvcache against scaled dot-product attention on
+ * the gathered cache; docs/k1/notes_w1.md:97-121 quotes its accounting):
+ *   q [B, s_q, h_q, 576], one latent kv head: K = cache[t, 0:576],
+ *   V = cache[t, 0:512];  for query position i, head h:
+ *   scores_t = scale * q[b, i, h, :] . K_t over t < S_b
+ *              (causal, s_q > 1: t < S_b - s_q + 1 + i),
+ *   out[b, i, h, :] = softmax(scores) @ V,  lse[b, h, i] = ln sum_t exp(scores_t);
+ * a query with no visible token gets out = 0 and lse = -inf.
+ * Parity is unpinned against the reference (it has no implementation); the
+ * tests cross-check this restatement against torch's fp32 SDPA. */
+
+#define MLA_D 576
+#define MLA_DV 512
+
+typedef struct {
+  const uint16_t *q, *kv;
+  const int32_t *bt, *sl;
+  int B, s_q, h_q, page, max_blocks, causal;
+  float scale;
+  float *out, *lse;
+} mla_ctx_t;
+
+static void mla_ref_task(void* vctx, int64_t row) {
+  const mla_ctx_t* c = (const mla_ctx_t*)vctx;
+  const int h = (int)(row % c->h_q);
+  const int i = (int)((row / c->h_q) % c->s_q);
+  const int b = (int)(row / ((int64_t)c->h_q * c->s_q));
+  const int S = c->sl[b];
+  int vis = c->causal ? S - c->s_q + 1 + i : S;
+  if (vis > S) vis = S;
+  if (vis < 0) vis = 0;
+  float* o = c->out + row * MLA_DV;
+  float* lse = c->lse + ((int64_t)b * c->h_q + h) * c->s_q + i;
+  memset(o, 0, sizeof(float) * MLA_DV);
+  if (vis == 0) {
+    *lse = -INFINITY;
+    return;
+  }
+  float qf[MLA_D];
+  const uint16_t* qrow = c->q + row * MLA_D;
+  for (int d = 0; d < MLA_D; ++d) qf[d] = bf16_to_f32(qrow[d]);
+  float* sc = (float*)malloc(sizeof(float) * (size_t)vis);
+  float mx = -INFINITY;
+  for (int t = 0; t < vis; ++t) {
+    const int p = c->bt[(int64_t)b * c->max_blocks + t / c->page];
+    const uint16_t* krow = c->kv + ((int64_t)p * c->page + t % c->page) * MLA_D;
+    float acc = 0.f;
+    for (int d = 0; d < MLA_D; ++d) acc += bf16_to_f32(krow[d]) * qf[d];
+    sc[t] = acc * c->scale;
+    if (sc[t] > mx) mx = sc[t];
+  }
+  double sum = 0.0;
+  for (int t = 0; t < vis; ++t) {
+    sc[t] = expf(sc[t] - mx);
+    sum += sc[t];
+  }
+  for (int t = 0; t < vis; ++t) {
+    const int p = c->bt[(int64_t)b * c->max_blocks + t / c->page];
+    const uint16_t* vrow = c->kv + ((int64_t)p * c->page + t % c->page) * MLA_D;
+    const float w = (float)(sc[t] / sum);
+    for (int d = 0; d < MLA_DV; ++d) o[d] += w * bf16_to_f32(vrow[d]);
+  }
+  *lse = (float)(log(sum) + mx);
+  free(sc);
+}
+
+void oracle_mla_ref(const uint16_t* q, const uint16_t* kv, const int32_t* block_table,
+                    const int32_t* seq_lens, int B, int s_q, int h_q, int page, int max_blocks,
+                    float scale, int causal, float* out, float* lse, int nthreads) {
+  mla_ctx_t c = {q, kv, block_table, seq_lens, B, s_q, h_q, page, max_blocks, causal, scale,
+                 out, lse};
+  parallel_for((int64_t)B * s_q * h_q, nthreads, mla_ref_task, &c);
+}

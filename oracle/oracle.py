@@ -60,6 +60,8 @@ def lib():
         i64 = ctypes.c_int64
         L.oracle_nhd_index.argtypes = [i64, i64, i64, i64, i64, i64]
         L.oracle_nhd_index.restype = i64
+        L.oracle_mla_ref.argtypes = [p, p, p, p, i, i, i, i, i, f, i, p, p, i]
+        L.oracle_mla_ref.restype = None
         _lib = L
     return _lib
 
@@ -110,6 +112,23 @@ def attention_state(q, k_cache, v_cache, block_table, seq_lens, scale, nthreads=
                                  bs, bt.shape[1], float(scale), _ptr(m), _ptr(l), _ptr(acc),
                                  nthreads or default_threads())
     return torch.from_numpy(m), torch.from_numpy(l), torch.from_numpy(acc)
+
+
+def mla_ref(q, kv_cache, block_table, seq_lens, scale, causal=False, nthreads=None):
+    """MLA absorbed-path decode on a latent cache (gqa_oracle.c: oracle_mla_ref):
+    q [B, s_q, h_q, 576] bf16, kv_cache [num_blocks, page, 1, 576] bf16 ->
+    out [B, s_q, h_q, 512] fp32, lse [B, h_q, s_q] fp32 (natural log)."""
+    B, s_q, h_q, D = q.shape
+    assert D == 576 and kv_cache.shape[-1] == 576 and kv_cache.shape[2] == 1
+    page = kv_cache.shape[1]
+    qb, kb = _bits(q), _bits(kv_cache)
+    bt, sl = _i32(block_table), _i32(seq_lens)
+    out = np.empty((B, s_q, h_q, 512), dtype=np.float32)
+    lse = np.empty((B, h_q, s_q), dtype=np.float32)
+    lib().oracle_mla_ref(_ptr(qb), _ptr(kb), _ptr(bt), _ptr(sl), B, s_q, h_q, page, bt.shape[1],
+                         float(scale), int(bool(causal)), _ptr(out), _ptr(lse),
+                         nthreads or default_threads())
+    return torch.from_numpy(out), torch.from_numpy(lse)
 
 
 def online_softmax(scores, values):

@@ -166,3 +166,35 @@ def test_block_table_to_paged_known_answer():
     assert indptr.tolist() == [0, 3, 5]
     assert indices.tolist() == [5, 1, 3, 0, 4]
     assert last.tolist() == [5, 6]
+
+
+@pytest.mark.parametrize("S,s_q,h_q,causal", [([1, 70, 200], 1, 16, False),
+                                              ([130, 64], 2, 16, True),
+                                              ([257], 1, 128, False),
+                                              ([5, 300], 2, 32, False)])
+def test_mla_oracle_matches_sdpa(S, s_q, h_q, causal):
+    # the MLA restatement against torch's fp32 SDPA on the gathered latent cache
+    q, kv, bt, sl = cases.make_mla_case(S, s_q, h_q, seed=4, poison=True)
+    scale = 1.0 / math.sqrt(192)
+    out, lse = oracle.mla_ref(q, kv, bt, sl, scale, causal=causal)
+    page = kv.shape[1]
+    for b, Sb in enumerate(S):
+        n = (Sb + page - 1) // page
+        K = kv.float()[bt[b, :n].long()].reshape(-1, 576)[:Sb]
+        qb = q[b].float()  # [s_q, h_q, 576]
+        sc = torch.einsum("ihd,td->iht", qb, K) * scale
+        if causal:
+            t = torch.arange(Sb)
+            mask = t[None, :] < (Sb - s_q + 1 + torch.arange(s_q))[:, None]
+            sc = sc.masked_fill(~mask[:, None, :], float("-inf"))
+        ref = torch.softmax(sc, dim=-1) @ K[:, :512]
+        np.testing.assert_allclose(out[b].numpy(), ref.numpy(), atol=2e-5, rtol=1e-4)
+        ref_lse = torch.logsumexp(sc, dim=-1).transpose(0, 1)  # [h_q, s_q]
+        np.testing.assert_allclose(lse[b].numpy(), ref_lse.numpy(), atol=1e-4, rtol=1e-5)
+
+
+def test_mla_oracle_empty_request():
+    q, kv, bt, sl = cases.make_mla_case([0, 10], 1, 16, seed=5)
+    out, lse = oracle.mla_ref(q, kv, bt, sl, 0.07)
+    assert torch.all(out[0] == 0) and torch.all(torch.isinf(lse[0])) and torch.all(lse[0] < 0)
+    assert torch.isfinite(out[1]).all()
