@@ -1,0 +1,59 @@
+/*
+ * MLA absorbed-path paged decode (latent cache) on B200, C ABI.
+ *
+ * The reference's roadmap kernel K2 (README.md "Roadmap": latent cache
+ * [num_blocks, 64, 576], baseline FlashMLA) has no code in the reference —
+ * kernels/mla_decode/ is empty — so there is no reference interface to
+ * replace.  The operator and argument meanings follow FlashMLA's
+ * flash_mla_with_kvcache, the baseline the reference names:
+ *   q          [B, s_q, h_q, 576] bf16 (absorbed nope part 512 + rope 64)
+ *   kv_cache   [num_blocks, 64, 1, 576] bf16 (one latent kv head; V = dims 0..511)
+ *   block_table[B, max_blocks] int32, seq_lens [B] int32
+ *   out        [B, s_q, h_q, 512] bf16
+ *   lse        [B, h_q, s_q] fp32 natural-log softmax normaliser
+ *              (-inf for a query row that sees no token; out is 0 there)
+ * causal != 0 with s_q > 1: query position i sees tokens t < S - s_q + 1 + i.
+ * All pointers are device pointers; every entry point is asynchronous on
+ * `stream` and allocates nothing.
+ */
+#ifndef MLA_DECODE_B200_H
+#define MLA_DECODE_B200_H
+
+#include <stddef.h>
+#include <cuda_runtime.h>
+
+#include "gqa_decode.h" /* gqa_bf16 */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Split count for B requests of up to max_pages 64-token pages on num_sms
+ * SMs: enough (request, query-row group, page range) CTAs to fill the GPU,
+ * at least two pages per split, at most 64. */
+int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms);
+
+/* Workspace bytes for num_splits > 1 (unnormalised partial states); 0 for
+ * num_splits == 1. */
+size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits);
+
+/* Decode.  Requirements: page_size == 64; s_q * h_q a multiple of 16; with
+ * causal and s_q > 1, h_q a multiple of 16; 1 <= num_splits <= 64; q and
+ * kv_cache 16-byte aligned; a 16-byte aligned workspace of
+ * mla_decode_workspace_bytes() when num_splits > 1.  Block ids outside
+ * [0, num_blocks) set bit 1 of mla_decode_get_status and read block 0. */
+cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const int* block_table,
+                              const int* seq_lens, gqa_bf16* out, float* lse, int B, int s_q,
+                              int h_q, int page_size, int max_blocks, int num_blocks,
+                              float softmax_scale, int causal, int num_splits, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream);
+
+/* Device status word of the MLA kernels (bit 0: a bounded wait gave up,
+ * bit 1: block id out of range); reset clears it.  Synchronises the device. */
+int mla_decode_get_status(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLA_DECODE_B200_H */

@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "gqa_decode.h"
+#include "mla_decode.h"
 
 namespace {
 
@@ -422,7 +423,82 @@ int64_t pick_splits(int64_t B, int64_t Hq, int64_t Hkv, int64_t seq_len, int64_t
                                 static_cast<int>(seq_len), static_cast<int>(num_sms));
 }
 
+// ---- MLA latent-cache decode (include/mla_decode.h) ------------------------
+
+// q [B, s_q, h_q, 576] bf16, kv_cache [num_blocks, 64, 1, 576] bf16 ->
+// (out [B, s_q, h_q, 512] bf16, lse [B, h_q, s_q] fp32).
+std::vector<torch::Tensor> mla_decode(torch::Tensor q, torch::Tensor kv_cache,
+                                      torch::Tensor block_table, torch::Tensor seq_lens,
+                                      double softmax_scale, bool causal, int64_t num_splits,
+                                      torch::Tensor workspace) {
+  // (block ids are always range-checked: the TMA tensor map spans exactly
+  // kv_cache's num_blocks pages)
+  TORCH_CHECK(q.is_cuda() && kv_cache.is_cuda() && block_table.is_cuda() && seq_lens.is_cuda(),
+              "all tensors must be CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && kv_cache.scalar_type() == torch::kBFloat16,
+              "q and kv_cache must be bf16");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
+              "block_table and seq_lens must be int32");
+  TORCH_CHECK(q.is_contiguous() && kv_cache.is_contiguous() && block_table.is_contiguous() &&
+                  seq_lens.is_contiguous(),
+              "all tensors must be contiguous");
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 576, "q must be [B, s_q, h_q, 576]");
+  TORCH_CHECK(kv_cache.dim() == 4 && kv_cache.size(2) == 1 && kv_cache.size(3) == 576,
+              "kv_cache must be [num_blocks, page, 1, 576]");
+  TORCH_CHECK(kv_cache.size(1) == 64, "page size must be 64");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == q.size(0) &&
+                  seq_lens.dim() == 1 && seq_lens.size(0) == q.size(0),
+              "block_table [B, max_blocks] and seq_lens [B] must match q's batch");
+  TORCH_CHECK(kv_cache.device() == q.device() && block_table.device() == q.device() &&
+                  seq_lens.device() == q.device(),
+              "all tensors must be on the same device");
+  TORCH_CHECK((q.size(1) * q.size(2)) % 16 == 0, "s_q * h_q must be a multiple of 16");
+  TORCH_CHECK(num_splits >= 1 && num_splits <= 64, "num_splits must be in [1, 64]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int64_t B = q.size(0), s_q = q.size(1), h_q = q.size(2);
+  auto out = torch::empty({B, s_q, h_q, 512}, q.options());
+  auto lse = torch::empty({B, h_q, s_q}, q.options().dtype(torch::kFloat32));
+  const size_t need = mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
+                                                 static_cast<int>(h_q), static_cast<int>(num_splits));
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  TORCH_CHECK(need == 0 || (workspace.is_cuda() && workspace.device() == q.device() &&
+                            workspace.is_contiguous() && ws_bytes >= need),
+              "workspace must be a contiguous CUDA tensor of at least ", need, " bytes");
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  check_launch(mla_decode_launch(reinterpret_cast<const gqa_bf16*>(q.data_ptr()),
+                                 reinterpret_cast<const gqa_bf16*>(kv_cache.data_ptr()),
+                                 block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),
+                                 reinterpret_cast<gqa_bf16*>(out.data_ptr()), lse.data_ptr<float>(),
+                                 static_cast<int>(B), static_cast<int>(s_q), static_cast<int>(h_q),
+                                 64, static_cast<int>(block_table.size(1)),
+                                 static_cast<int>(kv_cache.size(0)),
+                                 static_cast<float>(softmax_scale), causal ? 1 : 0,
+                                 static_cast<int>(num_splits), need ? workspace.data_ptr() : nullptr,
+                                 ws_bytes, stream),
+               "mla_decode");
+  return {out, lse};
+}
+
+int64_t mla_workspace_bytes(int64_t B, int64_t s_q, int64_t h_q, int64_t num_splits) {
+  return static_cast<int64_t>(mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
+                                                         static_cast<int>(h_q),
+                                                         static_cast<int>(num_splits)));
+}
+
+int64_t mla_pick_splits(int64_t B, int64_t s_q, int64_t h_q, int64_t max_pages, int64_t num_sms) {
+  return mla_decode_pick_splits(static_cast<int>(B), static_cast<int>(s_q), static_cast<int>(h_q),
+                                static_cast<int>(max_pages), static_cast<int>(num_sms));
+}
+
+int64_t mla_get_status(bool clear) { return mla_decode_get_status(clear ? 1 : 0); }
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("mla_decode", &mla_decode, "MLA latent-cache paged decode (tcgen05)", py::arg("q"),
+        py::arg("kv_cache"), py::arg("block_table"), py::arg("seq_lens"),
+        py::arg("softmax_scale"), py::arg("causal"), py::arg("num_splits"), py::arg("workspace"));
+  m.def("mla_workspace_bytes", &mla_workspace_bytes, "MLA split workspace bytes");
+  m.def("mla_pick_splits", &mla_pick_splits, "MLA split count heuristic");
+  m.def("mla_get_status", &mla_get_status, "MLA device status word", py::arg("clear") = false);
   m.def("gqa_decode_v0", &gqa_decode_v0, "GQA decode v0: CUDA-core grouped scan (paged KV, bf16)");
   m.def("gqa_decode_v1", &gqa_decode_v1,
         "GQA decode v1: pipelined TMA + tensor-core scan, unsplit (paged KV, bf16)");

@@ -2,6 +2,7 @@
 host-only planning functions behave.  No call here touches a GPU."""
 
 import ctypes
+import glob
 import os
 import re
 
@@ -34,10 +35,13 @@ def lib():
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    names = re.findall(r"^\s*(?:const\s+)?[\w]+\s*\*?\s+(gqa_decode_\w+)\s*\(", text, flags=re.M)
-    return sorted(set(names))
+    """Every function declared in include/*.h (gqa_decode_* and mla_decode_*)."""
+    names = set()
+    for h in sorted(glob.glob(os.path.join(REPO, "include", "*.h"))):
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names.update(re.findall(r"^\s*(?:const\s+)?[\w]+\s*\*?\s+((?:gqa|mla)_decode_\w+)\s*\(",
+                                text, flags=re.M))
+    return sorted(names)
 
 
 def test_header_declares_reference_launchers():
@@ -49,7 +53,7 @@ def test_header_declares_reference_launchers():
 
 @pytest.mark.parametrize("name", declared_functions())
 def test_symbol_exported(lib, name):
-    assert hasattr(lib, name), f"{name} declared in include/gqa_decode.h but not exported"
+    assert hasattr(lib, name), f"{name} declared in include/*.h but not exported"
 
 
 def test_symbols_are_c_linkage():
