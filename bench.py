@@ -69,7 +69,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="rep",
-                    choices=["rep", "wide", "ragged", "long", "long_peaked"])
+                    choices=["rep", "wide", "ragged", "long", "long_peaked", "mla"])
+    ap.add_argument("--mla-sq", type=int, default=1, help="mla: query tokens per request")
+    ap.add_argument("--mla-hq", type=int, default=128, help="mla: query heads")
+    ap.add_argument("--mla-sk", type=int, default=8192, help="mla: mean cached tokens")
+    ap.add_argument("--mla-causal", action="store_true")
     ap.add_argument("--num-splits", default="auto",
                     help="auto = balanced schedule; an integer = fixed splits (v2)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "v0", "v1", "v2"],
@@ -628,6 +632,139 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def mla_seq_lens(B, mean, s_q, seed=0):
+    """Ragged cache lengths ~ Normal(mean, mean / 2), at least s_q (the
+    distribution of FlashMLA's varlen performance grid, which the reference's
+    docs/g0/flashmla_bench_raw.txt logs at b = 128)."""
+    g = torch.Generator().manual_seed(seed)
+    s = torch.normal(float(mean), float(mean) / 2, (B,), generator=g)
+    return s.round().clamp(min=s_q).to(torch.int64).tolist()
+
+
+def run_mla(args, world, rank, local):
+    """MLA latent-cache decode (K2) on the FlashMLA performance grid shape:
+    b = 128 requests per GPU, h_q heads, s_q query tokens, 64-token pages."""
+    import cases
+    import mla_decode
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import sharding
+
+        sharding.init_process_group("nccl", timeout_s=120)
+    B = args.batch or 128
+    s_q, h_q = args.mla_sq, args.mla_hq
+    sl = mla_seq_lens(B, args.mla_sk, s_q, seed=rank)
+    case = cases.make_mla_case(sl, s_q, h_q, seed=10 + rank, pool_factor=1.0, poison=False,
+                               device=device)
+    q, kv, bt, sl_t = case
+    scale = 1.0 / math.sqrt(192)
+    ns = int(mla_decode._ext.mla_pick_splits(B, s_q, h_q, bt.shape[1],
+                                            torch.cuda.get_device_properties(device)
+                                            .multi_processor_count))
+    holder = {}
+
+    def step():
+        holder["o"] = mla_decode.mla_decode(q, kv, bt, sl_t, scale, causal=args.mla_causal,
+                                            num_splits=ns)
+
+    step()
+    torch.cuda.synchronize()
+    import oracle
+
+    reqs = [0, 1]
+    ro, rl = oracle.mla_ref(*cases.mla_subset(case, reqs), scale, causal=args.mla_causal)
+    out = holder["o"][0][reqs].float().cpu()
+    if not torch.allclose(out, ro, atol=1e-2, rtol=1e-2):
+        raise SystemExit(f"mla spot check failed: {(out - ro).abs().max().item():.3e}")
+    if mla_decode.get_status(True):
+        raise SystemExit("mla device status set")
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    uuids = [str(torch.cuda.get_device_properties(device).uuid)]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, uuids[0])
+        uuids = gathered
+    sampler = ClockSampler(uuids) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_loop(step, args.steps, world, stream)
+    clocks = sampler.stop() if sampler else None
+    ms_max = max_over_ranks(ms, world, device)
+    median_us = max_over_ranks(per_step_median_us(step, min(args.steps, 200), stream), world,
+                               device)
+    kv_local = cases.mla_kv_bytes(sl)
+    fl_local = cases.mla_flops(sl, s_q, h_q)
+    kv_total = sum_over_ranks(kv_local, world, device)
+    fl_total = sum_over_ranks(fl_local, world, device)
+
+    # e2e: q and the page table up, out and lse back, every step
+    out_buf = torch.empty((B, s_q, h_q, 512), dtype=torch.bfloat16, device=device)
+    e2e = E2ELoop((q, bt, sl_t), out_buf, stream)
+
+    def decode(q_d, bt_d, sl_d, out_d):
+        o, _ = mla_decode.mla_decode(q_d, kv, bt_d, sl_d, scale, causal=args.mla_causal,
+                                     num_splits=ns)
+        out_d.copy_(o)
+    for _ in range(3):
+        e2e.step(decode)
+    e2e.drain()
+    ms_e2e = max_over_ranks(time_loop(lambda: e2e.step(decode), args.steps, world, stream,
+                                      finish=e2e.drain), world, device)
+    if mla_decode.get_status(True):
+        raise SystemExit("mla device status set after timing")
+    if rank != 0:
+        return
+    peak, peak_src = measured_hbm_peak()
+    tc_peak = 1694.0
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            tc_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    achieved = kv_local / (ms * 1e-3) / 1e9
+    tflops = fl_local / (ms * 1e-3) / 1e12
+    value = kv_total / (ms_max * 1e-3) / 1e9
+    line = {
+        "metric": "MLA decode: latent-cache GB/s and TFLOP/s (FlashMLA accounting)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
+        "median_us_per_step": round(median_us, 2),
+        "pct_of_sol": round(100.0 * value / (peak * world), 2),
+        "tflops": round(fl_total / (ms_max * 1e-3) / 1e12, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "vs_baseline_basis": "FlashMLA on H100 at this grid point: docs/g0/flashmla_bench_raw.txt",
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16, cases.make_mla_case)",
+        "config": {"workload": f"mla_b{B}_sq{s_q}_hq{h_q}_sk{args.mla_sk}", "B": B,
+                   "s_q": s_q, "h_q": h_q, "mean_seq_len": args.mla_sk,
+                   "seq_lens": "Normal(mean, mean/2) >= s_q, seeded", "page": 64,
+                   "causal": args.mla_causal, "num_splits": ns, "kernel": "mla",
+                   "parallelism": f"dp{world}", "kv_bytes_per_step": int(kv_total),
+                   "flops_per_step": int(fl_total),
+                   "l2": "inputs > 126 MB L2; no flush needed"},
+        "e2e": {"value": round(kv_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(ms_e2e, 5),
+                "h2d_bytes_per_step": int(e2e.h2d_bytes * world),
+                "d2h_bytes_per_step": int(e2e.d2h_bytes * world),
+                "path": "mla_decode.mla_decode -> C ABI mla_decode_launch; q, block_table and "
+                        "seq_lens H2D, out D2H every step, double-buffered"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": peak_src, "kernel": "mla_decode_kernel",
+                     "algorithmic_bytes_per_launch": int(kv_local),
+                     "tensor_achieved_tflops": round(tflops, 1), "tensor_peak_tflops": tc_peak,
+                     "tensor_frac": round(tflops / tc_peak, 4)},
+        "gpu_launches": int(args.steps * (1 if ns == 1 else 2)),
+        "clocks": clocks, "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_env()
@@ -637,6 +774,9 @@ def main():
         run_reference(args, world, rank)
         return
     try:
+        if args.workload == "mla":
+            run_mla(args, world, rank, local)
+            return
         run_ours(args, world, rank, local)
     finally:
         if world > 1 and dist.is_initialized():

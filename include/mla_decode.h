@@ -37,8 +37,7 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms);
  * num_splits == 1. */
 size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits);
 
-/* Decode.  Requirements: page_size == 64; s_q * h_q a multiple of 16; with
- * causal and s_q > 1, h_q a multiple of 16; 1 <= num_splits <= 64; q and
+/* Decode.  Requirements: page_size == 64; 1 <= num_splits <= 64; q and
  * kv_cache 16-byte aligned; a 16-byte aligned workspace of
  * mla_decode_workspace_bytes() when num_splits > 1.  Block ids outside
  * [0, num_blocks) set bit 1 of mla_decode_get_status and read block 0. */

@@ -98,6 +98,9 @@ __device__ __forceinline__ int visible(const Params& p, int S, int row) {
 template <int NH>
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_constant__ Params p) {
   static_assert(NH == 16 || NH == 32 || NH == 64, "query rows per CTA");
+  // P^T buffers: two (softmax of tile t+1 overlaps PV of tile t) where shared
+  // memory allows, one at NH = 64
+  constexpr int NP = NH == 64 ? 1 : 2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment of every swizzle atom
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -107,17 +110,18 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
   const uint32_t sRing = s_base + p.smem_ring;
   const uint32_t sP = s_base + p.smem_p;
   unsigned char* small = smem + p.smem_small;
-  // small region: 12 mbarriers, TMEM base, votes [2][4], red [4][64],
-  // m_ref [64], alpha [64]
+  // small region: 14 mbarriers, TMEM base, votes [2][4], red [4][64],
+  // m_ref [64], alpha [64], visible tokens per query row [64]
   const uint32_t bars = s_base + p.smem_small;
   const uint32_t bar_q = bars + 0, bar_full = bars + 8, bar_empty = bars + 24,
                  bar_sfull = bars + 40, bar_sfree = bars + 56, bar_pfull = bars + 72,
-                 bar_pv = bars + 80, bar_fin = bars + 88;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + 96);
-  int* vote = reinterpret_cast<int*>(small + 112);              // [2][4]
-  float* red = reinterpret_cast<float*>(small + 160);           // [4][64]
-  float* mref = reinterpret_cast<float*>(small + 160 + 1024);   // [64]
+                 bar_pv = bars + 88, bar_fin = bars + 104;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + 112);
+  int* vote = reinterpret_cast<int*>(small + 128);                // [2][4]
+  float* red = reinterpret_cast<float*>(small + 160);             // [4][64]
+  float* mref = reinterpret_cast<float*>(small + 160 + 1024);     // [64]
   float* alpha_s = reinterpret_cast<float*>(small + 160 + 1280);  // [64]
+  int* vis_s = reinterpret_cast<int*>(small + 160 + 1536);        // [64]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int unit = blockIdx.x;
@@ -133,17 +137,18 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
   const int ntiles = pg1 - pg0;
   constexpr uint32_t o_col = 0, s_col0 = 4 * NH;  // TMEM columns: O^T blocks, S^T buffers
   constexpr uint32_t R = 2 * NH;                 // P^T row bytes
+  constexpr uint32_t kPBytes = kPage * R;        // one P^T buffer
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
       mbar_init(bar_sfull + 8 * s, 1);
       mbar_init(bar_sfree + 8 * s, 4);
+      mbar_init(bar_pfull + 8 * s, 4);
+      mbar_init(bar_pv + 8 * s, 1);
     }
-    mbar_init(bar_pfull, 4);
-    mbar_init(bar_pv, 1);
     mbar_init(bar_fin, 1);
     fence_mbar_init();
   }
@@ -151,7 +156,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
     tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
     tmem_relinquish();
   }
-  if (threadIdx.x < 64) mref[threadIdx.x] = -INFINITY;
+  if (threadIdx.x < 64) {
+    mref[threadIdx.x] = -INFINITY;
+    // rows past the last query row (padding of the final group) see nothing
+    const int row = row0 + threadIdx.x;
+    vis_s[threadIdx.x] = row < p.rows ? visible(p, S, row) : 0;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -165,13 +175,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
       for (int c = 0; c < kCols; ++c)
         tma_load_2d(sQ + c * NH * 128, &p.tm_q, 64 * c, b * p.rows + row0, bar_q);
       const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
-      bool ok = true;
       int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kStages;
-        if (t >= kStages && !mbar_wait(bar_empty + 8 * s, ((t - kStages) / kStages) & 1)) {
+        const int s = t & 1;
+        if (t >= kStages && !mbar_wait(bar_empty + 8 * s, ((t - kStages) >> 1) & 1)) {
           raise(kStatusWaitTimeout);
-          ok = false;
           break;
         }
         int page = __ldg(bt + pg0 + t);
@@ -188,23 +196,44 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
       // every issued copy has landed before the CTA may exit
       if (!mbar_wait(bar_q, 0)) raise(kStatusWaitTimeout);
       for (int t = max(0, issued - kStages); t < issued; ++t)
-        if (!mbar_wait(bar_full + 8 * (t % kStages), (t / kStages) & 1)) raise(kStatusWaitTimeout);
-      (void)ok;
+        if (!mbar_wait(bar_full + 8 * (t & 1), (t >> 1) & 1)) raise(kStatusWaitTimeout);
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
+    // Polls for the next ready step instead of blocking in a fixed order, so
+    // PV of tile t (which frees t's stage for the next load) never waits
+    // behind the arrival of page t+1.  Lane 0 decides and issues; the whole
+    // warp zeroes the tail rows of a request's last page.
     constexpr uint32_t idesc_qk = umma_idesc_bf16(64, NH, false, false);
     constexpr uint32_t idesc_pv = umma_idesc_bf16(128, NH, true, true);
     constexpr uint32_t p_layout = NH == 64 ? kSwizzle128 : (NH == 32 ? kSwizzle64 : kSwizzle32);
     bool ok = true;
     if (ntiles > 0) ok = wait_warp(bar_q, 0);
-    for (int t = 0; t <= ntiles && ok; ++t) {
-      if (t < ntiles) {
-        const int s = t % kStages;
-        if (!wait_warp(bar_full + 8 * s, (t / kStages) & 1)) { ok = false; break; }
-        // Zero the cache rows past the request's end in the last page (they
+    int qk = 0, pv = 0;  // next tile whose S = Q K^T / O^T += V^T P^T is issued
+    unsigned long long idle_since = global_timer_ns();
+    while (ok && pv < ntiles) {
+      int action = 0;  // 1 = PV(pv), 2 = QK(qk)
+      if (lane == 0) {
+        if (pv < qk && mbar_test_wait(bar_pfull + 8 * (pv & 1), (pv >> 1) & 1)) {
+          action = 1;
+        } else if (qk < ntiles && qk <= pv + 1 &&
+                   mbar_test_wait(bar_full + 8 * (qk & 1), (qk >> 1) & 1) &&
+                   (qk < 2 || mbar_test_wait(bar_sfree + 8 * (qk & 1), ((qk - 2) >> 1) & 1))) {
+          action = 2;
+        }
+      }
+      action = __shfl_sync(0xffffffffu, action, 0);
+      if (action == 0) {
+        if (global_timer_ns() - idle_since > kWaitLimitNs) ok = false;
+        continue;
+      }
+      idle_since = global_timer_ns();
+      tc_fence_after();
+      if (action == 2) {
+        const int s = qk & 1, buf = qk & 1;
+        // Zero the cache rows past the request's end in its last page (they
         // may hold anything, NaN included): 0 * NaN would poison O^T.
-        const int nv = min(kPage, S - (pg0 + t) * kPage);
+        const int nv = min(kPage, S - (pg0 + qk) * kPage);
         if (nv < kPage) {
           const int zrows = kPage - nv;
           for (int i = lane; i < kCols * zrows * 8; i += 32) {
@@ -217,9 +246,6 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
           fence_proxy_async_smem();
           __syncwarp();
         }
-        const int buf = t & 1;
-        if (t >= 2 && !wait_warp(bar_sfree + 8 * buf, ((t - 2) >> 1) & 1)) { ok = false; break; }
-        tc_fence_after();
         if (lane == 0) {
           const uint32_t kv = sRing + s * kStageBytes;
           #pragma unroll 1
@@ -236,28 +262,26 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
           umma_commit(bar_sfull + 8 * buf);
         }
         __syncwarp();
-      }
-      if (t >= 1) {
-        // PV of tile t-1 once its P^T is written (and O^T rescaled)
-        const int tp = t - 1, sp_ = tp % kStages;
-        if (!wait_warp(bar_pfull, tp & 1)) { ok = false; break; }
-        tc_fence_after();
+        ++qk;
+      } else {
         if (lane == 0) {
-          const uint32_t kv = sRing + sp_ * kStageBytes;
+          const uint32_t kv = sRing + (pv & 1) * kStageBytes;
+          const uint32_t pb = sP + (pv % NP) * kPBytes;
           #pragma unroll 1
           for (int j = 0; j < 4; ++j) {
             #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t a = umma_smem_desc(kv + 2 * j * kColBytes + kk * 16 * 128,
                                                 kColBytes, 1024, kSwizzle128);
-              const uint64_t bp = umma_smem_desc(sP + kk * 16 * R, 64 * R, 8 * R, p_layout);
-              umma_bf16_ss(tmem + o_col + j * NH, a, bp, idesc_pv, (tp | kk) != 0);
+              const uint64_t bp = umma_smem_desc(pb + kk * 16 * R, kPBytes, 8 * R, p_layout);
+              umma_bf16_ss(tmem + o_col + j * NH, a, bp, idesc_pv, (pv | kk) != 0);
             }
           }
-          umma_commit(bar_pv);
-          umma_commit(bar_empty + 8 * sp_);
+          umma_commit(bar_pv + 8 * (pv & 1));
+          umma_commit(bar_empty + 8 * (pv & 1));
         }
         __syncwarp();
+        ++pv;
       }
     }
     if (!ok) raise(kStatusWaitTimeout);
@@ -277,11 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
     float lpart[NH];
     #pragma unroll
     for (int h = 0; h < NH; ++h) lpart[h] = 0.f;
-    int vis[NH / 16];  // visible tokens per 16-row group of query rows (causal)
-    #pragma unroll
-    for (int g = 0; g < NH / 16; ++g) vis[g] = visible(p, S, row0 + 16 * g);
     bool ok = true;
-    bool o_live = false;  // O^T holds accumulated tiles
+    // Completion of PV(k) is phase k >> 1 of bar_pv[k & 1].
+    auto wait_pv = [&](int k) {
+      if (k >= 0 && ok && !wait_warp(bar_pv + 8 * (k & 1), (k >> 1) & 1)) ok = false;
+    };
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
       if (ok && !wait_warp(bar_sfull + 8 * buf, (t >> 1) & 1)) ok = false;
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
       bool need = false;
       #pragma unroll
       for (int h = 0; h < NH; ++h) {
-        const bool valid = active && tok < vis[h >> 4];
+        const bool valid = active && tok < vis_s[h];
         x[h] = valid ? x[h] * p.scale_log2 : -INFINITY;
         need |= x[h] > mref[h] + kRescaleLog2;
       }
@@ -311,9 +335,6 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
       named_bar_sync(1, 128);
       const int* v = vote + (t & 1) * 4;
       const bool rescale = (v[0] | v[1] | v[2] | v[3]) != 0;
-      // PV(t-1) must be complete before P^T is rewritten or O^T rescaled
-      if (t >= 1 && ok && !wait_warp(bar_pv, (t - 1) & 1)) ok = false;
-      tc_fence_after();
       if (rescale) {
         // tile max per head over the 64 token rows (16 lanes x 4 warps)
         #pragma unroll
@@ -335,8 +356,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
         named_bar_sync(1, 128);
         #pragma unroll
         for (int h = 0; h < NH; ++h) lpart[h] *= alpha_s[h];
-        if (o_live) {
-          // O^T[dv, h] *= alpha[h] on this warp's quadrant (dv rows 32 tq..)
+        if (t >= 1) {
+          // O^T[dv, h] *= alpha[h] on this warp's quadrant (dv rows 32 tq..),
+          // once every earlier PV has accumulated into it
+          wait_pv(t - 1);
+          tc_fence_after();
           #pragma unroll 1
           for (int j = 0; j < 4; ++j) {
             #pragma unroll
@@ -354,7 +378,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
           tmem_wait_st();
         }
       }
-      // P^T row of this token: p_h = 2^(x_h - m_ref_h), masked rows 0
+      // P^T row of this token: p_h = 2^(x_h - m_ref_h), masked rows 0; the
+      // buffer is free once the PV that last read it has completed
+      wait_pv(t - NP);
+      const uint32_t pb = sP + (t % NP) * kPBytes;
       if (active) {
         #pragma unroll
         for (int c8 = 0; c8 < NH / 8; ++c8) {
@@ -366,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
             lpart[h] += pv[k];
           }
           const uint32_t off = p_swz(tok_in_tile * R + 16 * c8, NH);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(sP + off),
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(pb + off),
                        "r"(pack2(pv[0], pv[1])), "r"(pack2(pv[2], pv[3])),
                        "r"(pack2(pv[4], pv[5])), "r"(pack2(pv[6], pv[7]))
                        : "memory");
@@ -375,11 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_pfull);
-      o_live = true;
+      if (lane == 0) mbar_arrive(bar_pfull + 8 * (t & 1));
     }
     // ------------------------------ epilogue ---------------------------------
-    if (ntiles > 0 && ok && !wait_warp(bar_pv, (ntiles - 1) & 1)) ok = false;
+    wait_pv(ntiles - 1);
     tc_fence_after();
     if (!ok) raise(kStatusWaitTimeout);
     // l[h] = sum over the 64 token rows of the per-thread partial sums
@@ -409,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
         #pragma unroll
         for (int k = 0; k < 16; ++k) {
           const int h = 16 * c16 + k;
+          if (row0 + h >= p.rows) continue;  // padding rows of the last group
           const float l = red[h] + red[64 + h] + red[128 + h] + red[192 + h];
           const float o = __uint_as_float(r[k]);
           const size_t grow = static_cast<size_t>(b) * p.rows + row0 + h;
@@ -419,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
         }
       }
     }
-    if (sidx < NH) {
+    if (sidx < NH && row0 + sidx < p.rows) {
       const int h = sidx;
       const int row = row0 + h;
       const float l = red[h] + red[64 + h] + red[128 + h] + red[192 + h];
@@ -539,11 +566,12 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Query rows per CTA: the smallest of 16 / 32 / 64 holding all rows of a
+// request, else 64 (the last group of a request is padded; padded rows are
+// computed on whatever the q tile holds there and never stored).
 int rows_per_cta(int rows) {
-  if (rows % 64 == 0) return 64;
-  if (rows % 32 == 0) return 32;
-  if (rows % 16 == 0) return 16;
-  return 0;
+  if (rows <= 0) return 0;
+  return rows <= 16 ? 16 : (rows <= 32 ? 32 : 64);
 }
 
 struct Layout {
@@ -555,12 +583,12 @@ Layout layout_for(int rows) {
   Layout L{};
   L.NH = rows_per_cta(rows);
   if (L.NH == 0) return L;
-  L.n_hg = rows / L.NH;
+  L.n_hg = (rows + L.NH - 1) / L.NH;
   L.q = 0;
   L.ring = L.q + gqa::mla::kCols * L.NH * 128;
   L.pbuf = L.ring + gqa::mla::kStages * gqa::mla::kStageBytes;
-  L.small = L.pbuf + kPage * 2 * L.NH;
-  L.total = L.small + 1536 + 1024;  // small region + alignment slack
+  L.small = L.pbuf + (L.NH == 64 ? 1 : 2) * kPage * 2 * L.NH;  // one / two P^T buffers
+  L.total = L.small + 2048 + 1024;  // small region (1952 B used) + alignment slack
   const int cols = 6 * L.NH;
   L.tmem_cols = cols <= 128 ? 128u : (cols <= 256 ? 256u : 512u);
   return L;
@@ -583,10 +611,23 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
   const Layout L = layout_for(rows);
   if (L.NH == 0 || B <= 0 || num_sms <= 0) return 1;
   const long long units = static_cast<long long>(B) * L.n_hg;
-  // enough CTAs to fill the SMs once, at least 2 pages per split
-  long long ns = (num_sms + units - 1) / units;
-  ns = std::min<long long>(ns, std::max(1, max_pages / 2));
-  return static_cast<int>(std::max<long long>(1, std::min<long long>(ns, 64)));
+  // One CTA per SM at a time: the smallest split count whose CTAs fill their
+  // last wave to >= 90 % (at least one full wave), keeping >= 4 pages per
+  // split; else the best fill among those.
+  const long long cap = std::max(1, std::min(64, max_pages / 4));
+  long long best = 1;
+  double best_fill = 0.0;
+  for (long long ns = 1; ns <= cap; ++ns) {
+    const long long ctas = units * ns;
+    const long long waves = (ctas + num_sms - 1) / num_sms;
+    const double fill = static_cast<double>(ctas) / (static_cast<double>(waves) * num_sms);
+    if (ctas >= num_sms && fill >= 0.9) return static_cast<int>(ns);
+    if (fill > best_fill + 1e-9) {
+      best_fill = fill;
+      best = ns;
+    }
+  }
+  return static_cast<int>(best);
 }
 
 size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits) {
@@ -607,8 +648,6 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   const int rows = s_q * h_q;
   const Layout L = layout_for(rows);
   if (L.NH == 0) return cudaErrorInvalidValue;
-  // causal masks are applied per 16 query rows: those must share one position
-  if (causal && s_q > 1 && h_q % 16 != 0) return cudaErrorInvalidValue;
   if (!q || !kv_cache || !block_table || !seq_lens || !out || !lse) return cudaErrorInvalidValue;
   if (!aligned16(q) || !aligned16(kv_cache)) return cudaErrorMisalignedAddress;
   Params p{};

@@ -452,7 +452,6 @@ std::vector<torch::Tensor> mla_decode(torch::Tensor q, torch::Tensor kv_cache,
   TORCH_CHECK(kv_cache.device() == q.device() && block_table.device() == q.device() &&
                   seq_lens.device() == q.device(),
               "all tensors must be on the same device");
-  TORCH_CHECK((q.size(1) * q.size(2)) % 16 == 0, "s_q * h_q must be a multiple of 16");
   TORCH_CHECK(num_splits >= 1 && num_splits <= 64, "num_splits must be in [1, 64]");
   const c10::cuda::CUDAGuard guard(q.device());
   const int64_t B = q.size(0), s_q = q.size(1), h_q = q.size(2);

@@ -69,6 +69,14 @@ def test_empty_request_and_auto_splits():
     assert torch.all(out[0] == 0)
 
 
+@pytest.mark.parametrize("s_q,h_q,causal", [(1, 1, False), (1, 3, False), (2, 63, True),
+                                             (1, 100, False), (2, 9, True)])
+def test_any_head_count(s_q, h_q, causal):
+    # FlashMLA's test grid also covers head counts that are not multiples of
+    # 16 (h_q 1, 3, 9, 63, 126): the last row group of a request is padded
+    check(*run_case([129, 64, 1000], s_q, h_q, causal=causal, num_splits=2, seed=5))
+
+
 def test_splits_agree():
     # the same request decoded with 1, 2 and 5 splits (combine kernel)
     case = tuple(t.cuda() for t in cases.make_mla_case([3000, 777], 1, 32, seed=4))
