@@ -42,11 +42,8 @@ namespace mla {
 constexpr int kD = 576;             // latent + rope dims per cached token
 constexpr int kDV = 512;            // value dims (the latent part)
 constexpr int kPage = 64;           // tokens per cache page (FlashMLA's block size)
-constexpr int kCols = kD / 64;      // 64-element (128-byte) column boxes per row: 9
-constexpr int kColBytes = kPage * 128;            // one box of a page: 8 KB
-constexpr int kStageBytes = kCols * kColBytes;    // one page: 72 KB
-constexpr int kStages = 2;
-constexpr int kThreads = 192;       // producer, MMA, 4 softmax warps
+constexpr int kColBytes = kPage * 128;            // one 64-dim box of a page: 8 KB
+constexpr int kThreads = 320;       // producer, MMA, 8 softmax warps (2 per TMEM quadrant)
 constexpr float kRescaleLog2 = 8.f; // lazy rescale threshold (log2 units)
 
 __device__ int g_mla_status;
@@ -63,8 +60,6 @@ struct Params {
   float* part_l;       // [B * rows, ns]
   int B, s_q, h_q, rows, n_hg, max_blocks, num_blocks, num_splits, causal;
   float scale_log2;    // softmax_scale * log2(e)
-  int smem_q, smem_ring, smem_p, smem_small;  // byte offsets in dynamic smem
-  uint32_t tmem_cols;
 };
 
 __device__ __forceinline__ void raise(int bit) { atomicOr(&g_mla_status, bit); }
@@ -95,36 +90,72 @@ __device__ __forceinline__ int visible(const Params& p, int S, int row) {
   return max(0, min(S, S - p.s_q + 1 + i));
 }
 
+// Compile-time geometry of the 2-CTA kernel for NH query rows per pair.
 template <int NH>
-__global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_constant__ Params p) {
-  static_assert(NH == 16 || NH == 32 || NH == 64, "query rows per CTA");
-  // P^T buffers: two (softmax of tile t+1 overlaps PV of tile t) where shared
-  // memory allows, one at NH = 64
-  constexpr int NP = NH == 64 ? 1 : 2;
+struct Pair {
+  static constexpr int kHalf = NH / 4;               // S^T values per softmax thread
+  static constexpr int kWarpCols = NH / 2;           // query rows per softmax warp
+  static constexpr int kChunk = kWarpCols < 16 ? kWarpCols : 16;  // TMEM columns per load
+  static constexpr int kCols = 5;                    // 64-dim boxes a CTA loads per row
+  static constexpr int kStageBytes = kCols * kColBytes;  // 40 KB per page
+  static constexpr int kStages = NH == 128 ? 2 : (NH == 64 ? 3 : 4);
+  static constexpr int kNP = NH == 128 ? 1 : 2;      // P^T buffers
+  static constexpr int kAtomN = NH < 64 ? NH : 64;   // heads per P^T swizzle atom
+  static constexpr int kRowB = 2 * kAtomN;           // P^T row bytes inside an atom
+  static constexpr int kAtoms = NH / kAtomN;
+  static constexpr int kAtomBytes = kPage * kRowB;
+  static constexpr int kPBytes = kAtoms * kAtomBytes;
+  static constexpr uint32_t kPLayout =
+      kAtomN == 64 ? kSwizzle128 : (kAtomN == 32 ? kSwizzle64 : kSwizzle32);
+  static constexpr uint32_t kPMask = kAtomN == 64 ? 7u : (kAtomN == 32 ? 3u : 1u);
+  static constexpr int kXBytes = kPage * NH * 4;     // partial S^T exchanged per tile
+  static constexpr int kQBytes = kCols * NH * 128;
+  static constexpr int kQ = 0;
+  static constexpr int kRing = kQ + kQBytes;
+  static constexpr int kP = kRing + kStages * kStageBytes;
+  static constexpr int kX = kP + kNP * kPBytes;
+  static constexpr int kSmall = kX + kXBytes;
+  static constexpr int kSmallBytes = 4096;
+  static constexpr int kSmem = kSmall + kSmallBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = 4 * NH;      // O^T 2 x NH, S^T 2 x NH
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+// One CTA pair (a 2-CTA cluster) = (request, NH <= 128 query rows, page
+// range).  CTA r loads, per 64-token page, latent columns 4r..4r+3 and the
+// rope column (five 64-dim boxes, 40 KB): it computes the partial
+//   S^T_r[64 tok, NH] over its 256 latent dims + half of the 64 rope dims
+// (18 MMAs of M = 64, N = NH), exchanges S^T_r with the peer through
+// st.async into the peer's shared memory, and from the full S^T = S^T_0 +
+// S^T_1 (identical in both CTAs) the softmax, P^T and
+//   O^T_r[256 dv, NH] += C[:, 256 r .. 256 r + 255]^T . P^T
+// (8 MMAs of M = 128).  26 MMAs per page per CTA instead of 52.
+template <int NH>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    mla_decode_kernel(const __grid_constant__ Params p) {
+  using G = Pair<NH>;
+  constexpr int kStages_ = G::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte alignment of every swizzle atom
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t s_base = smem_u32(smem);
-  const uint32_t sQ = s_base + p.smem_q;
-  const uint32_t sRing = s_base + p.smem_ring;
-  const uint32_t sP = s_base + p.smem_p;
-  unsigned char* small = smem + p.smem_small;
-  // small region: 14 mbarriers, TMEM base, votes [2][4], red [4][64],
-  // m_ref [64], alpha [64], visible tokens per query row [64]
-  const uint32_t bars = s_base + p.smem_small;
-  const uint32_t bar_q = bars + 0, bar_full = bars + 8, bar_empty = bars + 24,
-                 bar_sfull = bars + 40, bar_sfree = bars + 56, bar_pfull = bars + 72,
-                 bar_pv = bars + 88, bar_fin = bars + 104;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + 112);
-  int* vote = reinterpret_cast<int*>(small + 128);                // [2][4]
-  float* red = reinterpret_cast<float*>(small + 160);             // [4][64]
-  float* mref = reinterpret_cast<float*>(small + 160 + 1024);     // [64]
-  float* alpha_s = reinterpret_cast<float*>(small + 160 + 1280);  // [64]
-  int* vis_s = reinterpret_cast<int*>(small + 160 + 1536);        // [64]
+  const uint32_t sQ = s_base + G::kQ, sRing = s_base + G::kRing, sP = s_base + G::kP,
+                 sX = s_base + G::kX;
+  unsigned char* small = smem + G::kSmall;
+  const uint32_t bars = s_base + G::kSmall;
+  const uint32_t bar_q = bars, bar_full = bars + 8, bar_empty = bars + 40, bar_sfull = bars + 72,
+                 bar_sfree = bars + 88, bar_pfull = bars + 104, bar_pv = bars + 120,
+                 bar_xfull = bars + 136, bar_xfree = bars + 144, bar_fin = bars + 152;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + 160);
+  int* vote = reinterpret_cast<int*>(small + 176);                // [2][8]
+  float* red = reinterpret_cast<float*>(small + 256);             // [4][128]
+  float* mref = reinterpret_cast<float*>(small + 2304);           // [128]
+  float* alpha_s = reinterpret_cast<float*>(small + 2816);        // [128]
+  int* vis_s = reinterpret_cast<int*>(small + 3328);              // [128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int unit = blockIdx.x;
+  const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+  const int unit = blockIdx.x >> 1;
   const int hg = unit % p.n_hg;
   const int sp = (unit / p.n_hg) % p.num_splits;
   const int b = unit / (p.n_hg * p.num_splits);
@@ -135,50 +166,55 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
   const int chunk = (pages + p.num_splits - 1) / p.num_splits;
   const int pg0 = min(pages, sp * chunk), pg1 = min(pages, pg0 + chunk);
   const int ntiles = pg1 - pg0;
-  constexpr uint32_t o_col = 0, s_col0 = 4 * NH;  // TMEM columns: O^T blocks, S^T buffers
-  constexpr uint32_t R = 2 * NH;                 // P^T row bytes
-  constexpr uint32_t kPBytes = kPage * R;        // one P^T buffer
+  constexpr uint32_t o_col = 0, s_col0 = 2 * NH;  // TMEM columns: O^T blocks, S^T buffers
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < 4; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar_sfull + 8 * s, 1);
-      mbar_init(bar_sfree + 8 * s, 4);
-      mbar_init(bar_pfull + 8 * s, 4);
+      mbar_init(bar_sfree + 8 * s, 8);  // one arrival per softmax warp
+      mbar_init(bar_pfull + 8 * s, 8);
       mbar_init(bar_pv + 8 * s, 1);
     }
+    mbar_init(bar_xfull, 1);  // armed with the byte count by this CTA, bytes from the peer
+    mbar_init(bar_xfree, 8);  // the peer's eight softmax warps have read our partial
     mbar_init(bar_fin, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
+    tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
     tmem_relinquish();
   }
-  if (threadIdx.x < 64) {
+  if (threadIdx.x < 128) {
     mref[threadIdx.x] = -INFINITY;
     // rows past the last query row (padding of the final group) see nothing
     const int row = row0 + threadIdx.x;
-    vis_s[threadIdx.x] = row < p.rows ? visible(p, S, row) : 0;
+    vis_s[threadIdx.x] = threadIdx.x < NH && row < p.rows ? visible(p, S, row) : 0;
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote access
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // dims of the five boxes this CTA loads: latent columns 4r..4r+3, rope
+  auto col_of = [&](int c) { return c < 4 ? 4 * static_cast<int>(rank) + c : 8; };
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && ntiles > 0) {
       tma_prefetch_desc(&p.tm_kv);
-      mbar_arrive_expect_tx(bar_q, static_cast<uint32_t>(NH * kD * 2));
-      for (int c = 0; c < kCols; ++c)
-        tma_load_2d(sQ + c * NH * 128, &p.tm_q, 64 * c, b * p.rows + row0, bar_q);
+      mbar_arrive_expect_tx(bar_q, static_cast<uint32_t>(G::kQBytes));
+      for (int c = 0; c < G::kCols; ++c)
+        tma_load_2d(sQ + c * NH * 128, &p.tm_q, 64 * col_of(c), b * p.rows + row0, bar_q);
       const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
       int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
-        const int s = t & 1;
-        if (t >= kStages && !mbar_wait(bar_empty + 8 * s, ((t - kStages) >> 1) & 1)) {
+        const int s = t % kStages_;
+        if (t >= kStages_ && !mbar_wait(bar_empty + 8 * s, ((t - kStages_) / kStages_) & 1)) {
           raise(kStatusWaitTimeout);
           break;
         }
@@ -187,29 +223,27 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
           raise(kStatusBadPage);
           page = 0;
         }
-        mbar_arrive_expect_tx(bar_full + 8 * s, kStageBytes);
-        for (int c = 0; c < kCols; ++c)
-          tma_load_2d(sRing + s * kStageBytes + c * kColBytes, &p.tm_kv, 64 * c, page * kPage,
-                      bar_full + 8 * s);
+        mbar_arrive_expect_tx(bar_full + 8 * s, G::kStageBytes);
+        for (int c = 0; c < G::kCols; ++c)
+          tma_load_2d(sRing + s * G::kStageBytes + c * kColBytes, &p.tm_kv, 64 * col_of(c),
+                      page * kPage, bar_full + 8 * s);
         issued = t + 1;
       }
       // every issued copy has landed before the CTA may exit
       if (!mbar_wait(bar_q, 0)) raise(kStatusWaitTimeout);
-      for (int t = max(0, issued - kStages); t < issued; ++t)
-        if (!mbar_wait(bar_full + 8 * (t & 1), (t >> 1) & 1)) raise(kStatusWaitTimeout);
+      for (int t = max(0, issued - kStages_); t < issued; ++t)
+        if (!mbar_wait(bar_full + 8 * (t % kStages_), (t / kStages_) & 1))
+          raise(kStatusWaitTimeout);
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer --------------------------------
-    // Polls for the next ready step instead of blocking in a fixed order, so
-    // PV of tile t (which frees t's stage for the next load) never waits
-    // behind the arrival of page t+1.  Lane 0 decides and issues; the whole
-    // warp zeroes the tail rows of a request's last page.
+    // Polls (non-blocking) for the next ready step so that PV of tile t,
+    // which frees t's stage for the next load, never waits behind page t+1.
     constexpr uint32_t idesc_qk = umma_idesc_bf16(64, NH, false, false);
     constexpr uint32_t idesc_pv = umma_idesc_bf16(128, NH, true, true);
-    constexpr uint32_t p_layout = NH == 64 ? kSwizzle128 : (NH == 32 ? kSwizzle64 : kSwizzle32);
     bool ok = true;
     if (ntiles > 0) ok = wait_warp(bar_q, 0);
-    int qk = 0, pv = 0;  // next tile whose S = Q K^T / O^T += V^T P^T is issued
+    int qk = 0, pv = 0;
     unsigned long long idle_since = global_timer_ns();
     while (ok && pv < ntiles) {
       int action = 0;  // 1 = PV(pv), 2 = QK(qk)
@@ -217,29 +251,32 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
         if (pv < qk && mbar_test_wait(bar_pfull + 8 * (pv & 1), (pv >> 1) & 1)) {
           action = 1;
         } else if (qk < ntiles && qk <= pv + 1 &&
-                   mbar_test_wait(bar_full + 8 * (qk & 1), (qk >> 1) & 1) &&
+                   mbar_test_wait(bar_full + 8 * (qk % kStages_), (qk / kStages_) & 1) &&
                    (qk < 2 || mbar_test_wait(bar_sfree + 8 * (qk & 1), ((qk - 2) >> 1) & 1))) {
           action = 2;
         }
       }
       action = __shfl_sync(0xffffffffu, action, 0);
       if (action == 0) {
+        // back off: this warp shares an issue slot with a softmax warp
+        __nanosleep(64);
         if (global_timer_ns() - idle_since > kWaitLimitNs) ok = false;
         continue;
       }
       idle_since = global_timer_ns();
       tc_fence_after();
       if (action == 2) {
-        const int s = qk & 1, buf = qk & 1;
+        const int s = qk % kStages_, buf = qk & 1;
+        const uint32_t kv = sRing + s * G::kStageBytes;
         // Zero the cache rows past the request's end in its last page (they
         // may hold anything, NaN included): 0 * NaN would poison O^T.
         const int nv = min(kPage, S - (pg0 + qk) * kPage);
         if (nv < kPage) {
           const int zrows = kPage - nv;
-          for (int i = lane; i < kCols * zrows * 8; i += 32) {
+          for (int i = lane; i < G::kCols * zrows * 8; i += 32) {
             const int c = i / (zrows * 8), r = nv + (i / 8) % zrows, k = i % 8;
             asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(
-                             sRing + s * kStageBytes + c * kColBytes + r * 128 + k * 16),
+                             kv + c * kColBytes + r * 128 + k * 16),
                          "r"(0u)
                          : "memory");
           }
@@ -247,17 +284,14 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
           __syncwarp();
         }
         if (lane == 0) {
-          const uint32_t kv = sRing + s * kStageBytes;
+          // latent columns: all four k-steps; rope column: k-steps 2r, 2r+1
           #pragma unroll 1
-          for (int c = 0; c < kCols; ++c) {
-            #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a =
-                  umma_smem_desc(kv + c * kColBytes + kk * 32, 16, 1024, kSwizzle128);
-              const uint64_t bq =
-                  umma_smem_desc(sQ + c * NH * 128 + kk * 32, 16, 1024, kSwizzle128);
-              umma_bf16_ss(tmem + s_col0 + buf * NH, a, bq, idesc_qk, (c | kk) != 0);
-            }
+          for (int i = 0; i < 18; ++i) {
+            const int c = i < 16 ? i >> 2 : 4;
+            const int kk = i < 16 ? i & 3 : 2 * static_cast<int>(rank) + (i - 16);
+            const uint64_t a = umma_smem_desc(kv + c * kColBytes + kk * 32, 16, 1024, kSwizzle128);
+            const uint64_t bq = umma_smem_desc(sQ + c * NH * 128 + kk * 32, 16, 1024, kSwizzle128);
+            umma_bf16_ss(tmem + s_col0 + buf * NH, a, bq, idesc_qk, i != 0);
           }
           umma_commit(bar_sfull + 8 * buf);
         }
@@ -265,20 +299,21 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
         ++qk;
       } else {
         if (lane == 0) {
-          const uint32_t kv = sRing + (pv & 1) * kStageBytes;
-          const uint32_t pb = sP + (pv % NP) * kPBytes;
+          const uint32_t kv = sRing + (pv % kStages_) * G::kStageBytes;
+          const uint32_t pb = sP + (pv % G::kNP) * G::kPBytes;
           #pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 2; ++j) {
             #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a = umma_smem_desc(kv + 2 * j * kColBytes + kk * 16 * 128,
-                                                kColBytes, 1024, kSwizzle128);
-              const uint64_t bp = umma_smem_desc(pb + kk * 16 * R, kPBytes, 8 * R, p_layout);
+              const uint64_t a = umma_smem_desc(kv + 2 * j * kColBytes + kk * 16 * 128, kColBytes,
+                                                1024, kSwizzle128);
+              const uint64_t bp = umma_smem_desc(pb + kk * 16 * G::kRowB, G::kAtomBytes,
+                                                 8 * G::kRowB, G::kPLayout);
               umma_bf16_ss(tmem + o_col + j * NH, a, bp, idesc_pv, (pv | kk) != 0);
             }
           }
           umma_commit(bar_pv + 8 * (pv & 1));
-          umma_commit(bar_empty + 8 * (pv & 1));
+          umma_commit(bar_empty + 8 * (pv % kStages_));
         }
         __syncwarp();
         ++pv;
@@ -290,166 +325,267 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
     __syncwarp();
     if (!wait_warp(bar_fin, 0)) raise(kStatusWaitTimeout);
   } else {
-    // --------------------------- softmax warps 2..5 ----------------------------
+    // --------------------------- softmax warps 2..9 ----------------------------
+    // Warp w reads TMEM lane quadrant w % 4 (tokens 16 q .. 16 q + 15 in the
+    // M = 64 layout) and query rows [cg NH/2, (cg + 1) NH/2), cg = (w - 2) / 4;
+    // lanes 0-15 / 16-31 take the first / second half of those rows.
     // Every softmax warp runs the same sequence of named barriers whatever
     // happens (a failed wait only clears `ok`), so they can never deadlock.
-    const int tq = warp & 3;        // TMEM lane quadrant
-    const bool active = lane < 16;  // S^T rows (M = 64 layout): lanes 0-15 of a quadrant
-    const int tok_in_tile = 16 * tq + lane;
+    const int tq = warp & 3;              // TMEM lane quadrant
+    const int cg = (warp - 2) >> 2;       // column group
+    const int wi = warp - 2;              // 0..7
+    const int t0 = lane & 15, half = lane >> 4;
+    const int tok_in_tile = 16 * tq + t0;
+    const int hw = cg * G::kWarpCols;     // first query row of this warp
+    const int h0 = hw + half * G::kHalf;  // first query row of this thread
     const uint32_t lane_base = static_cast<uint32_t>(32 * tq) << 16;
-    const int sidx = threadIdx.x - 64;  // 0..127
-    float lpart[NH];
+    const int sidx = threadIdx.x - 64;    // 0..255
+    const uint32_t peer_x = mapa_shared(sX, peer);
+    const uint32_t peer_xfull = mapa_shared(bar_xfull, peer);
+    const uint32_t peer_xfree = mapa_shared(bar_xfree, peer);
+    float lpart[G::kHalf];
     #pragma unroll
-    for (int h = 0; h < NH; ++h) lpart[h] = 0.f;
+    for (int k = 0; k < G::kHalf; ++k) lpart[k] = 0.f;
+    int vis_min = 0x7fffffff;  // fewest visible tokens over this thread's rows
+    #pragma unroll 1
+    for (int k = 0; k < G::kHalf; ++k) vis_min = min(vis_min, vis_s[h0 + k]);
     bool ok = true;
-    // Completion of PV(k) is phase k >> 1 of bar_pv[k & 1].
-    auto wait_pv = [&](int k) {
+    auto wait_pv = [&](int k) {  // completion of PV(k): phase k >> 1 of bar_pv[k & 1]
       if (k >= 0 && ok && !wait_warp(bar_pv + 8 * (k & 1), (k >> 1) & 1)) ok = false;
+    };
+    auto wait_cluster = [&](uint32_t bar, uint32_t parity) {
+      if (!ok) return;
+      bool done = mbar_try_wait_cluster(bar, parity);
+      if (!done) {
+        const unsigned long long t_start = global_timer_ns();
+        while (!(done = mbar_try_wait_cluster(bar, parity)))
+          if (global_timer_ns() - t_start > kWaitLimitNs) break;
+      }
+      if (!__all_sync(0xffffffffu, done)) ok = false;
     };
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
+      if (sidx == 0) mbar_arrive_expect_tx(bar_xfull, G::kXBytes);  // the peer's partial
       if (ok && !wait_warp(bar_sfull + 8 * buf, (t >> 1) & 1)) ok = false;
       tc_fence_after();
-      float x[NH];
-      #pragma unroll
-      for (int c16 = 0; c16 < NH / 16; ++c16) {
-        uint32_t r[16];
-        tmem_ld16(tmem + lane_base + s_col0 + buf * NH + 16 * c16, r);
-        tmem_wait_ld();
-        #pragma unroll
-        for (int k = 0; k < 16; ++k) x[16 * c16 + k] = __uint_as_float(r[k]);
+      float x[G::kHalf];
+      {
+        const uint32_t a = tmem + lane_base + s_col0 + buf * NH + hw;
+        if constexpr (G::kHalf == 4) {
+          uint32_t r[4];
+          tmem_ld_16x32bx2_4<4>(a, r);
+          tmem_wait_ld();
+          #pragma unroll
+          for (int k = 0; k < 4; ++k) x[k] = __uint_as_float(r[k]);
+        } else if constexpr (G::kHalf == 8) {
+          uint32_t r[8];
+          tmem_ld_16x32bx2_8<8>(a, r);
+          tmem_wait_ld();
+          #pragma unroll
+          for (int k = 0; k < 8; ++k) x[k] = __uint_as_float(r[k]);
+        } else {
+          uint32_t r[G::kHalf / 16][16];
+          #pragma unroll
+          for (int c16 = 0; c16 < G::kHalf / 16; ++c16)
+            tmem_ld_16x32bx2_16<G::kHalf>(a + 16 * c16, r[c16]);
+          tmem_wait_ld();
+          #pragma unroll
+          for (int c16 = 0; c16 < G::kHalf / 16; ++c16) {
+            #pragma unroll
+            for (int k = 0; k < 16; ++k) x[16 * c16 + k] = __uint_as_float(r[c16][k]);
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sfree + 8 * buf);
+      // exchange: our partial into the peer's buffer (once it has read the
+      // previous one), the peer's partial out of ours
+      if (t >= 1) wait_cluster(bar_xfree, (t - 1) & 1);
+      #pragma unroll
+      for (int k4 = 0; k4 < G::kHalf / 4; ++k4)
+        st_async_v4(peer_x + (k4 * 256 + sidx) * 16, __float_as_uint(x[4 * k4]),
+                    __float_as_uint(x[4 * k4 + 1]), __float_as_uint(x[4 * k4 + 2]),
+                    __float_as_uint(x[4 * k4 + 3]), peer_xfull);
+      wait_cluster(bar_xfull, t & 1);
+      uint32_t dep = 0;
+      #pragma unroll
+      for (int k4 = 0; k4 < G::kHalf / 4; ++k4) {
+        float4 o;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                     : "r"(sX + (k4 * 256 + sidx) * 16)
+                     : "memory");
+        // S0 + S1 in both CTAs (addition commutes: identical bits)
+        x[4 * k4] += o.x;
+        x[4 * k4 + 1] += o.y;
+        x[4 * k4 + 2] += o.z;
+        x[4 * k4 + 3] += o.w;
+        dep ^= __float_as_uint(o.x) ^ __float_as_uint(o.w);
+      }
+      // every lane's reads of the peer's partial are complete once all lanes
+      // have produced dep; then the peer may overwrite the buffer
+      dep = __reduce_xor_sync(0xffffffffu, dep);
+      if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree, dep);
       const int tok = (pg0 + t) * kPage + tok_in_tile;
       bool need = false;
-      #pragma unroll
-      for (int h = 0; h < NH; ++h) {
-        const bool valid = active && tok < vis_s[h];
-        x[h] = valid ? x[h] * p.scale_log2 : -INFINITY;
-        need |= x[h] > mref[h] + kRescaleLog2;
+      if (tok < vis_min) {  // every row of this thread sees the token
+        #pragma unroll
+        for (int k = 0; k < G::kHalf; ++k) {
+          x[k] *= p.scale_log2;
+          need |= x[k] > mref[h0 + k] + kRescaleLog2;
+        }
+      } else {
+        #pragma unroll
+        for (int k = 0; k < G::kHalf; ++k) {
+          const bool valid = tok < vis_s[h0 + k];
+          x[k] = valid ? x[k] * p.scale_log2 : -INFINITY;
+          need |= x[k] > mref[h0 + k] + kRescaleLog2;
+        }
       }
       need = __any_sync(0xffffffffu, need);
-      if (lane == 0) vote[(t & 1) * 4 + tq] = need ? 1 : 0;
-      named_bar_sync(1, 128);
-      const int* v = vote + (t & 1) * 4;
-      const bool rescale = (v[0] | v[1] | v[2] | v[3]) != 0;
+      if (lane == 0) vote[(t & 1) * 8 + wi] = need ? 1 : 0;
+      named_bar_sync(1, 256);
+      const int* v = vote + (t & 1) * 8;
+      const bool rescale = (v[0] | v[1] | v[2] | v[3] | v[4] | v[5] | v[6] | v[7]) != 0;
       if (rescale) {
-        // tile max per head over the 64 token rows (16 lanes x 4 warps)
+        // tile max per row over the 64 tokens (16 lanes of each half x 4 warps)
         #pragma unroll
-        for (int h = 0; h < NH; ++h) {
-          float m = x[h];
+        for (int k = 0; k < G::kHalf; ++k) {
+          float m = x[k];
           #pragma unroll
           for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-          if (lane == 0) red[tq * 64 + h] = m;
+          if (t0 == 0) red[tq * 128 + h0 + k] = m;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 256);
         if (sidx < NH) {
           const int h = sidx;
-          const float tmax = fmaxf(fmaxf(red[h], red[64 + h]), fmaxf(red[128 + h], red[192 + h]));
+          const float tmax =
+              fmaxf(fmaxf(red[h], red[128 + h]), fmaxf(red[256 + h], red[384 + h]));
           const float mo = mref[h];
           const float mn = fmaxf(mo, tmax);
           alpha_s[h] = mo == -INFINITY ? 0.f : exp2f(mo - mn);
           mref[h] = mn;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 256);
         #pragma unroll
-        for (int h = 0; h < NH; ++h) lpart[h] *= alpha_s[h];
+        for (int k = 0; k < G::kHalf; ++k) lpart[k] *= alpha_s[h0 + k];
         if (t >= 1) {
           // O^T[dv, h] *= alpha[h] on this warp's quadrant (dv rows 32 tq..),
           // once every earlier PV has accumulated into it
           wait_pv(t - 1);
           tc_fence_after();
           #pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-            #pragma unroll
-            for (int c16 = 0; c16 < NH / 16; ++c16) {
-              uint32_t r[16];
-              const uint32_t a = tmem + lane_base + o_col + j * NH + 16 * c16;
-              tmem_ld16(a, r);
-              tmem_wait_ld();
-              #pragma unroll
-              for (int k = 0; k < 16; ++k)
-                r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha_s[16 * c16 + k]);
-              tmem_st16(a, r);
+          for (int j = 0; j < 2; ++j) {
+            #pragma unroll 1
+            for (int c = 0; c < G::kWarpCols; c += G::kChunk) {
+              const uint32_t a = tmem + lane_base + o_col + j * NH + hw + c;
+              if constexpr (G::kChunk == 16) {
+                uint32_t r[16];
+                tmem_ld16(a, r);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int k = 0; k < 16; ++k)
+                  r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha_s[hw + c + k]);
+                tmem_st16(a, r);
+              } else {
+                uint32_t r[8];
+                tmem_ld8(a, r);
+                tmem_wait_ld();
+                #pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha_s[hw + c + k]);
+                tmem_st8(a, r);
+              }
             }
           }
           tmem_wait_st();
         }
       }
-      // P^T row of this token: p_h = 2^(x_h - m_ref_h), masked rows 0; the
-      // buffer is free once the PV that last read it has completed
-      wait_pv(t - NP);
-      const uint32_t pb = sP + (t % NP) * kPBytes;
-      if (active) {
+      // P^T of this token for this thread's rows: p = 2^(x - m_ref), masked
+      // entries 0; the buffer is free once the PV that last read it is done
+      wait_pv(t - G::kNP);
+      const uint32_t pb = sP + (t % G::kNP) * G::kPBytes;
+      #pragma unroll
+      for (int c4 = 0; c4 < G::kHalf / 4; ++c4) {
+        float pv[4], mr[4];
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(mr[0]), "=f"(mr[1]), "=f"(mr[2]), "=f"(mr[3])
+                     : "r"(smem_u32(mref + h0 + 4 * c4)));
         #pragma unroll
-        for (int c8 = 0; c8 < NH / 8; ++c8) {
-          float pv[8];
-          #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int h = 8 * c8 + k;
-            pv[k] = x[h] == -INFINITY ? 0.f : exp2f(x[h] - mref[h]);
-            lpart[h] += pv[k];
-          }
-          const uint32_t off = p_swz(tok_in_tile * R + 16 * c8, NH);
-          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(pb + off),
-                       "r"(pack2(pv[0], pv[1])), "r"(pack2(pv[2], pv[3])),
-                       "r"(pack2(pv[4], pv[5])), "r"(pack2(pv[6], pv[7]))
-                       : "memory");
+        for (int k = 0; k < 4; ++k) {
+          const int kk = 4 * c4 + k;
+          // x = -inf (masked) gives 0; m_ref is finite once any score was
+          // seen (the first visible tile always rescales)
+          pv[k] = x[kk] == -INFINITY ? 0.f : fast_exp2(x[kk] - mr[k]);
+          lpart[kk] += pv[k];
         }
+        const int hcol = h0 + 4 * c4;  // first query row of these 4 values
+        const uint32_t off = static_cast<uint32_t>((hcol / 64) * G::kAtomBytes +
+                                                   tok_in_tile * G::kRowB + (hcol % 64) * 2);
+        const uint32_t swz = off ^ (((off >> 7) & G::kPMask) << 4);
+        asm volatile("st.shared.v2.u32 [%0], {%1, %2};" ::"r"(pb + swz),
+                     "r"(pack2(pv[0], pv[1])), "r"(pack2(pv[2], pv[3]))
+                     : "memory");
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull + 8 * (t & 1));
     }
+    // the peer has read our last partial before either CTA may exit
+    if (ntiles >= 1) wait_cluster(bar_xfree, (ntiles - 1) & 1);
     // ------------------------------ epilogue ---------------------------------
     wait_pv(ntiles - 1);
     tc_fence_after();
     if (!ok) raise(kStatusWaitTimeout);
     // l[h] = sum over the 64 token rows of the per-thread partial sums
-    named_bar_sync(1, 128);
+    named_bar_sync(1, 256);
     #pragma unroll
-    for (int h = 0; h < NH; ++h) {
-      float l = active ? lpart[h] : 0.f;
+    for (int k = 0; k < G::kHalf; ++k) {
+      float l = lpart[k];
       #pragma unroll
       for (int off = 8; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-      if (lane == 0) red[tq * 64 + h] = l;
+      if (t0 == 0) red[tq * 128 + h0 + k] = l;
     }
-    named_bar_sync(1, 128);
+    named_bar_sync(1, 256);
     const int L = 32 * tq + lane;  // dv row within each 128-row block of O^T
     const bool final_out = p.num_splits == 1;
+    const int dv0 = 256 * static_cast<int>(rank);
     #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
-      #pragma unroll
-      for (int c16 = 0; c16 < NH / 16; ++c16) {
-        uint32_t r[16];
+    for (int j = 0; j < 2; ++j) {
+      #pragma unroll 1
+      for (int c = 0; c < G::kWarpCols; c += G::kChunk) {
+        uint32_t r[G::kChunk];
         if (ntiles > 0) {
-          tmem_ld16(tmem + lane_base + o_col + j * NH + 16 * c16, r);
+          if constexpr (G::kChunk == 16)
+            tmem_ld16(tmem + lane_base + o_col + j * NH + hw + c, r);
+          else
+            tmem_ld8(tmem + lane_base + o_col + j * NH + hw + c, r);
           tmem_wait_ld();
         } else {
           #pragma unroll
-          for (int k = 0; k < 16; ++k) r[k] = 0u;
+          for (int k = 0; k < G::kChunk; ++k) r[k] = 0u;
         }
         #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int h = 16 * c16 + k;
+        for (int k = 0; k < G::kChunk; ++k) {
+          const int h = hw + c + k;
           if (row0 + h >= p.rows) continue;  // padding rows of the last group
-          const float l = red[h] + red[64 + h] + red[128 + h] + red[192 + h];
+          const float l = red[h] + red[128 + h] + red[256 + h] + red[384 + h];
           const float o = __uint_as_float(r[k]);
           const size_t grow = static_cast<size_t>(b) * p.rows + row0 + h;
+          const int d = dv0 + 128 * j + L;
           if (final_out)
-            p.out[grow * kDV + 128 * j + L] = __float2bfloat16(l > 0.f ? o / l : 0.f);
+            p.out[grow * kDV + d] = __float2bfloat16(l > 0.f ? o / l : 0.f);
           else
-            p.part_acc[(grow * p.num_splits + sp) * kDV + 128 * j + L] = l > 0.f ? o : 0.f;
+            p.part_acc[(grow * p.num_splits + sp) * kDV + d] = l > 0.f ? o : 0.f;
         }
       }
     }
-    if (sidx < NH && row0 + sidx < p.rows) {
+    if (rank == 0 && sidx < NH && row0 + sidx < p.rows) {
       const int h = sidx;
       const int row = row0 + h;
-      const float l = red[h] + red[64 + h] + red[128 + h] + red[192 + h];
+      const float l = red[h] + red[128 + h] + red[256 + h] + red[384 + h];
       const float m = l > 0.f ? mref[h] : -INFINITY;
       const size_t grow = static_cast<size_t>(b) * p.rows + row;
       if (final_out) {
@@ -466,8 +602,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_kernel(const __grid_co
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, p.tmem_cols);
+    tmem_dealloc(tmem, G::kTmemCols);
   }
+  cluster_sync();  // no CTA leaves while its peer may still address its shared memory
 }
 
 // Merge of the num_splits partial states of every (request, query row):
@@ -569,28 +706,28 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows
 // Query rows per CTA: the smallest of 16 / 32 / 64 holding all rows of a
 // request, else 64 (the last group of a request is padded; padded rows are
 // computed on whatever the q tile holds there and never stored).
-int rows_per_cta(int rows) {
+// Query rows per CTA pair: the smallest of 16 / 32 / 64 / 128 holding all
+// rows of a request, else 128 (the last group of a request is padded;
+// padded rows are computed on whatever the q tile holds there and never
+// stored).
+int rows_per_pair(int rows) {
   if (rows <= 0) return 0;
-  return rows <= 16 ? 16 : (rows <= 32 ? 32 : 64);
+  return rows <= 16 ? 16 : (rows <= 32 ? 32 : (rows <= 64 ? 64 : 128));
 }
 
 struct Layout {
-  int NH, n_hg, q, ring, pbuf, small, total;
-  uint32_t tmem_cols;
+  int NH, n_hg, smem;
 };
 
 Layout layout_for(int rows) {
   Layout L{};
-  L.NH = rows_per_cta(rows);
+  L.NH = rows_per_pair(rows);
   if (L.NH == 0) return L;
   L.n_hg = (rows + L.NH - 1) / L.NH;
-  L.q = 0;
-  L.ring = L.q + gqa::mla::kCols * L.NH * 128;
-  L.pbuf = L.ring + gqa::mla::kStages * gqa::mla::kStageBytes;
-  L.small = L.pbuf + (L.NH == 64 ? 1 : 2) * kPage * 2 * L.NH;  // one / two P^T buffers
-  L.total = L.small + 2048 + 1024;  // small region (1952 B used) + alignment slack
-  const int cols = 6 * L.NH;
-  L.tmem_cols = cols <= 128 ? 128u : (cols <= 256 ? 256u : 512u);
+  L.smem = L.NH == 16    ? gqa::mla::Pair<16>::kSmem
+           : L.NH == 32  ? gqa::mla::Pair<32>::kSmem
+           : L.NH == 64  ? gqa::mla::Pair<64>::kSmem
+                         : gqa::mla::Pair<128>::kSmem;
   return L;
 }
 
@@ -611,17 +748,18 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
   const Layout L = layout_for(rows);
   if (L.NH == 0 || B <= 0 || num_sms <= 0) return 1;
   const long long units = static_cast<long long>(B) * L.n_hg;
-  // One CTA per SM at a time: the smallest split count whose CTAs fill their
-  // last wave to >= 90 % (at least one full wave), keeping >= 4 pages per
-  // split; else the best fill among those.
+  // One CTA pair per two SMs at a time: the smallest split count whose pairs
+  // fill their last wave to >= 90 % (at least one full wave), keeping >= 4
+  // pages per split; else the best fill among those.
+  const long long slots = std::max(1, num_sms / 2);
   const long long cap = std::max(1, std::min(64, max_pages / 4));
   long long best = 1;
   double best_fill = 0.0;
   for (long long ns = 1; ns <= cap; ++ns) {
     const long long ctas = units * ns;
-    const long long waves = (ctas + num_sms - 1) / num_sms;
-    const double fill = static_cast<double>(ctas) / (static_cast<double>(waves) * num_sms);
-    if (ctas >= num_sms && fill >= 0.9) return static_cast<int>(ns);
+    const long long waves = (ctas + slots - 1) / slots;
+    const double fill = static_cast<double>(ctas) / (static_cast<double>(waves) * slots);
+    if (ctas >= slots && fill >= 0.9) return static_cast<int>(ns);
     if (fill > best_fill + 1e-9) {
       best_fill = fill;
       best = ns;
@@ -668,11 +806,6 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   p.num_splits = num_splits;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.smem_q = L.q;
-  p.smem_ring = L.ring;
-  p.smem_p = L.pbuf;
-  p.smem_small = L.small;
-  p.tmem_cols = L.tmem_cols;
   if (num_splits > 1) {
     const size_t need = part_bytes(B, rows, num_splits);
     if (!workspace || workspace_bytes < need || !aligned16(workspace)) return cudaErrorInvalidValue;
@@ -687,23 +820,30 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    for (auto fn : {mla_decode_kernel<16>, mla_decode_kernel<32>, mla_decode_kernel<64>}) {
-      const cudaError_t e =
-          cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
-      if (e != cudaSuccess) attr_err = e;
-    }
+    const cudaError_t e[4] = {
+        cudaFuncSetAttribute(mla_decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Pair<16>::kSmem),
+        cudaFuncSetAttribute(mla_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Pair<32>::kSmem),
+        cudaFuncSetAttribute(mla_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Pair<64>::kSmem),
+        cudaFuncSetAttribute(mla_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Pair<128>::kSmem)};
+    for (cudaError_t x : e)
+      if (x != cudaSuccess) attr_err = x;
   });
   if (attr_err != cudaSuccess) return attr_err;
-  if (L.total > 232448) return cudaErrorInvalidValue;
-  const long long grid = static_cast<long long>(B) * L.n_hg * num_splits;
+  const long long grid = 2LL * B * L.n_hg * num_splits;  // 2-CTA clusters
   if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   const unsigned g = static_cast<unsigned>(grid);
-  if (L.NH == 64)
-    mla_decode_kernel<64><<<g, kThreads, L.total, stream>>>(p);
+  if (L.NH == 128)
+    mla_decode_kernel<128><<<g, kThreads, L.smem, stream>>>(p);
+  else if (L.NH == 64)
+    mla_decode_kernel<64><<<g, kThreads, L.smem, stream>>>(p);
   else if (L.NH == 32)
-    mla_decode_kernel<32><<<g, kThreads, L.total, stream>>>(p);
+    mla_decode_kernel<32><<<g, kThreads, L.smem, stream>>>(p);
   else
-    mla_decode_kernel<16><<<g, kThreads, L.total, stream>>>(p);
+    mla_decode_kernel<16><<<g, kThreads, L.smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || num_splits == 1) return e;
   CombineParams c{p.part_acc, p.part_m, p.part_l, out, lse, B, s_q, h_q, rows, num_splits};

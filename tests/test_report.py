@@ -52,7 +52,8 @@ def test_every_gqa_kernel_has_a_capture():
                for _, m in secs}
     for k in ("gqa_decode_scan_kernel", "gqa_decode_fixed_merge_kernel",
               "gqa_decode_shard_merge_kernel", "gqa_decode_simt_kernel",
-              "gqa_decode_plan_kernel", "gqa_decode_block_table_to_csr_kernel"):
+              "gqa_decode_plan_kernel", "gqa_decode_block_table_to_csr_kernel",
+              "mla_decode_kernel"):
         assert k in kernels, k
     for _, (_, secs) in caps.items():
         for _, m in secs:
