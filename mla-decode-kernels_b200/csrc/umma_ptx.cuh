@@ -1,7 +1,7 @@
 // Inline-PTX building blocks for the tcgen05 (5th-generation tensor core)
 // kernels: tensor-memory allocation, UMMA shared-memory and instruction
 // descriptors, tcgen05.mma / commit, tensor-memory loads and stores, and
-// 2-D tiled TMA loads (cp.async.bulk.tensor, never with multicast).
+// 2-D tiled TMA loads (cp.async.bulk.tensor, each CTA loading its own tiles).
 //
 // Descriptor bit layouts follow the PTX ISA's tcgen05 "shared memory
 // descriptor" and "instruction descriptor" tables (restated in CUTLASS's
