@@ -254,3 +254,35 @@ def mla_flops(seq_lens, s_q, h_q, causal=False):
     """FlashMLA's FLOP count: per query row 2 * S * (576 + 512) (no causal discount)."""
     total = int(torch.as_tensor(seq_lens, dtype=torch.int64).clamp_min(0).sum())
     return total * s_q * h_q * 2 * (MLA_D + MLA_DV)
+
+
+# ---- DSA-style sparse decode cases (K3) -------------------------------------
+#
+# The MLA case plus DeepSeek-sparse-attention indexer inputs: index queries
+# q_idx [B, s_q, H, 128], per-head weights w_idx [B, s_q, H] and an index-key
+# cache k_idx [num_blocks, 64, 128] paged by the same block table.
+
+DSA_D = 128
+
+
+def make_dsa_case(seq_lens, s_q, h_q, n_idx_heads=64, page=64, *, seed=0, pool_factor=2.0,
+                  poison=True, device="cpu"):
+    gen = torch.Generator(device=torch.device(device)).manual_seed(seed)
+    q, kv, bt, sl = make_mla_case(seq_lens, s_q, h_q, page, seed=seed, pool_factor=pool_factor,
+                                  poison=poison, device=device, gen=gen)
+    B = len(seq_lens)
+    pool = kv.shape[0]
+    q_idx = _randn_bf16((B, s_q, n_idx_heads, DSA_D), gen, 1.0, device)
+    w_idx = (torch.randn((B, s_q, n_idx_heads), generator=gen, device=device)
+             / math.sqrt(n_idx_heads)).float()
+    k_idx = _randn_bf16((pool, page, DSA_D), gen, 1.0, device)
+    if poison:
+        used = torch.zeros(pool, dtype=torch.bool, device=device)
+        for b, s in enumerate(seq_lens):
+            n = (int(s) + page - 1) // page
+            used[bt[b, :n].long()] = True
+            rem = int(s) % page
+            if s > 0 and rem:
+                k_idx[int(bt[b, n - 1]), rem:] = float("nan")
+        k_idx[~used] = float("nan")
+    return q, kv, q_idx, w_idx, k_idx, bt, sl

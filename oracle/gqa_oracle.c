@@ -312,3 +312,65 @@ void oracle_mla_ref(const uint16_t* q, const uint16_t* kv, const int32_t* block_
                  out, lse};
   parallel_for((int64_t)B * s_q * h_q, nthreads, mla_ref_task, &c);
 }
+
+/* ---- DSA-style sparse decode (K3): the indexer ------------------------------
+ *
+ * The reference's roadmap kernel K3 ("DSA-style sparse decode: indexer +
+ * top-k + sparse gather", README.md "Roadmap") has no code in the reference.
+ * Restated operator (DeepSeek sparse attention's lightning indexer): for
+ * request b, query position i, cached token t < visible(b, i):
+ *   I[b, i, t] = sum_j w[b, i, j] * relu(q_idx[b, i, j, :] . k_idx[t, :])
+ * with H index heads of 128 dims, k_idx paged like the latent cache
+ * ([num_blocks, page, 128]); tokens a query cannot see score -inf.  The
+ * top-k selection and the attention over the selected tokens are restated
+ * in oracle.py (selection) and oracle_mla_ref (attention). */
+
+#define DSA_D 128
+
+typedef struct {
+  const uint16_t *q, *k;
+  const float* w;
+  const int32_t *bt, *sl;
+  int B, s_q, H, page, max_blocks, causal, smax;
+  float* scores;
+} dsa_ctx_t;
+
+static void dsa_scores_task(void* vctx, int64_t bi) {
+  const dsa_ctx_t* c = (const dsa_ctx_t*)vctx;
+  const int i = (int)(bi % c->s_q);
+  const int b = (int)(bi / c->s_q);
+  const int S = c->sl[b];
+  int vis = c->causal ? S - c->s_q + 1 + i : S;
+  if (vis > S) vis = S;
+  if (vis < 0) vis = 0;
+  float* out = c->scores + bi * c->smax;
+  for (int t = 0; t < c->smax; ++t) out[t] = -INFINITY;
+  float* qf = (float*)malloc(sizeof(float) * (size_t)c->H * DSA_D);
+  const uint16_t* qrow = c->q + bi * c->H * DSA_D;
+  for (int e = 0; e < c->H * DSA_D; ++e) qf[e] = bf16_to_f32(qrow[e]);
+  const float* w = c->w + bi * c->H;
+  for (int t = 0; t < vis && t < c->smax; ++t) {
+    const int p = c->bt[(int64_t)b * c->max_blocks + t / c->page];
+    const uint16_t* krow = c->k + ((int64_t)p * c->page + t % c->page) * DSA_D;
+    float kf[DSA_D];
+    for (int d = 0; d < DSA_D; ++d) kf[d] = bf16_to_f32(krow[d]);
+    float s = 0.f;
+    for (int j = 0; j < c->H; ++j) {
+      float dot = 0.f;
+      const float* qj = qf + j * DSA_D;
+      for (int d = 0; d < DSA_D; ++d) dot += qj[d] * kf[d];
+      s += w[j] * (dot > 0.f ? dot : 0.f);
+    }
+    out[t] = s;
+  }
+  free(qf);
+}
+
+void oracle_dsa_scores(const uint16_t* q_idx, const float* w_idx, const uint16_t* k_idx,
+                       const int32_t* block_table, const int32_t* seq_lens, int B, int s_q, int H,
+                       int page, int max_blocks, int causal, int smax, float* scores,
+                       int nthreads) {
+  dsa_ctx_t c = {q_idx, k_idx, w_idx, block_table, seq_lens, B, s_q, H, page, max_blocks, causal,
+                 smax, scores};
+  parallel_for((int64_t)B * s_q, nthreads, dsa_scores_task, &c);
+}

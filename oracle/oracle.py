@@ -62,6 +62,8 @@ def lib():
         L.oracle_nhd_index.restype = i64
         L.oracle_mla_ref.argtypes = [p, p, p, p, i, i, i, i, i, f, i, p, p, i]
         L.oracle_mla_ref.restype = None
+        L.oracle_dsa_scores.argtypes = [p, p, p, p, p, i, i, i, i, i, i, i, p, i]
+        L.oracle_dsa_scores.restype = None
         _lib = L
     return _lib
 
@@ -129,6 +131,45 @@ def mla_ref(q, kv_cache, block_table, seq_lens, scale, causal=False, nthreads=No
                          float(scale), int(bool(causal)), _ptr(out), _ptr(lse),
                          nthreads or default_threads())
     return torch.from_numpy(out), torch.from_numpy(lse)
+
+
+def dsa_scores(q_idx, w_idx, k_idx_cache, block_table, seq_lens, causal=False, smax=None,
+               nthreads=None):
+    """Indexer scores (gqa_oracle.c: oracle_dsa_scores): q_idx [B, s_q, H, 128]
+    bf16, w_idx [B, s_q, H] fp32, k_idx_cache [num_blocks, page, 128] bf16 ->
+    [B, s_q, smax] fp32, -inf where the query cannot see the token."""
+    B, s_q, H, D = q_idx.shape
+    assert D == 128
+    page = k_idx_cache.shape[1]
+    sl = _i32(seq_lens)
+    smax = int(smax if smax is not None else max(1, int(sl.max()) if sl.size else 1))
+    qb, kb = _bits(q_idx), _bits(k_idx_cache)
+    w = np.ascontiguousarray(w_idx.detach().cpu().numpy().astype(np.float32))
+    bt = _i32(block_table)
+    out = np.empty((B, s_q, smax), dtype=np.float32)
+    lib().oracle_dsa_scores(_ptr(qb), _ptr(w), _ptr(kb), _ptr(bt), _ptr(sl), B, s_q, H, page,
+                            bt.shape[1], int(bool(causal)), smax, _ptr(out),
+                            nthreads or default_threads())
+    return torch.from_numpy(out)
+
+
+def dsa_topk(scores, k):
+    """Top-k token indices per query row of a [..., S] score array: the k
+    largest finite scores, ties to the lower token index, returned in
+    ascending token order and padded with -1 (numpy restatement of the
+    selection; -inf scores are never selected)."""
+    sc = np.asarray(scores.detach().cpu().numpy() if hasattr(scores, "detach") else scores,
+                    dtype=np.float32)
+    flat = sc.reshape(-1, sc.shape[-1])
+    out = np.full((flat.shape[0], k), -1, dtype=np.int32)
+    idx = np.arange(flat.shape[1])
+    for r, row in enumerate(flat):
+        fin = np.isfinite(row)
+        cand = idx[fin]
+        order = np.lexsort((cand, -row[fin]))[:k]
+        sel = np.sort(cand[order])
+        out[r, :len(sel)] = sel
+    return out.reshape(sc.shape[:-1] + (k,))
 
 
 def online_softmax(scores, values):

@@ -198,3 +198,29 @@ def test_mla_oracle_empty_request():
     out, lse = oracle.mla_ref(q, kv, bt, sl, 0.07)
     assert torch.all(out[0] == 0) and torch.all(torch.isinf(lse[0])) and torch.all(lse[0] < 0)
     assert torch.isfinite(out[1]).all()
+
+
+@pytest.mark.parametrize("S,s_q,causal", [([5, 130, 64], 1, False), ([70, 200], 2, True)])
+def test_dsa_scores_match_torch(S, s_q, causal):
+    q, kv, q_idx, w_idx, k_idx, bt, sl = cases.make_dsa_case(S, s_q, 16, n_idx_heads=8, seed=6)
+    sc = oracle.dsa_scores(q_idx, w_idx, k_idx, bt, sl, causal=causal)
+    page = k_idx.shape[1]
+    for b, Sb in enumerate(S):
+        n = (Sb + page - 1) // page
+        K = k_idx.float()[bt[b, :n].long()].reshape(-1, 128)[:Sb]
+        dots = torch.einsum("ihd,td->iht", q_idx[b].float(), K).clamp_min(0)
+        ref = torch.einsum("ih,iht->it", w_idx[b], dots)
+        for i in range(s_q):
+            vis = Sb - s_q + 1 + i if causal else Sb
+            np.testing.assert_allclose(sc[b, i, :vis].numpy(), ref[i, :vis].numpy(), rtol=1e-4,
+                                       atol=1e-4)
+            assert torch.all(torch.isinf(sc[b, i, vis:]))
+
+
+def test_dsa_topk_ties_order_and_padding():
+    row = np.array([1.0, 3.0, 3.0, -np.inf, 2.0, 3.0, 0.5], dtype=np.float32)
+    # three 3.0 ties: the lower indices win when only two fit
+    assert oracle.dsa_topk(row[None], 2).tolist() == [[1, 2]]
+    assert oracle.dsa_topk(row[None], 4).tolist() == [[1, 2, 4, 5]]
+    # more slots than finite scores: -1 padding, -inf never selected
+    assert oracle.dsa_topk(row[None], 8).tolist() == [[0, 1, 2, 4, 5, 6, -1, -1]]
