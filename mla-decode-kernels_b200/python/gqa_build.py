@@ -25,8 +25,10 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build")
 EXT_NAME = "gqa_decode_ext"
 EXT_PATH = os.path.join(BUILD_DIR, EXT_NAME + ".so")
 
-CU_SOURCES = ["gqa_scan.cu", "gqa_simt.cu", "gqa_api.cu", "gqa_noalloc.cu", "mla_decode.cu"]
+CU_SOURCES = ["gqa_scan.cu", "gqa_simt.cu", "gqa_api.cu", "gqa_noalloc.cu", "mla_decode.cu",
+              "dsa_decode.cu"]
 CU_HEADERS = ["gqa_internal.h", "gqa_ptx.cuh", "umma_ptx.cuh"]
+PUBLIC_HEADERS = ["gqa_decode.h", "mla_decode.h", "dsa_decode.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -53,7 +55,7 @@ def build_lib(force=False, verbose=False, extra_flags=()):
     """Compile the CUDA sources into lib/libgqa_decode_b200.so."""
     srcs = [os.path.join(CSRC_DIR, s) for s in CU_SOURCES]
     deps = srcs + [os.path.join(CSRC_DIR, h) for h in CU_HEADERS]
-    deps += [os.path.join(INCLUDE_DIR, h) for h in ("gqa_decode.h", "mla_decode.h")]
+    deps += [os.path.join(INCLUDE_DIR, h) for h in PUBLIC_HEADERS]
     if not force and not _newer(LIB_PATH, deps):
         return LIB_PATH
     os.makedirs(LIB_DIR, exist_ok=True)
@@ -77,8 +79,7 @@ def preload_lib():
 def build_ext(force=False, verbose=False):
     """Compile python/gqa_decode_ext.cpp against the C ABI into _build/."""
     src = os.path.join(PY_DIR, "gqa_decode_ext.cpp")
-    deps = [src, os.path.join(INCLUDE_DIR, "gqa_decode.h"), os.path.join(INCLUDE_DIR, "mla_decode.h"),
-            LIB_PATH]
+    deps = [src, LIB_PATH] + [os.path.join(INCLUDE_DIR, h) for h in PUBLIC_HEADERS]
     if not force and not _newer(EXT_PATH, deps):
         return EXT_PATH
     preload_lib()

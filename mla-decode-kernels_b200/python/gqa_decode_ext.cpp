@@ -14,6 +14,7 @@
 
 #include "gqa_decode.h"
 #include "mla_decode.h"
+#include "dsa_decode.h"
 
 namespace {
 
@@ -491,6 +492,119 @@ int64_t mla_pick_splits(int64_t B, int64_t s_q, int64_t h_q, int64_t max_pages, 
 
 int64_t mla_get_status(bool clear) { return mla_decode_get_status(clear ? 1 : 0); }
 
+// ---- DSA sparse decode: indexer, top-k, gather (include/dsa_decode.h) --------
+
+void check_paged(const torch::Tensor& t, const char* name, int64_t dim) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous bf16 CUDA tensor");
+  const bool shape4 = t.dim() == 4 && t.size(2) == 1 && t.size(3) == dim;
+  const bool shape3 = t.dim() == 3 && t.size(2) == dim;
+  TORCH_CHECK((shape4 || shape3) && t.size(1) == 64, name, " must be [num_blocks, 64, 1, ", dim,
+              "] or [num_blocks, 64, ", dim, "]");
+}
+
+void check_table(const torch::Tensor& block_table, const torch::Tensor& seq_lens, int64_t B,
+                 const torch::Device& dev) {
+  TORCH_CHECK(block_table.is_cuda() && seq_lens.is_cuda() && block_table.device() == dev &&
+                  seq_lens.device() == dev,
+              "block_table and seq_lens must be CUDA tensors on the query's device");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
+              "block_table and seq_lens must be int32");
+  TORCH_CHECK(block_table.is_contiguous() && seq_lens.is_contiguous(),
+              "block_table and seq_lens must be contiguous");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == B && seq_lens.dim() == 1 &&
+                  seq_lens.size(0) == B,
+              "block_table [B, max_blocks] and seq_lens [B] must match the batch");
+}
+
+// q_idx [B, s_q, H, 128] bf16, w_idx [B, s_q, H] fp32, k_idx [num_blocks, 64, (1,) 128]
+// bf16 -> scores [B, s_q, max_blocks * 64] fp32 (columns past S_b unwritten).
+torch::Tensor dsa_indexer(torch::Tensor q_idx, torch::Tensor w_idx, torch::Tensor k_idx,
+                          torch::Tensor block_table, torch::Tensor seq_lens, bool causal) {
+  TORCH_CHECK(q_idx.is_cuda() && q_idx.scalar_type() == torch::kBFloat16 && q_idx.is_contiguous(),
+              "q_idx must be a contiguous bf16 CUDA tensor");
+  TORCH_CHECK(q_idx.dim() == 4 && q_idx.size(3) == 128, "q_idx must be [B, s_q, H, 128]");
+  const int64_t B = q_idx.size(0), s_q = q_idx.size(1), H = q_idx.size(2);
+  TORCH_CHECK(w_idx.is_cuda() && w_idx.scalar_type() == torch::kFloat32 && w_idx.is_contiguous() &&
+                  w_idx.device() == q_idx.device(),
+              "w_idx must be a contiguous fp32 CUDA tensor on q_idx's device");
+  TORCH_CHECK(w_idx.dim() == 3 && w_idx.size(0) == B && w_idx.size(1) == s_q && w_idx.size(2) == H,
+              "w_idx must be [B, s_q, H]");
+  check_paged(k_idx, "k_idx", 128);
+  TORCH_CHECK(k_idx.device() == q_idx.device(), "k_idx must be on q_idx's device");
+  check_table(block_table, seq_lens, B, q_idx.device());
+  TORCH_CHECK(s_q >= 1 && s_q <= 2 && (s_q * H == 64 || s_q * H == 128),
+              "the indexer takes s_q in {1, 2} and s_q * H in {64, 128}");
+  const c10::cuda::CUDAGuard guard(q_idx.device());
+  const int64_t stride = block_table.size(1) * 64;
+  auto scores = torch::empty({B, s_q, stride}, w_idx.options());
+  check_launch(dsa_indexer_launch(reinterpret_cast<const gqa_bf16*>(q_idx.data_ptr()),
+                                  w_idx.data_ptr<float>(),
+                                  reinterpret_cast<const gqa_bf16*>(k_idx.data_ptr()),
+                                  block_table.data_ptr<int>(), seq_lens.data_ptr<int>(),
+                                  scores.data_ptr<float>(), stride, static_cast<int>(B),
+                                  static_cast<int>(s_q), static_cast<int>(H), 64,
+                                  static_cast<int>(block_table.size(1)),
+                                  static_cast<int>(k_idx.size(0)), causal ? 1 : 0,
+                                  at::cuda::getCurrentCUDAStream()),
+               "dsa_indexer");
+  return scores;
+}
+
+// scores [B, s_q, stride] fp32 -> (indices [B, s_q, k] int32, counts [B, s_q] int32).
+std::vector<torch::Tensor> dsa_topk(torch::Tensor scores, torch::Tensor seq_lens, int64_t k,
+                                    bool causal) {
+  TORCH_CHECK(scores.is_cuda() && scores.scalar_type() == torch::kFloat32 &&
+                  scores.is_contiguous() && scores.dim() == 3,
+              "scores must be a contiguous fp32 CUDA tensor [B, s_q, S]");
+  TORCH_CHECK(seq_lens.is_cuda() && seq_lens.scalar_type() == torch::kInt32 &&
+                  seq_lens.is_contiguous() && seq_lens.dim() == 1 &&
+                  seq_lens.size(0) == scores.size(0) && seq_lens.device() == scores.device(),
+              "seq_lens must be a contiguous int32 CUDA tensor [B] on scores' device");
+  TORCH_CHECK(k >= 1 && k <= (1 << 20), "k must be in [1, 2^20]");
+  const c10::cuda::CUDAGuard guard(scores.device());
+  const int64_t B = scores.size(0), s_q = scores.size(1), S = scores.size(2);
+  auto opts = scores.options().dtype(torch::kInt32);
+  auto indices = torch::empty({B, s_q, k}, opts);
+  auto counts = torch::empty({B, s_q}, opts);
+  check_launch(dsa_topk_launch(scores.data_ptr<float>(), S, seq_lens.data_ptr<int>(),
+                               static_cast<int>(B), static_cast<int>(s_q), static_cast<int>(k),
+                               static_cast<int>(S), causal ? 1 : 0, indices.data_ptr<int>(),
+                               counts.data_ptr<int>(), at::cuda::getCurrentCUDAStream()),
+               "dsa_topk");
+  return {indices, counts};
+}
+
+// kv_cache [num_blocks, 64, 1, 576] bf16, indices [B, s_q, k] int32 ->
+// pages [B * s_q * kpad / 64, 64, 1, 576] bf16, kpad = k rounded up to 64.
+torch::Tensor dsa_gather(torch::Tensor kv_cache, torch::Tensor block_table, torch::Tensor indices) {
+  check_paged(kv_cache, "kv_cache", 576);
+  TORCH_CHECK(indices.is_cuda() && indices.scalar_type() == torch::kInt32 &&
+                  indices.is_contiguous() && indices.dim() == 3 &&
+                  indices.device() == kv_cache.device(),
+              "indices must be a contiguous int32 CUDA tensor [B, s_q, k] on kv_cache's device");
+  TORCH_CHECK(block_table.is_cuda() && block_table.scalar_type() == torch::kInt32 &&
+                  block_table.is_contiguous() && block_table.dim() == 2 &&
+                  block_table.size(0) == indices.size(0) &&
+                  block_table.device() == kv_cache.device(),
+              "block_table must be a contiguous int32 CUDA tensor [B, max_blocks]");
+  const c10::cuda::CUDAGuard guard(kv_cache.device());
+  const int64_t B = indices.size(0), s_q = indices.size(1), k = indices.size(2);
+  const int64_t kpad = (k + 63) / 64 * 64;
+  auto pages = torch::empty({B * s_q * kpad / 64, 64, 1, 576}, kv_cache.options());
+  check_launch(dsa_gather_launch(reinterpret_cast<const gqa_bf16*>(kv_cache.data_ptr()),
+                                 block_table.data_ptr<int>(), indices.data_ptr<int>(),
+                                 static_cast<int>(B), static_cast<int>(s_q), static_cast<int>(k),
+                                 static_cast<int>(block_table.size(1)),
+                                 static_cast<int>(kv_cache.size(0)),
+                                 reinterpret_cast<gqa_bf16*>(pages.data_ptr()),
+                                 at::cuda::getCurrentCUDAStream()),
+               "dsa_gather");
+  return pages;
+}
+
+int64_t dsa_get_status(bool clear) { return dsa_decode_get_status(clear ? 1 : 0); }
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "MLA latent-cache paged decode (tcgen05)", py::arg("q"),
         py::arg("kv_cache"), py::arg("block_table"), py::arg("seq_lens"),
@@ -498,6 +612,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_workspace_bytes", &mla_workspace_bytes, "MLA split workspace bytes");
   m.def("mla_pick_splits", &mla_pick_splits, "MLA split count heuristic");
   m.def("mla_get_status", &mla_get_status, "MLA device status word", py::arg("clear") = false);
+  m.def("dsa_indexer", &dsa_indexer, "DSA lightning-indexer scores (tcgen05)", py::arg("q_idx"),
+        py::arg("w_idx"), py::arg("k_idx"), py::arg("block_table"), py::arg("seq_lens"),
+        py::arg("causal"));
+  m.def("dsa_topk", &dsa_topk, "DSA top-k token selection", py::arg("scores"),
+        py::arg("seq_lens"), py::arg("k"), py::arg("causal"));
+  m.def("dsa_gather", &dsa_gather, "DSA gather of the selected latent rows", py::arg("kv_cache"),
+        py::arg("block_table"), py::arg("indices"));
+  m.def("dsa_get_status", &dsa_get_status, "DSA device status word", py::arg("clear") = false);
   m.def("gqa_decode_v0", &gqa_decode_v0, "GQA decode v0: CUDA-core grouped scan (paged KV, bf16)");
   m.def("gqa_decode_v1", &gqa_decode_v1,
         "GQA decode v1: pipelined TMA + tensor-core scan, unsplit (paged KV, bf16)");

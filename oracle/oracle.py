@@ -172,6 +172,33 @@ def dsa_topk(scores, k):
     return out.reshape(sc.shape[:-1] + (k,))
 
 
+def dsa_sparse_ref(q, kv_cache, block_table, indices, scale, nthreads=None):
+    """Attention of each query position over its selected tokens only:
+    q [B, s_q, h_q, 576] bf16, kv_cache [num_blocks, page, 1, 576] bf16,
+    indices [B, s_q, k] token positions (-1 = none) -> out [B, s_q, h_q, 512]
+    fp32, lse [B, h_q, s_q] fp32.  The selected rows of (b, i) are copied
+    into a one-page cache of their own and decoded by oracle_mla_ref, whose
+    result does not depend on the order of the tokens beyond rounding."""
+    B, s_q, h_q, D = q.shape
+    page = kv_cache.shape[1]
+    idx = _i32(indices).reshape(B * s_q, -1)
+    bt = _i32(block_table)
+    k = idx.shape[1]
+    kv = kv_cache.reshape(-1, 576)
+    rows = torch.zeros((B * s_q, max(k, 1), 1, 576), dtype=kv_cache.dtype)
+    counts = np.zeros(B * s_q, dtype=np.int32)
+    for r in range(B * s_q):
+        sel = idx[r][idx[r] >= 0]
+        b = r // s_q
+        phys = bt[b, sel // page].astype(np.int64) * page + sel % page
+        rows[r, :len(sel), 0] = kv[torch.from_numpy(phys)]
+        counts[r] = len(sel)
+    table = torch.arange(B * s_q, dtype=torch.int32).view(B * s_q, 1)
+    out, lse = mla_ref(q.reshape(B * s_q, 1, h_q, D), rows, table, torch.from_numpy(counts),
+                       scale, causal=False, nthreads=nthreads)
+    return out.view(B, s_q, h_q, 512), lse.view(B, s_q, h_q).permute(0, 2, 1).contiguous()
+
+
 def online_softmax(scores, values):
     s = np.ascontiguousarray(scores, dtype=np.float32)
     v = np.ascontiguousarray(values, dtype=np.float32)

@@ -224,3 +224,24 @@ def test_dsa_topk_ties_order_and_padding():
     assert oracle.dsa_topk(row[None], 4).tolist() == [[1, 2, 4, 5]]
     # more slots than finite scores: -1 padding, -inf never selected
     assert oracle.dsa_topk(row[None], 8).tolist() == [[0, 1, 2, 4, 5, 6, -1, -1]]
+
+
+def test_dsa_sparse_ref_matches_torch():
+    S, s_q, h_q = [90, 3, 200], 2, 16
+    q, kv, q_idx, w_idx, k_idx, bt, sl = cases.make_dsa_case(S, s_q, h_q, n_idx_heads=8, seed=7)
+    sc = oracle.dsa_scores(q_idx, w_idx, k_idx, bt, sl, causal=True)
+    idx = torch.from_numpy(oracle.dsa_topk(sc, 40))
+    scale = 0.05
+    out, lse = oracle.dsa_sparse_ref(q, kv, bt, idx, scale)
+    page = kv.shape[1]
+    for b in range(len(S)):
+        for i in range(s_q):
+            sel = idx[b, i][idx[b, i] >= 0].long()
+            assert len(sel) == min(40, S[b] - s_q + 1 + i)
+            rows = kv[bt[b, sel // page].long(), sel % page, 0].float()
+            s = q[b, i].float() @ rows.T * scale
+            p = torch.softmax(s, -1)
+            np.testing.assert_allclose(out[b, i].numpy(), (p @ rows[:, :512]).numpy(),
+                                       rtol=1e-4, atol=1e-5)
+            np.testing.assert_allclose(lse[b, :, i].numpy(), torch.logsumexp(s, -1).numpy(),
+                                       rtol=1e-5, atol=1e-5)
