@@ -7,7 +7,7 @@ inputs resident in HBM.  KV bytes per step = sum_b S_b * Hkv * 128 * 2 * 2
 traffic is excluded from the metric, as in the reference.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload rep|wide|ragged|long|long_peaked] [--num-splits auto|N]
+                  [--workload rep|wide|ragged|long|long_peaked|mla|dsa] [--num-splits auto|N]
                   [--kernel auto|v0|v1|v2] [--api block_table|csr|csr_replan]
 
 N > 1 runs under torchrun, one rank per GPU.  Workloads (BASELINE.json
@@ -20,6 +20,10 @@ configs; seeded synthetic data, cases.py):
   long         config 5: B=1, S=262144, bs=64, KV range split over the ranks,
                states all-gathered (NCCL) and merged (strong scaling).
   long_peaked  config 5 with K x 8.
+  mla          MLA latent-cache decode (K2), FlashMLA grid: b=128, h_q=128,
+               mean S=8192 (--mla-sq / --mla-hq / --mla-sk / --mla-causal).
+  dsa          sparse decode (K3): indexer + top-k 2048 + gather + MLA over
+               the selected tokens, same grid (--dsa-topk).
 Every input set is larger than the 126 MB L2, so no flush is needed between
 steps.  --impl reference times the CPU restatement of the reference's oracle
 (oracle/, python/reference.py semantics) on the host cores instead.
@@ -69,11 +73,12 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="rep",
-                    choices=["rep", "wide", "ragged", "long", "long_peaked", "mla"])
+                    choices=["rep", "wide", "ragged", "long", "long_peaked", "mla", "dsa"])
     ap.add_argument("--mla-sq", type=int, default=1, help="mla: query tokens per request")
     ap.add_argument("--mla-hq", type=int, default=128, help="mla: query heads")
     ap.add_argument("--mla-sk", type=int, default=8192, help="mla: mean cached tokens")
     ap.add_argument("--mla-causal", action="store_true")
+    ap.add_argument("--dsa-topk", type=int, default=2048, help="dsa: tokens selected per query")
     ap.add_argument("--num-splits", default="auto",
                     help="auto = balanced schedule; an integer = fixed splits (v2)")
     ap.add_argument("--kernel", default="auto", choices=["auto", "v0", "v1", "v2"],
@@ -765,6 +770,169 @@ def run_mla(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_dsa(args, world, rank, local):
+    """DSA-style sparse decode (K3): indexer -> top-k -> gather -> MLA decode
+    over the selected tokens, b = 128 requests per GPU at the MLA grid's cache
+    lengths, DeepSeek-V3.2's indexer shape (64 index heads of 128 dims) and
+    top-k 2048."""
+    import numpy as np
+
+    import cases
+    import dsa_decode
+    import mla_decode
+    import oracle
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import sharding
+
+        sharding.init_process_group("nccl", timeout_s=120)
+    B = args.batch or 128
+    s_q, h_q, topk = args.mla_sq, args.mla_hq, args.dsa_topk
+    n_idx = 64 // s_q
+    causal = args.mla_causal
+    sl = mla_seq_lens(B, args.mla_sk, s_q, seed=rank)
+    case = cases.make_dsa_case(sl, s_q, h_q, n_idx_heads=n_idx, seed=20 + rank, pool_factor=1.0,
+                               poison=False, device=device)
+    q, kv, q_idx, w_idx, k_idx, bt, sl_t = case
+    scale = 1.0 / math.sqrt(192)
+    kpad = (topk + 63) // 64 * 64
+    rows = B * s_q
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    ns = int(mla_decode._ext.mla_pick_splits(rows, 1, h_q, kpad // 64, sms))
+    holder = {}
+
+    def step():
+        holder["o"] = dsa_decode.sparse_decode(q, kv, q_idx, w_idx, k_idx, bt, sl_t, topk, scale,
+                                               causal, ns)
+
+    step()
+    torch.cuda.synchronize()
+    # spot check: selection bit-exact on the GPU's own scores, attention vs the oracle
+    reqs = [0, 1]
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t, causal)
+    sc = scores[reqs].cpu()
+    for j, b in enumerate(reqs):
+        sc[j, :, sl[b]:] = -math.inf
+    out, lse, idx = holder["o"]
+    if not np.array_equal(idx[reqs].cpu().numpy(), oracle.dsa_topk(sc, topk)):
+        raise SystemExit("dsa top-k spot check failed")
+    sub = cases.mla_subset((q, kv, bt, sl_t), reqs)
+    ro, _ = oracle.dsa_sparse_ref(sub[0], sub[1], sub[2], idx[reqs].cpu(), scale)
+    if not torch.allclose(out[reqs].float().cpu(), ro, atol=1e-2, rtol=1e-2):
+        raise SystemExit("dsa attention spot check failed")
+    if dsa_decode.get_status(True) or mla_decode.get_status(True):
+        raise SystemExit("dsa device status set")
+    del scores, sc, out, lse, idx
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    uuids = [str(torch.cuda.get_device_properties(device).uuid)]
+    if world > 1:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, uuids[0])
+        uuids = gathered
+    sampler = ClockSampler(uuids) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    ms = time_loop(step, args.steps, world, stream)
+    clocks = sampler.stop() if sampler else None
+    ms_max = max_over_ranks(ms, world, device)
+    median_us = max_over_ranks(per_step_median_us(step, min(args.steps, 200), stream), world,
+                               device)
+
+    # each stage alone, on the same inputs (stage times sum to about the step)
+    st_scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t, causal)
+    st_idx, st_counts = dsa_decode.dsa_topk(st_scores, sl_t, topk, causal)
+    st_pages = dsa_decode.dsa_gather(kv, bt, st_idx)
+    table = dsa_decode._identity_table(rows, kpad // 64, device)
+    q_rows = q.reshape(rows, 1, h_q, 576)
+    cnt_rows = st_counts.reshape(rows)
+    stages = {
+        "dsa_indexer_kernel": lambda: dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t,
+                                                             causal),
+        "dsa_topk_kernel": lambda: dsa_decode.dsa_topk(st_scores, sl_t, topk, causal),
+        "dsa_gather_kernel": lambda: dsa_decode.dsa_gather(kv, bt, st_idx),
+        "mla_decode_kernel": lambda: mla_decode.mla_decode(q_rows, st_pages, table, cnt_rows,
+                                                           scale, num_splits=ns),
+    }
+    n_stage = max(3, min(args.steps, 200))
+    stage_ms = {}
+    for name, fn in stages.items():
+        for _ in range(3):
+            fn()
+        stage_ms[name] = time_loop(fn, n_stage, 1, stream)
+    counts = st_counts.cpu().to(torch.int64)
+    vis = [[max(0, min(S, S - s_q + 1 + i)) if causal else S for i in range(s_q)] for S in sl]
+    tok_sel = int(counts.sum())
+    sum_S = sum(sl)
+    stage_bytes = {
+        "dsa_indexer_kernel": sum_S * 128 * 2 + rows * n_idx * (128 * 2 + 4) + s_q * sum_S * 4,
+        "dsa_topk_kernel": sum(sum(v) for v in vis) * 4 + rows * topk * 4,
+        "dsa_gather_kernel": tok_sel * 1152 + rows * kpad * 1152 + rows * topk * 4,
+        "mla_decode_kernel": tok_sel * 1152 + rows * h_q * (576 + 512) * 2,
+    }
+    bytes_local = sum(stage_bytes.values())
+    bytes_total = sum_over_ranks(bytes_local, world, device)
+
+    # e2e: q, q_idx, w_idx and the page table up, out back, every step
+    out_buf = torch.empty((B, s_q, h_q, 512), dtype=torch.bfloat16, device=device)
+    e2e = E2ELoop((q, q_idx, w_idx, bt, sl_t), out_buf, stream)
+
+    def decode(q_d, qi_d, w_d, bt_d, sl_d, out_d):
+        o, _, _ = dsa_decode.sparse_decode(q_d, kv, qi_d, w_d, k_idx, bt_d, sl_d, topk, scale,
+                                           causal, ns)
+        out_d.copy_(o)
+    for _ in range(3):
+        e2e.step(decode)
+    e2e.drain()
+    ms_e2e = max_over_ranks(time_loop(lambda: e2e.step(decode), args.steps, world, stream,
+                                      finish=e2e.drain), world, device)
+    if dsa_decode.get_status(True) or mla_decode.get_status(True):
+        raise SystemExit("dsa device status set after timing")
+    if rank != 0:
+        return
+    peak, peak_src = measured_hbm_peak()
+    top = max(stage_ms, key=stage_ms.get)
+    achieved = stage_bytes[top] / (stage_ms[top] * 1e-3) / 1e9
+    value = bytes_total / (ms_max * 1e-3) / 1e9
+    line = {
+        "metric": "DSA sparse decode step: algorithmic GB/s (indexer + top-k + gather + MLA)",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
+        "median_us_per_step": round(median_us, 2),
+        "pct_of_sol": round(100.0 * value / (peak * world), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16, cases.make_dsa_case)",
+        "config": {"workload": f"dsa_b{B}_sq{s_q}_hq{h_q}_sk{args.mla_sk}_topk{topk}", "B": B,
+                   "s_q": s_q, "h_q": h_q, "index_heads": n_idx, "topk": topk,
+                   "mean_seq_len": args.mla_sk,
+                   "seq_lens": "Normal(mean, mean/2) >= s_q, seeded", "page": 64,
+                   "causal": causal, "mla_num_splits": ns, "parallelism": f"dp{world}",
+                   "bytes_per_step": int(bytes_total),
+                   "l2": "index keys + latent cache > 126 MB L2; no flush needed"},
+        "stages_us": {k: round(v * 1e3, 2) for k, v in stage_ms.items()},
+        "stage_bytes": {k: int(v) for k, v in stage_bytes.items()},
+        "e2e": {"value": round(bytes_total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(ms_e2e, 5),
+                "h2d_bytes_per_step": int(e2e.h2d_bytes * world),
+                "d2h_bytes_per_step": int(e2e.d2h_bytes * world),
+                "path": "dsa_decode.sparse_decode -> C ABI dsa_indexer_launch, dsa_topk_launch, "
+                        "dsa_gather_launch, mla_decode_launch; q, q_idx, w_idx, block_table and "
+                        "seq_lens H2D, out D2H every step, double-buffered"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": peak_src, "kernel": top,
+                     "algorithmic_bytes_per_launch": int(stage_bytes[top])},
+        "gpu_launches": int(args.steps * (4 if ns == 1 else 5)),
+        "clocks": clocks, "cpu_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_env()
@@ -776,6 +944,9 @@ def main():
     try:
         if args.workload == "mla":
             run_mla(args, world, rank, local)
+            return
+        if args.workload == "dsa":
+            run_dsa(args, world, rank, local)
             return
         run_ours(args, world, rank, local)
     finally:

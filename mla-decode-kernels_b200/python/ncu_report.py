@@ -290,9 +290,9 @@ def bench_lines(log_path):
 _KEEP = {
     None: ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
            "median_us_per_step", "pct_of_sol", "higher_is_better", "scaling", "vs_baseline",
-           "dtype", "gpu_launches", "unavailable"),
+           "dtype", "gpu_launches", "unavailable", "stages_us"),
     "config": ("workload", "api", "kernel", "num_splits", "exchange", "parallelism",
-               "global_batch", "kv_bytes_per_step", "per_step_sample_requests"),
+               "global_batch", "kv_bytes_per_step", "bytes_per_step", "per_step_sample_requests"),
     "e2e": ("value", "unit", "ms_per_step", "h2d_bytes_per_step", "d2h_bytes_per_step"),
     "roofline": ("bound", "achieved", "peak", "unit", "frac", "traffic", "kernel"),
     "clocks": ("sm_mhz", "sm_max_mhz", "reasons", "samples"),
@@ -396,10 +396,11 @@ def check_bench(stem, lines):
             continue
         if d.get("warmup", 0) < 3:
             raise SanityError(f"{where}: {d.get('warmup')} warm-up steps (3 required)")
-        kv = d.get("config", {}).get("kv_bytes_per_step")
+        cfg = d.get("config", {})
+        kv = cfg.get("kv_bytes_per_step") or cfg.get("bytes_per_step")
         ms = d.get("ms_per_step")
         if kv and ms and not _close(d["value"], kv / (ms * 1e-3) / 1e9, 0.005):
-            raise SanityError(f"{where}: value {d['value']} GB/s but kv_bytes_per_step / "
+            raise SanityError(f"{where}: value {d['value']} GB/s but bytes per step / "
                               f"ms_per_step = {kv / (ms * 1e-3) / 1e9:.2f}")
         e2e = d.get("e2e") or {}
         if kv and e2e.get("ms_per_step") and \
