@@ -161,13 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (t >= 2 && !wait_warp(bar_sfree + 8 * buf, ((t - 2) >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
       if (lane == 0) {
+        // unrolled, descriptors as constant offsets (16-byte units) from two
+        // bases: rebuilding them per MMA roughly doubles the issue cost
+        const uint64_t a0 = umma_smem_desc(sRing + s * kTileBytes, 16, 1024, kSwizzle128);
+        const uint64_t b0 = umma_smem_desc(sQ, 16, 1024, kSwizzle128);
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = i >> 2, kk = i & 3;
-          const uint64_t a = umma_smem_desc(sRing + s * kTileBytes + c * 2 * kBox + kk * 32, 16,
-                                            1024, kSwizzle128);
-          const uint64_t bq = umma_smem_desc(sQ + c * NQ * 128 + kk * 32, 16, 1024, kSwizzle128);
-          umma_bf16_ss(tmem + buf * NQ, a, bq, idesc, i != 0);
+          umma_bf16_ss(tmem + buf * NQ, a0 + static_cast<uint64_t>((c * 2 * kBox + kk * 32) >> 4),
+                       b0 + static_cast<uint64_t>((c * NQ * 128 + kk * 32) >> 4), idesc, i != 0);
         }
         umma_commit(bar_sfull + 8 * buf);
         umma_commit(bar_empty + 8 * s);

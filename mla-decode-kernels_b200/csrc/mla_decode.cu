@@ -51,6 +51,8 @@ __device__ int g_mla_status;
 struct Params {
   CUtensorMap tm_q;   // [rows_total, 576] bf16, box {64, NH}, 128B swizzle
   CUtensorMap tm_kv;  // [num_blocks * 64, 576] bf16, box {64, 64}, 128B swizzle
+  CUtensorMap tm_q_rope;   // the same rows, box {32, NH}, 64B swizzle (128-row groups)
+  CUtensorMap tm_kv_rope;  // the same rows, box {32, 64}, 64B swizzle (128-row groups)
   const int* block_table;
   const int* seq_lens;
   __nv_bfloat16* out;  // [B, s_q, h_q, 512] (num_splits == 1)
@@ -284,13 +286,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
         if (lane == 0) {
-          // latent columns: all four k-steps; rope column: k-steps 2r, 2r+1
-          #pragma unroll 1
+          // latent columns: all four k-steps; rope column: k-steps 2r, 2r+1.
+          // Unrolled, every descriptor a constant offset (16-byte units) from
+          // one base: rebuilding descriptors in a loop roughly doubles the
+          // issue cost of each MMA.
+          const uint64_t a0 = umma_smem_desc(kv, 16, 1024, kSwizzle128);
+          const uint64_t b0 = umma_smem_desc(sQ, 16, 1024, kSwizzle128);
+          const uint64_t rope = static_cast<uint64_t>(4 * static_cast<int>(rank));  // 64 bytes
+          #pragma unroll
           for (int i = 0; i < 18; ++i) {
             const int c = i < 16 ? i >> 2 : 4;
-            const int kk = i < 16 ? i & 3 : 2 * static_cast<int>(rank) + (i - 16);
-            const uint64_t a = umma_smem_desc(kv + c * kColBytes + kk * 32, 16, 1024, kSwizzle128);
-            const uint64_t bq = umma_smem_desc(sQ + c * NH * 128 + kk * 32, 16, 1024, kSwizzle128);
+            const int kk = i < 16 ? i & 3 : i - 16;
+            const uint64_t a = a0 + static_cast<uint64_t>((c * kColBytes + kk * 32) >> 4) +
+                               (i < 16 ? 0ull : rope);
+            const uint64_t bq = b0 + static_cast<uint64_t>((c * NH * 128 + kk * 32) >> 4) +
+                                (i < 16 ? 0ull : rope);
             umma_bf16_ss(tmem + s_col0 + buf * NH, a, bq, idesc_qk, i != 0);
           }
           umma_commit(bar_sfull + 8 * buf);
@@ -301,16 +311,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
           const uint32_t kv = sRing + (pv % kStages_) * G::kStageBytes;
           const uint32_t pb = sP + (pv % G::kNP) * G::kPBytes;
-          #pragma unroll 1
+          const uint64_t a0 = umma_smem_desc(kv, kColBytes, 1024, kSwizzle128);
+          const uint64_t p0 = umma_smem_desc(pb, G::kAtomBytes, 8 * G::kRowB, G::kPLayout);
+          #pragma unroll
           for (int j = 0; j < 2; ++j) {
             #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a = umma_smem_desc(kv + 2 * j * kColBytes + kk * 16 * 128, kColBytes,
-                                                1024, kSwizzle128);
-              const uint64_t bp = umma_smem_desc(pb + kk * 16 * G::kRowB, G::kAtomBytes,
-                                                 8 * G::kRowB, G::kPLayout);
-              umma_bf16_ss(tmem + o_col + j * NH, a, bp, idesc_pv, (pv | kk) != 0);
-            }
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_ss(tmem + o_col + j * NH,
+                           a0 + static_cast<uint64_t>((2 * j * kColBytes + kk * 16 * 128) >> 4),
+                           p0 + static_cast<uint64_t>((kk * 16 * G::kRowB) >> 4), idesc_pv,
+                           (pv | kk) != 0);
           }
           umma_commit(bar_pv + 8 * (pv & 1));
           umma_commit(bar_empty + 8 * (pv % kStages_));
@@ -607,6 +617,497 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // no CTA leaves while its peer may still address its shared memory
 }
 
+// ---- 128-row groups: query rows on the MMA M dimension ------------------------
+//
+// For groups of 128 query rows the roles of the operands flip: the rows are
+// the M = 128 dimension, so every thread of the four softmax warps owns one
+// row of S, P and O (row max, exp2 and the row sum stay in registers), and
+// this CTA's half of Q (256 latent + 32 rope dims) lives in tensor memory as
+// the A operand of the QK MMAs, as does P for the PV MMAs.  A page stage
+// holds only what this CTA multiplies: its four latent boxes and its 32-dim
+// half of the rope box (36 KB): a four-stage ring beside two exchange
+// buffers (the partial-S exchange over distributed shared memory, ~16 bytes
+// per SM cycle each way, is the kernel's throughput limit; double buffering
+// overlaps it with a tile of softmax work).
+//   S_r[128 rows, 64 tok]  = Q_r[128, 288] . C_r[64 tok, 288]^T   (18 MMAs, N = 64)
+//   S = S_0 + S_1 (the partials exchanged over distributed shared memory)
+//   O_r[128 rows, 256 dv] += P[128, 64 tok] . C[64 tok, 256 r .. 256 r + 255]
+//                                                                (4 MMAs, N = 256)
+// Tensor memory: O_r columns 0-255, Q_r 256-399, P 416-447, S 448-511.
+// Q_r arrives by TMA in the last two ring stages, is copied into tensor
+// memory by the softmax warps, and those stages then take pages.
+struct Rows {
+  static constexpr int kRopeBytes = kPage * 64;          // 32 rope dims x 64 tokens
+  static constexpr int kStageBytes = 4 * kColBytes + kRopeBytes;  // 36 KB
+  static constexpr int kStages = 4;
+  static constexpr int kXBytes = 128 * kPage * 4;        // the peer's partial S of a tile
+  static constexpr int kRing = 0;
+  static constexpr int kX = kRing + kStages * kStageBytes;  // two tiles' partials
+  static constexpr int kSmall = kX + 2 * kXBytes;
+  static constexpr int kSmem = kSmall + 256 + 3 * 2 * 128 * 4 + 1024;
+  static constexpr int kThreads = 320;  // producer, MMA, eight softmax warps
+  static constexpr int kQStage = kStages - 2;            // Q_r staged in stages 3-4
+  static constexpr int kQLatBytes = 128 * 128;           // one 64-dim box of 128 rows
+  static constexpr int kQBytes = 4 * kQLatBytes + 128 * 64;  // = 2 stages
+  static constexpr uint32_t kOCol = 0, kQCol = 256, kPCol = 416, kSCol = 448;
+  static_assert(kQBytes == 2 * kStageBytes, "Q staging spans the last two stages");
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
+    mla_decode_rows_kernel(const __grid_constant__ Params p) {
+  using G = Rows;
+  constexpr int kSt = G::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t s_base = smem_u32(smem);
+  const uint32_t sRing = s_base + G::kRing, sX = s_base + G::kX;
+  const uint32_t sQ = sRing + G::kQStage * G::kStageBytes;
+  const uint32_t bars = s_base + G::kSmall;
+  const uint32_t bar_full = bars, bar_empty = bars + 40, bar_sfull = bars + 80,
+                 bar_sfree = bars + 88, bar_pfull = bars + 96, bar_pv = bars + 104,
+                 bar_xfull = bars + 112, bar_xfree = bars + 128, bar_q = bars + 144,
+                 bar_qready = bars + 152, bar_fin = bars + 160;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kSmall + 176);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
+  const int unit = blockIdx.x >> 1;
+  const int hg = unit % p.n_hg;
+  const int sp = (unit / p.n_hg) % p.num_splits;
+  const int b = unit / (p.n_hg * p.num_splits);
+  const int row0 = hg * 128;
+  const int S = max(0, min(p.seq_lens[b], p.max_blocks * kPage));
+  const int pages = (S + kPage - 1) / kPage;
+  const int chunk = (pages + p.num_splits - 1) / p.num_splits;
+  const int pg0 = min(pages, sp * chunk), pg1 = min(pages, pg0 + chunk);
+  const int ntiles = pg1 - pg0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSt; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_sfull, 1);
+    mbar_init(bar_sfree, 8);   // one arrival per softmax warp
+    mbar_init(bar_pfull, 8);
+    mbar_init(bar_pv, 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(bar_xfull + 8 * j, 1);  // armed with the byte count here, bytes from the peer
+      mbar_init(bar_xfree + 8 * j, 8);  // the peer's eight softmax warps have read our partial
+    }
+    mbar_init(bar_q, 1);
+    mbar_init(bar_qready, 8);  // Q_r is in tensor memory and out of the ring
+    mbar_init(bar_fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote access
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int rope_x = 512 + 32 * static_cast<int>(rank);  // this CTA's rope dims
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&p.tm_kv);
+      mbar_arrive_expect_tx(bar_q, G::kQBytes);
+      for (int c = 0; c < 4; ++c)
+        tma_load_2d(sQ + c * G::kQLatBytes, &p.tm_q, 64 * (4 * static_cast<int>(rank) + c),
+                    b * p.rows + row0, bar_q);
+      tma_load_2d(sQ + 4 * G::kQLatBytes, &p.tm_q_rope, rope_x, b * p.rows + row0, bar_q);
+      const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % kSt;
+        bool ok = true;
+        if (t >= kSt)
+          ok = mbar_wait(bar_empty + 8 * s, ((t - kSt) / kSt) & 1);
+        else if (s >= G::kQStage)
+          ok = mbar_wait(bar_qready, 0);  // Q_r has left these stages
+        if (!ok) {
+          raise(kStatusWaitTimeout);
+          break;
+        }
+        int page = __ldg(bt + pg0 + t);
+        if (page < 0 || page >= p.num_blocks) {
+          raise(kStatusBadPage);
+          page = 0;
+        }
+        const uint32_t st = sRing + s * G::kStageBytes;
+        mbar_arrive_expect_tx(bar_full + 8 * s, G::kStageBytes);
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(st + c * kColBytes, &p.tm_kv, 64 * (4 * static_cast<int>(rank) + c),
+                      page * kPage, bar_full + 8 * s);
+        tma_load_2d(st + 4 * kColBytes, &p.tm_kv_rope, rope_x, page * kPage, bar_full + 8 * s);
+        issued = t + 1;
+        // The page kSt tiles ahead into L2: a stage is held from its load
+        // until its PV completes, so the ring alone would expose the full
+        // DRAM latency once per kSt tiles.
+        if (t + kSt < ntiles) {
+          const int pf = __ldg(bt + pg0 + t + kSt);
+          if (pf >= 0 && pf < p.num_blocks) {
+            for (int c = 0; c < 4; ++c)
+              tma_prefetch_2d(&p.tm_kv, 64 * (4 * static_cast<int>(rank) + c), pf * kPage);
+            tma_prefetch_2d(&p.tm_kv_rope, rope_x, pf * kPage);
+          }
+        }
+      }
+      // every issued copy has landed before the CTA may exit
+      if (!mbar_wait(bar_q, 0)) raise(kStatusWaitTimeout);
+      for (int t = max(0, issued - kSt); t < issued; ++t)
+        if (!mbar_wait(bar_full + 8 * (t % kSt), (t / kSt) & 1)) raise(kStatusWaitTimeout);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    constexpr uint32_t idesc_qk = umma_idesc_bf16(128, 64, false, false);
+    constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 256, false, true);
+    bool ok = true;
+    if (ntiles > 0) ok = wait_warp(bar_qready, 0);
+    int qk = 0, pv = 0;
+    unsigned long long idle_since = global_timer_ns();
+    while (ok && pv < ntiles) {
+      int action = 0;  // 1 = PV(pv), 2 = QK(qk)
+      if (lane == 0) {
+        if (pv < qk && mbar_test_wait(bar_pfull, pv & 1)) {
+          action = 1;
+        } else if (qk < ntiles && mbar_test_wait(bar_full + 8 * (qk % kSt), (qk / kSt) & 1) &&
+                   (qk == 0 || mbar_test_wait(bar_sfree, (qk - 1) & 1))) {
+          action = 2;
+        }
+      }
+      action = __shfl_sync(0xffffffffu, action, 0);
+      if (action == 0) {
+        __nanosleep(64);
+        if (global_timer_ns() - idle_since > kWaitLimitNs) ok = false;
+        continue;
+      }
+      idle_since = global_timer_ns();
+      tc_fence_after();
+      if (action == 2) {
+        const uint32_t kv = sRing + (qk % kSt) * G::kStageBytes;
+        // zero the cache rows past the request's end in its last page (they
+        // may hold anything, NaN included): 0 * NaN would poison O
+        const int nv = min(kPage, S - (pg0 + qk) * kPage);
+        if (nv < kPage) {
+          const int zrows = kPage - nv;
+          for (int i = lane; i < 36 * zrows; i += 32) {
+            // 16-byte chunks: 8 per row of each latent box, 4 per rope row
+            const int r = nv + i / 36, k = i % 36;
+            const uint32_t a = k < 32 ? kv + (k >> 3) * kColBytes + r * 128 + (k & 7) * 16
+                                      : kv + 4 * kColBytes + r * 64 + (k - 32) * 16;
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        if (lane == 0) {
+          // latent dims 256 r .. 256 r + 255 (16 k-steps, 128-byte swizzle),
+          // rope dims 512 + 32 r .. (2 k-steps, 64-byte swizzle).  Fully
+          // unrolled with every descriptor a constant offset from two bases
+          // (the start address field counts 16-byte units): a loop that
+          // rebuilds descriptors costs ~90 issue cycles per MMA against ~46.
+          const uint64_t b_lat = umma_smem_desc(kv, 16, 1024, kSwizzle128);
+          const uint64_t b_rope = umma_smem_desc(kv + 4 * kColBytes, 16, 512, kSwizzle64);
+          #pragma unroll
+          for (int i = 0; i < 18; ++i) {
+            const uint64_t bk =
+                i < 16 ? b_lat + static_cast<uint64_t>(((i >> 2) * kColBytes + (i & 3) * 32) >> 4)
+                       : b_rope + static_cast<uint64_t>(((i - 16) * 32) >> 4);
+            umma_bf16_ts(tmem + G::kSCol, tmem + G::kQCol + 8 * i, bk, idesc_qk, i != 0);
+          }
+          umma_commit(bar_sfull);
+        }
+        __syncwarp();
+        ++qk;
+      } else {
+        if (lane == 0) {
+          const uint32_t kv = sRing + (pv % kSt) * G::kStageBytes;
+          const uint64_t bv = umma_smem_desc(kv, kColBytes, 1024, kSwizzle128);
+          #pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16_ts(tmem + G::kOCol, tmem + G::kPCol + 8 * kk,
+                         bv + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_pv,
+                         (pv | kk) != 0);
+          umma_commit(bar_pv);
+          umma_commit(bar_empty + 8 * (pv % kSt));
+        }
+        __syncwarp();
+        ++pv;
+      }
+    }
+    if (!ok) raise(kStatusWaitTimeout);
+    // every MMA this thread issued has completed before TMEM is released
+    if (lane == 0) umma_commit(bar_fin);
+    __syncwarp();
+    if (!wait_warp(bar_fin, 0)) raise(kStatusWaitTimeout);
+  } else {
+    // ------------------------- softmax warps 2..9 ----------------------------
+    // Warp w owns query rows h = 32 (w % 4) + lane (TMEM lane quadrant w % 4)
+    // and token columns 32 hf .. 32 hf + 31 of every tile, hf = (w - 2) / 4;
+    // the two warps of a quadrant agree on each tile's row max through
+    // shared memory.  Every softmax warp runs the same named-barrier
+    // sequence whatever happens (a failed wait only clears `ok`).
+    const int q4 = warp & 3, hf = (warp - 2) >> 2;
+    const int h = 32 * q4 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
+    const int row = row0 + h;
+    const bool valid = row < p.rows;
+    const int vis = valid ? visible(p, S, row) : 0;
+    const uint32_t peer_x = mapa_shared(sX, peer);
+    const uint32_t peer_xfull = mapa_shared(bar_xfull, peer);
+    const uint32_t peer_xfree = mapa_shared(bar_xfree, peer);
+    float* red = reinterpret_cast<float*>(smem + G::kSmall + 256);  // [2 tiles][2 halves][128]
+    bool ok = true;
+    auto wait_pv = [&](int k) {  // completion of PV(k): phase k of bar_pv
+      if (k >= 0 && ok && !wait_warp(bar_pv, k & 1)) ok = false;
+    };
+    auto wait_cluster = [&](uint32_t bar, uint32_t parity) {
+      if (!ok) return;
+      bool done = mbar_try_wait_cluster(bar, parity);
+      if (!done) {
+        const unsigned long long t_start = global_timer_ns();
+        while (!(done = mbar_try_wait_cluster(bar, parity)))
+          if (global_timer_ns() - t_start > kWaitLimitNs) break;
+      }
+      if (!__all_sync(0xffffffffu, done)) ok = false;
+    };
+    // Q_r row h: staged (swizzled) in the ring -> tensor memory columns
+    // kQCol.. (two bf16 per column); padding rows are zero.  Chunks j of 16
+    // columns: 0-4 by the first warp of the quadrant, 5-8 by the second.
+    if (ntiles > 0) {
+      if (ok && !wait_warp(bar_q, 0)) ok = false;
+      #pragma unroll 1
+      for (int j = 5 * hf; j < (hf ? 9 : 5); ++j) {
+        uint32_t r[16];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (valid) {
+            // j < 8: latent box j / 2, 16-byte chunks 4 (j % 2) + k of the
+            // 128-byte row (swizzle: chunk ^ (h & 7)); j = 8: the 64-byte
+            // rope row (swizzle: chunk ^ ((h >> 1) & 3))
+            const uint32_t a =
+                j < 8 ? sQ + (j >> 1) * G::kQLatBytes + h * 128 +
+                            (((4 * (j & 1) + k) ^ (h & 7)) << 4)
+                      : sQ + 4 * G::kQLatBytes + h * 64 + ((k ^ ((h >> 1) & 3)) << 4);
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                         : "r"(a));
+          }
+          r[4 * k] = v.x;
+          r[4 * k + 1] = v.y;
+          r[4 * k + 2] = v.z;
+          r[4 * k + 3] = v.w;
+        }
+        tmem_st16(tmem + lane_base + G::kQCol + 16 * j, r);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();  // our reads precede the TMA writes into these stages
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_qready);
+    }
+    // Software pipeline over tiles: iteration t reads S(t + 1) (freeing it
+    // for QK(t + 2)) and sends it to the peer before the softmax of tile t,
+    // whose partial the peer sent one iteration earlier, so the exchange
+    // overlaps a tile of softmax work.  Partials of tiles t and t + 1 sit in
+    // the two exchange buffers X[t & 1], each [16][128] 16-byte chunks (4
+    // tokens of one row): conflict-free for the writes and the reads.
+    auto read_s = [&](int t, float (&x)[32]) {
+      if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
+      tc_fence_after();
+      uint32_t r[2][16];
+      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf, r[0]);
+      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf + 16, r[1]);
+      tmem_wait_ld();
+      #pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        x[k] = __uint_as_float(r[0][k]);
+        x[16 + k] = __uint_as_float(r[1][k]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree);
+    };
+    auto send = [&](int t, const float (&x)[32]) {
+      const int j = t & 1;
+      if (t >= 2) wait_cluster(bar_xfree + 8 * j, ((t - 2) >> 1) & 1);
+      #pragma unroll
+      for (int g = 0; g < 8; ++g)
+        st_async_v4(peer_x + j * G::kXBytes + ((8 * hf + g) * 128 + h) * 16,
+                    __float_as_uint(x[4 * g]), __float_as_uint(x[4 * g + 1]),
+                    __float_as_uint(x[4 * g + 2]), __float_as_uint(x[4 * g + 3]),
+                    peer_xfull + 8 * j);
+    };
+    float m_ref = -INFINITY, l = 0.f;
+    float xn[32];
+    if (ntiles > 0) {
+      if (warp == 2 && lane == 0) {
+        mbar_arrive_expect_tx(bar_xfull, G::kXBytes);
+        if (ntiles > 1) mbar_arrive_expect_tx(bar_xfull + 8, G::kXBytes);
+      }
+      read_s(0, xn);
+      send(0, xn);
+    }
+    for (int t = 0; t < ntiles; ++t) {
+      float x[32];
+      #pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = xn[k];
+      if (t + 1 < ntiles) {
+        read_s(t + 1, xn);
+        send(t + 1, xn);
+      }
+      const int j = t & 1;
+      wait_cluster(bar_xfull + 8 * j, (t >> 1) & 1);
+      uint32_t dep = 0;
+      #pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        float4 o;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                     : "r"(sX + j * G::kXBytes + ((8 * hf + g) * 128 + h) * 16)
+                     : "memory");
+        // S_0 + S_1 in both CTAs (addition commutes: identical bits)
+        x[4 * g] += o.x;
+        x[4 * g + 1] += o.y;
+        x[4 * g + 2] += o.z;
+        x[4 * g + 3] += o.w;
+        dep ^= __float_as_uint(o.x) ^ __float_as_uint(o.w);
+      }
+      // every lane's reads are complete once all lanes produced dep; then the
+      // peer may overwrite the buffer (with tile t + 2, armed here)
+      dep = __reduce_xor_sync(0xffffffffu, dep);
+      if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree + 8 * j, dep);
+      if (warp == 2 && lane == 0 && t + 2 < ntiles)
+        mbar_arrive_expect_tx(bar_xfull + 8 * j, G::kXBytes);
+      // scores in the log2 domain, masked past the row's visible range
+      const int nvis = min(32, max(0, vis - (pg0 + t) * kPage - 32 * hf));
+      float mt = -INFINITY;
+      #pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        x[k] = k < nvis ? x[k] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, x[k]);
+      }
+      // the row max over both halves of the tile
+      red[(j * 2 + hf) * 128 + h] = mt;
+      named_bar_sync(1 + q4, 64);
+      mt = fmaxf(mt, red[(j * 2 + (hf ^ 1)) * 128 + h]);
+      const bool need = mt > m_ref + kRescaleLog2;
+      if (__any_sync(0xffffffffu, need)) {
+        float alpha = 1.f;
+        if (need) {
+          alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
+          m_ref = mt;
+          l *= alpha;
+        }
+        if (t >= 1) {
+          // this warp's 128 of the row's O columns *= alpha once every
+          // earlier PV has accumulated into them
+          wait_pv(t - 1);
+          tc_fence_after();
+          #pragma unroll 1
+          for (int c = 0; c < 8; ++c) {
+            uint32_t r[16];
+            const uint32_t a = tmem + lane_base + G::kOCol + 128 * hf + 16 * c;
+            tmem_ld16(a, r);
+            tmem_wait_ld();
+            #pragma unroll
+            for (int k = 0; k < 16; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha);
+            tmem_st16(a, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P = 2^(x - m_ref) as bf16 pairs; the buffer is free once PV(t - 1) is done
+      uint32_t pk[16];
+      #pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float p0 = x[2 * k] == -INFINITY ? 0.f : fast_exp2(x[2 * k] - m_ref);
+        const float p1 = x[2 * k + 1] == -INFINITY ? 0.f : fast_exp2(x[2 * k + 1] - m_ref);
+        l += p0 + p1;
+        pk[k] = pack2(p0, p1);
+      }
+      wait_pv(t - 1);
+      tc_fence_after();
+      tmem_st16(tmem + lane_base + G::kPCol + 16 * hf, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_pfull);
+    }
+    // the peer has read our last two partials before either CTA may exit
+    for (int t = max(0, ntiles - 2); t < ntiles; ++t)
+      wait_cluster(bar_xfree + 8 * (t & 1), (t >> 1) & 1);
+    // ------------------------------ epilogue ---------------------------------
+    wait_pv(ntiles - 1);
+    tc_fence_after();
+    if (!ok) raise(kStatusWaitTimeout);
+    // the row sum over both halves
+    red[(2 * 2 + hf) * 128 + h] = l;
+    named_bar_sync(1 + q4, 64);
+    l += red[(2 * 2 + (hf ^ 1)) * 128 + h];
+    const bool final_out = p.num_splits == 1;
+    const int dv0 = 256 * static_cast<int>(rank) + 128 * hf;
+    const size_t grow = static_cast<size_t>(b) * p.rows + (valid ? row : 0);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    #pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t r[16];
+      if (ntiles > 0) {
+        tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * c, r);
+        tmem_wait_ld();
+      } else {
+        #pragma unroll
+        for (int k = 0; k < 16; ++k) r[k] = 0u;
+      }
+      if (!valid) continue;
+      if (final_out) {
+        uint4* dst = reinterpret_cast<uint4*>(p.out + grow * kDV + dv0 + 16 * c);
+        uint32_t w[8];
+        #pragma unroll
+        for (int k = 0; k < 8; ++k)
+          w[k] = pack2(__uint_as_float(r[2 * k]) * inv, __uint_as_float(r[2 * k + 1]) * inv);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else {
+        float4* dst = reinterpret_cast<float4*>(p.part_acc + (grow * p.num_splits + sp) * kDV +
+                                                dv0 + 16 * c);
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+          dst[k] = l > 0.f ? make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
+                                         __uint_as_float(r[4 * k + 2]),
+                                         __uint_as_float(r[4 * k + 3]))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (rank == 0 && hf == 0 && valid) {
+      const float m = l > 0.f ? m_ref : -INFINITY;
+      if (final_out) {
+        const int i = row / p.h_q, hq = row % p.h_q;
+        p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + i] =
+            l > 0.f ? (m + log2f(l)) * 0.69314718056f : -INFINITY;
+      } else {
+        p.part_m[grow * p.num_splits + sp] = m;
+        p.part_l[grow * p.num_splits + sp] = l;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  cluster_sync();  // no CTA leaves while its peer may still address its shared memory
+}
+
 // Merge of the num_splits partial states of every (request, query row):
 // one warp per row, lane = 16 of the 512 value dims; writes out and lse.
 struct CombineParams {
@@ -691,15 +1192,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D bf16 tensor map over rows of 576 elements (1152 bytes), box 64 x box_rows,
 // 128-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows) {
+bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint32_t box_rows,
+              uint32_t box_cols = 64) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD) * 2};
-  cuuint32_t box[2] = {64u, box_rows};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1u, 1u};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -792,6 +1295,10 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   if (!make_map(&p.tm_q, q, static_cast<uint64_t>(B) * rows, static_cast<uint32_t>(L.NH)) ||
       !make_map(&p.tm_kv, kv_cache, static_cast<uint64_t>(num_blocks) * kPage, kPage))
     return cudaErrorInvalidValue;
+  if (L.NH == 128 &&
+      (!make_map(&p.tm_q_rope, q, static_cast<uint64_t>(B) * rows, 128u, 32u) ||
+       !make_map(&p.tm_kv_rope, kv_cache, static_cast<uint64_t>(num_blocks) * kPage, kPage, 32u)))
+    return cudaErrorInvalidValue;
   p.block_table = block_table;
   p.seq_lens = seq_lens;
   p.out = out;
@@ -820,7 +1327,7 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    const cudaError_t e[4] = {
+    const cudaError_t e[5] = {
         cudaFuncSetAttribute(mla_decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<16>::kSmem),
         cudaFuncSetAttribute(mla_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -828,7 +1335,9 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
         cudaFuncSetAttribute(mla_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<64>::kSmem),
         cudaFuncSetAttribute(mla_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Pair<128>::kSmem)};
+                             Pair<128>::kSmem),
+        cudaFuncSetAttribute(mla_decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Rows::kSmem)};
     for (cudaError_t x : e)
       if (x != cudaSuccess) attr_err = x;
   });
@@ -837,7 +1346,7 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   const unsigned g = static_cast<unsigned>(grid);
   if (L.NH == 128)
-    mla_decode_kernel<128><<<g, kThreads, L.smem, stream>>>(p);
+    mla_decode_rows_kernel<<<g, Rows::kThreads, Rows::kSmem, stream>>>(p);
   else if (L.NH == 64)
     mla_decode_kernel<64><<<g, kThreads, L.smem, stream>>>(p);
   else if (L.NH == 32)

@@ -111,6 +111,19 @@ __device__ __forceinline__ void umma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, u
       : "memory");
 }
 
+// D[tmem] = A * B (+ D), A read from tensor memory (M rows in lanes 0..M-1,
+// K-major: two bf16 per 32-bit column, the lower K index in the low half),
+// B from shared memory.  Issued by one thread.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (count one) on the mbarrier once every tcgen05.mma this thread has
 // issued so far has completed.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -130,6 +143,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(tmap), "r"(x), "r"(y), "r"(bar)
       : "memory");
+}
+
+// Prefetch of a 2-D tile of a tensor map into L2 (no shared memory, no
+// completion): a later tma_load_2d of the same tile then reads L2.
+__device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(tmap),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
