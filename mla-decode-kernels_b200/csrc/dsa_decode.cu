@@ -52,22 +52,31 @@ struct IndexerParams {
   const int* seq_lens;
   float* scores;     // [B, s_q, stride]
   long long stride;
-  int B, s_q, H, max_blocks, num_blocks, causal, num_splits;
+  int B, s_q, H, max_blocks, num_blocks, causal;
 };
 
-// Smem: Q (two 64-dim columns of NQ rows), 4-stage ring of 128-token tiles
-// laid out column-major (column c: page A rows 0-63, page B rows 64-127),
-// weights, barriers.
+constexpr int kMaxBatch = 4096;  // requests per launch (the host splits larger batches)
+
+// Smem: two Q buffers (two 64-dim columns of NQ rows each: a CTA's range of
+// tiles can span requests, and the next request's Q loads while the last
+// tiles of the current one are multiplied), a 4-stage ring of 128-token
+// tiles laid out column-major (column c: page A rows 0-63, page B rows
+// 64-127), the per-request weights, the tile prefix over the batch, barriers.
 template <int NQ>
 struct IdxGeom {
   static constexpr int kQBytes = 2 * NQ * 128;
-  static constexpr int kRing = kQBytes;
+  static constexpr int kRing = 2 * kQBytes;
   static constexpr int kW = kRing + kStages * kTileBytes;
-  static constexpr int kSmall = kW + NQ * 4;
+  static constexpr int kPrefix = kW + NQ * 4;
+  static constexpr int kSmall = (kPrefix + (kMaxBatch + 1) * 4 + 15) / 16 * 16;
   static constexpr int kSmem = kSmall + 256 + 1024;
   static constexpr uint32_t kTmemCols = 2 * NQ;  // S^T double buffer
+  static_assert(kSmem <= 232448, "shared memory");
 };
 
+// Persistent: one CTA per SM, and CTA c takes tiles [c T / G, (c + 1) T / G)
+// of the batch's T 128-token tiles (request by request), so every SM scans
+// the same number of index keys whatever the length distribution.
 template <int NQ>
 __global__ void __launch_bounds__(kThreads, 1)
     dsa_indexer_kernel(const __grid_constant__ IndexerParams p) {
@@ -78,29 +87,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s_base = smem_u32(smem);
   const uint32_t sQ = s_base, sRing = s_base + G::kRing;
   float* w_s = reinterpret_cast<float*>(smem + G::kW);
+  int* tstart = reinterpret_cast<int*>(smem + G::kPrefix);  // [B + 1] first tile of each request
   const uint32_t bars = s_base + G::kSmall;
-  const uint32_t bar_q = bars, bar_full = bars + 8, bar_empty = bars + 40, bar_sfull = bars + 72,
-                 bar_sfree = bars + 88, bar_fin = bars + 104;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kSmall + 112);
+  const uint32_t bar_q = bars, bar_qfree = bars + 16, bar_full = bars + 32, bar_empty = bars + 64,
+                 bar_sfull = bars + 96, bar_sfree = bars + 112, bar_fin = bars + 128;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kSmall + 144);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.x / p.num_splits, sp = blockIdx.x % p.num_splits;
-  const int S = max(0, min(p.seq_lens[b], p.max_blocks * kPage));
-  const int tiles = (S + kTile - 1) / kTile;
-  const int chunk = (tiles + p.num_splits - 1) / p.num_splits;
-  const int tl0 = min(tiles, sp * chunk), tl1 = min(tiles, tl0 + chunk);
-  const int ntiles = tl1 - tl0;
-  const int pages = (S + kPage - 1) / kPage;
-
+  const int max_tokens = p.max_blocks * kPage;
+  // tile prefix over the batch (block-wide scan in chunks of blockDim)
+  {
+    __shared__ int carry_s;
+    __shared__ int wsum[kThreads / 32];
+    if (threadIdx.x == 0) carry_s = 0;
+    __syncthreads();
+    for (int base = 0; base < p.B; base += blockDim.x) {
+      const int b = base + threadIdx.x;
+      const int S = b < p.B ? max(0, min(p.seq_lens[b], max_tokens)) : 0;
+      const int n = (S + kTile - 1) / kTile;
+      int x = n;
+      #pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+      }
+      if (lane == 31) wsum[warp] = x;
+      __syncthreads();
+      int before = carry_s;
+      for (int w2 = 0; w2 < warp; ++w2) before += wsum[w2];
+      if (b < p.B) tstart[b] = before + x - n;
+      __syncthreads();
+      if (threadIdx.x == blockDim.x - 1) carry_s = before + x;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) tstart[p.B] = carry_s;
+  }
   if (threadIdx.x == 0) {
-    mbar_init(bar_q, 1);
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(bar_q + 8 * j, 1);
+      mbar_init(bar_qfree + 8 * j, 1);
+      mbar_init(bar_sfull + 8 * j, 1);
+      mbar_init(bar_sfree + 8 * j, 4);  // one arrival per epilogue warp
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar_sfull + 8 * s, 1);
-      mbar_init(bar_sfree + 8 * s, 4);  // one arrival per epilogue warp
     }
     mbar_init(bar_fin, 1);
     fence_mbar_init();
@@ -109,29 +140,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
     tmem_relinquish();
   }
-  for (int e = threadIdx.x; e < NQ; e += blockDim.x)
-    w_s[e] = e < p.s_q * p.H ? p.w[static_cast<size_t>(b) * p.s_q * p.H + e] : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const long long T = tstart[p.B];
+  const int g0 = static_cast<int>(T * blockIdx.x / gridDim.x);
+  const int g1 = static_cast<int>(T * (blockIdx.x + 1) / gridDim.x);
+  const int ntiles = g1 - g0;
+  // every role walks the same tiles: request b of global tile g
+  auto req_of = [&](int g, int b) {
+    while (b + 1 < p.B && tstart[b + 1] <= g) ++b;
+    return b;
+  };
+  int b_first = 0;
+  if (ntiles > 0) {  // binary search for the request of the first tile
+    int lo = 0, hi = p.B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tstart[mid] <= g0) lo = mid;
+      else hi = mid - 1;
+    }
+    b_first = lo;
+  }
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && ntiles > 0) {
-      mbar_arrive_expect_tx(bar_q, static_cast<uint32_t>(G::kQBytes));
-      for (int c = 0; c < 2; ++c)
-        tma_load_2d(sQ + c * NQ * 128, &p.tm_q, 64 * c, b * p.s_q * p.H, bar_q);
-      const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
-      int issued = 0;
+      int b = b_first, ord = -1, prev = -1, issued = 0;
       for (int t = 0; t < ntiles; ++t) {
+        const int g = g0 + t;
+        b = req_of(g, b);
+        if (b != prev) {  // Q of request b into buffer ord & 1
+          ++ord;
+          prev = b;
+          const int qb = ord & 1;
+          if (ord >= 2 && !mbar_wait(bar_qfree + 8 * qb, ((ord - 2) >> 1) & 1)) {
+            raise(1);
+            break;
+          }
+          mbar_arrive_expect_tx(bar_q + 8 * qb, static_cast<uint32_t>(G::kQBytes));
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d(sQ + qb * G::kQBytes + c * NQ * 128, &p.tm_q, 64 * c, b * p.s_q * p.H,
+                        bar_q + 8 * qb);
+        }
         const int s = t % kStages;
         if (t >= kStages && !mbar_wait(bar_empty + 8 * s, ((t - kStages) / kStages) & 1)) {
           raise(1);
           break;
         }
-        const int pg = 2 * (tl0 + t);
+        const int S = max(0, min(p.seq_lens[b], max_tokens));
+        const int pages = (S + kPage - 1) / kPage;
+        const int pg = 2 * (g - tstart[b]);
         const int npg = min(2, pages - pg);  // the second page may not exist
+        const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
         mbar_arrive_expect_tx(bar_full + 8 * s, static_cast<uint32_t>(npg * 2 * kBox));
         for (int h = 0; h < npg; ++h) {
           int page = __ldg(bt + pg + h);
@@ -146,7 +208,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = t + 1;
       }
       // every issued copy has landed before the CTA may exit
-      if (!mbar_wait(bar_q, 0)) raise(1);
+      for (int o = max(0, ord - 1); o <= ord; ++o)
+        if (!mbar_wait(bar_q + 8 * (o & 1), (o >> 1) & 1)) raise(1);
       for (int t = max(0, issued - kStages); t < issued; ++t)
         if (!mbar_wait(bar_full + 8 * (t % kStages), (t / kStages) & 1)) raise(1);
     }
@@ -154,17 +217,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ MMA issuer --------------------------------
     constexpr uint32_t idesc = umma_idesc_bf16(128, NQ, false, false);
     bool ok = true;
-    if (ntiles > 0) ok = wait_warp(bar_q, 0);
+    int b = b_first, ord = -1, prev = -1;
     for (int t = 0; t < ntiles && ok; ++t) {
+      const int g = g0 + t;
+      b = req_of(g, b);
+      if (b != prev) {
+        ++ord;
+        prev = b;
+        if (!wait_warp(bar_q + 8 * (ord & 1), (ord >> 1) & 1)) { ok = false; break; }
+      }
+      const int qb = ord & 1;
       const int s = t % kStages, buf = t & 1;
       if (!wait_warp(bar_full + 8 * s, (t / kStages) & 1)) { ok = false; break; }
       if (t >= 2 && !wait_warp(bar_sfree + 8 * buf, ((t - 2) >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
+      // the request's last tile of this CTA releases its Q buffer
+      const bool last_of_req = t + 1 == ntiles || tstart[b + 1] <= g + 1;
       if (lane == 0) {
         // unrolled, descriptors as constant offsets (16-byte units) from two
         // bases: rebuilding them per MMA roughly doubles the issue cost
         const uint64_t a0 = umma_smem_desc(sRing + s * kTileBytes, 16, 1024, kSwizzle128);
-        const uint64_t b0 = umma_smem_desc(sQ, 16, 1024, kSwizzle128);
+        const uint64_t b0 = umma_smem_desc(sQ + qb * G::kQBytes, 16, 1024, kSwizzle128);
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int c = i >> 2, kk = i & 3;
@@ -173,6 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(bar_sfull + 8 * buf);
         umma_commit(bar_empty + 8 * s);
+        if (last_of_req) umma_commit(bar_qfree + 8 * qb);
       }
       __syncwarp();
     }
@@ -186,12 +260,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tq = warp & 3;
     const uint32_t lane_base = static_cast<uint32_t>(32 * tq) << 16;
     const int row = 32 * tq + lane;  // token within the tile
+    const int et = threadIdx.x - 64;  // 0..127
     bool ok = true;
+    int b = b_first, prev = -1, S = 0;
     for (int t = 0; t < ntiles; ++t) {
+      const int g = g0 + t;
+      b = req_of(g, b);
+      if (b != prev) {  // the request's head weights
+        prev = b;
+        S = max(0, min(p.seq_lens[b], max_tokens));
+        named_bar_sync(1, 128);
+        for (int e = et; e < NQ; e += 128)
+          w_s[e] = e < p.s_q * p.H ? p.w[static_cast<size_t>(b) * p.s_q * p.H + e] : 0.f;
+        named_bar_sync(1, 128);
+      }
       const int buf = t & 1;
       if (ok && !wait_warp(bar_sfull + 8 * buf, (t >> 1) & 1)) ok = false;
       tc_fence_after();
-      const int tok = (tl0 + t) * kTile + row;
+      const int tok = (g - tstart[b]) * kTile + row;
       float acc[2] = {0.f, 0.f};  // per query position (s_q <= 2)
       #pragma unroll
       for (int c16 = 0; c16 < NQ / 16; ++c16) {
@@ -248,40 +334,25 @@ struct TopkParams {
 };
 
 constexpr int kTopkThreads = 1024;
+constexpr int kTopkSmemKeys = 40 * 1024;  // rows up to this many tokens keep their keys in smem
+constexpr int kHistStride = 257;          // per-warp histogram row (padded against bank overlap)
 
-// Inclusive block scan of one int per thread; also returns the block total.
-// Every thread of the block must call it.
-__device__ __forceinline__ int block_scan(int v, int* sh, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-  #pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, off);
-    if (lane >= off) x += y;
-  }
-  if (lane == 31) sh[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int s = sh[lane];
-    #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, s, off);
-      if (lane >= off) s += y;
-    }
-    sh[lane] = s;
-  }
-  __syncthreads();
-  const int r = x + (warp > 0 ? sh[warp - 1] : 0);
-  *total = sh[31];
-  __syncthreads();
-  return r;
-}
-
+// One CTA per query row.  Keys (order-preserving integers of the scores) are
+// visited in chunks of 1024 tokens, token c * 1024 + tid by thread tid, so
+// every pass reads them coalesced.  Four 8-bit radix passes find the k-th
+// largest key T and how many keys equal to T to take: each warp counts into
+// its own histogram, a thread adds runs of equal digits before touching it
+// (the leading digits of similar scores coincide), and one warp turns the
+// 256 bins into the next digit with a parallel scan.  The selection is then
+// written in token order by ballots over the same chunks, with the chunk x
+// warp offsets scanned by one warp (two block barriers per 32 chunks).
+template <bool kSmemKeys>
 __global__ void __launch_bounds__(kTopkThreads) dsa_topk_kernel(const __grid_constant__ TopkParams p) {
-  __shared__ int hist[256];
-  __shared__ int sh[32];
+  extern __shared__ uint32_t keys[];
+  __shared__ int hw[32 * kHistStride];
+  __shared__ int offs[32 * 32];  // [chunk][warp] counts, then exclusive offsets
   __shared__ uint32_t sh_prefix;
-  __shared__ int sh_need;
+  __shared__ int sh_need, sh_eq, sh_total;
   const int r = blockIdx.x;  // (b, i)
   const int b = r / p.s_q, i = r % p.s_q;
   const int S = max(0, min(p.seq_lens[b], p.max_tokens));
@@ -289,55 +360,159 @@ __global__ void __launch_bounds__(kTopkThreads) dsa_topk_kernel(const __grid_con
   const float* sc = p.scores + static_cast<size_t>(r) * p.stride;
   int* out = p.indices + static_cast<size_t>(r) * p.k;
   const int k = p.k;
-  if (p.counts && threadIdx.x == 0) p.counts[r] = min(k, vis);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (p.counts && tid == 0) p.counts[r] = min(k, vis);
   if (vis <= k) {  // every visible token is selected
-    for (int e = threadIdx.x; e < k; e += blockDim.x) out[e] = e < vis ? e : -1;
+    for (int e = tid; e < k; e += blockDim.x) out[e] = e < vis ? e : -1;
     return;
   }
-  // radix select of the k-th largest key, 8 bits per pass from the top
+  if (kSmemKeys) {
+    for (int t = tid; t < vis; t += blockDim.x) keys[t] = order_key(sc[t]);
+  }
+  auto key_at = [&](int t) -> uint32_t { return kSmemKeys ? keys[t] : order_key(sc[t]); };
+  const int nch = (vis + blockDim.x - 1) / blockDim.x;
+  // ---- radix select of the k-th largest key, 8 bits per pass from the top
   uint32_t prefix = 0, pmask = 0;
-  int need = k;  // keys still to take at or below the current prefix
+  int need = k, eq_total = 0;  // keys still to take at or below the current prefix
+  int* hist = hw;              // bins after the per-warp reduction (row 0)
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int e = threadIdx.x; e < 256; e += blockDim.x) hist[e] = 0;
+    for (int e = tid; e < 32 * kHistStride; e += blockDim.x) hw[e] = 0;
     __syncthreads();
-    for (int t = threadIdx.x; t < vis; t += blockDim.x) {
-      const uint32_t key = order_key(sc[t]);
-      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1);
+    int run_d = -1, run_n = 0;
+    for (int c = 0; c < nch; ++c) {
+      const int t = c * blockDim.x + tid;
+      if (t < vis) {
+        const uint32_t key = key_at(t);
+        if ((key & pmask) == prefix) {
+          const int d = static_cast<int>((key >> shift) & 255u);
+          if (d != run_d) {
+            if (run_n) atomicAdd(&hw[warp * kHistStride + run_d], run_n);
+            run_d = d;
+            run_n = 0;
+          }
+          ++run_n;
+        }
+      }
+    }
+    if (run_n) atomicAdd(&hw[warp * kHistStride + run_d], run_n);
+    __syncthreads();
+    int bin_sum = 0;
+    if (tid < 256) {
+      #pragma unroll 8
+      for (int w = 0; w < 32; ++w) bin_sum += hw[w * kHistStride + tid];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int above = 0, dig = 255;
-      for (; dig > 0; --dig) {
-        if (above + hist[dig] >= need) break;
-        above += hist[dig];
+    if (tid < 256) hist[tid] = bin_sum;
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255 - 8 l down to 248 - 8 l (descending digits)
+      int c8[8], local = 0;
+      #pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c8[j] = hist[255 - 8 * lane - j];
+        local += c8[j];
       }
-      sh_prefix = prefix | (static_cast<uint32_t>(dig) << shift);
-      sh_need = need - above;
+      int incl = local;
+      #pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      const int above = incl - local;  // keys in the bins above this lane's
+      if (above < need && need <= incl) {
+        int a = above, j = 0;
+        for (; j < 7; ++j) {
+          if (a + c8[j] >= need) break;
+          a += c8[j];
+        }
+        const int dig = 255 - 8 * lane - j;
+        sh_prefix = prefix | (static_cast<uint32_t>(dig) << shift);
+        sh_need = need - a;
+        sh_eq = c8[j];
+      }
     }
     __syncthreads();
     prefix = sh_prefix;
     need = sh_need;
+    eq_total = sh_eq;
     pmask |= 255u << shift;
+  }
+  // ---- ordered compaction: every key > T and the first `need` keys == T
+  const uint32_t T = prefix;
+  const bool all_ties = need == eq_total;  // block-uniform
+  const unsigned lt = (1u << lane) - 1u;
+  int sel_base = 0, eq_base = 0;
+  // one warp turns the [chunk][warp] counts of up to 32 chunks into exclusive
+  // offsets (chunk-major, token order) and the running total
+  auto scan_offsets = [&](int nc, int base) {
     __syncthreads();
+    if (warp == 0) {
+      int v[32], local = 0;
+      #pragma unroll
+      for (int w = 0; w < 32; ++w) {
+        v[w] = lane < nc ? offs[lane * 32 + w] : 0;
+        local += v[w];
+      }
+      int incl = local;
+      #pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      int run = base + incl - local;
+      if (lane < nc) {
+        #pragma unroll
+        for (int w = 0; w < 32; ++w) {
+          offs[lane * 32 + w] = run;
+          run += v[w];
+        }
+      }
+      if (lane == 31) sh_total = base + incl;
+    }
+    __syncthreads();
+  };
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const int nc = min(32, nch - c0);
+    uint32_t eq_bits = 0, gt_bits = 0;  // this thread's keys of the super-chunk
+    for (int c = 0; c < nc; ++c) {
+      const int t = (c0 + c) * blockDim.x + tid;
+      const uint32_t key = t < vis ? key_at(t) : 0u;
+      if (t < vis && key > T) gt_bits |= 1u << c;
+      if (t < vis && key == T) eq_bits |= 1u << c;
+    }
+    uint32_t sel_bits = gt_bits;
+    if (all_ties) {
+      sel_bits |= eq_bits;
+    } else {
+      // ranks of the ties in token order
+      for (int c = 0; c < nc; ++c) {
+        const unsigned bal = __ballot_sync(0xffffffffu, (eq_bits >> c) & 1u);
+        if (lane == 0) offs[c * 32 + warp] = __popc(bal);
+      }
+      scan_offsets(nc, eq_base);
+      for (int c = 0; c < nc; ++c) {
+        const unsigned bal = __ballot_sync(0xffffffffu, (eq_bits >> c) & 1u);
+        if ((eq_bits >> c) & 1u) {
+          const int rank = offs[c * 32 + warp] + __popc(bal & lt);
+          if (rank < need) sel_bits |= 1u << c;
+        }
+      }
+      eq_base = sh_total;
+      __syncthreads();  // offs is rewritten below
+    }
+    for (int c = 0; c < nc; ++c) {
+      const unsigned bal = __ballot_sync(0xffffffffu, (sel_bits >> c) & 1u);
+      if (lane == 0) offs[c * 32 + warp] = __popc(bal);
+    }
+    scan_offsets(nc, sel_base);
+    for (int c = 0; c < nc; ++c) {
+      const unsigned bal = __ballot_sync(0xffffffffu, (sel_bits >> c) & 1u);
+      if ((sel_bits >> c) & 1u) out[offs[c * 32 + warp] + __popc(bal & lt)] = (c0 + c) * blockDim.x + tid;
+    }
+    sel_base = sh_total;
+    __syncthreads();  // offs is rewritten by the next super-chunk
   }
-  // prefix = threshold key T: take every key > T and the first `need` keys
-  // equal to T (lowest token indices), in token order
-  int base_out = 0, eq_seen = 0;
-  for (int c0 = 0; c0 < vis; c0 += blockDim.x) {
-    const int t = c0 + threadIdx.x;
-    const uint32_t key = t < vis ? order_key(sc[t]) : 0u;
-    const int eq = t < vis && key == prefix;
-    const int gt = t < vis && key > prefix;
-    int eq_total;
-    const int eq_rank = block_scan(eq, sh, &eq_total) - eq + eq_seen;  // exclusive
-    const int sel = gt || (eq && eq_rank < need);
-    int sel_total;
-    const int pos = block_scan(sel, sh, &sel_total) - sel + base_out;
-    if (sel) out[pos] = t;
-    base_out += sel_total;
-    eq_seen += eq_total;
-  }
-  for (int e = base_out + threadIdx.x; e < k; e += blockDim.x) out[e] = -1;
+  // vis > k: exactly k tokens were selected, so there is no padding
 }
 
 // ---- gather of the selected latent rows ---------------------------------------
@@ -430,29 +605,6 @@ cudaError_t dsa_indexer_launch(const gqa_bf16* q_idx, const float* w_idx, const 
   if (!q_idx || !w_idx || !k_idx || !block_table || !seq_lens || !scores)
     return cudaErrorInvalidValue;
   if (!aligned16(q_idx) || !aligned16(k_idx)) return cudaErrorMisalignedAddress;
-  IndexerParams p{};
-  if (!make_map128(&p.tm_k, k_idx, static_cast<uint64_t>(num_blocks) * kPage, kPage) ||
-      !make_map128(&p.tm_q, q_idx, static_cast<uint64_t>(B) * NQ, static_cast<uint32_t>(NQ)))
-    return cudaErrorInvalidValue;
-  p.w = w_idx;
-  p.block_table = block_table;
-  p.seq_lens = seq_lens;
-  p.scores = scores;
-  p.stride = scores_stride;
-  p.B = B;
-  p.s_q = s_q;
-  p.H = n_heads;
-  p.max_blocks = max_blocks;
-  p.num_blocks = num_blocks;
-  p.causal = causal ? 1 : 0;
-  // splits of each request's 128-token tiles: enough CTAs to fill the GPU
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int max_tiles = (max_blocks * kPage + kTile - 1) / kTile;
-  int ns = (sms + B - 1) / B;
-  ns = ns < 1 ? 1 : (ns > max_tiles ? max_tiles : ns);
-  p.num_splits = ns;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -463,14 +615,39 @@ cudaError_t dsa_indexer_launch(const gqa_bf16* q_idx, const float* w_idx, const 
     attr_err = e1 != cudaSuccess ? e1 : e2;
   });
   if (attr_err != cudaSuccess) return attr_err;
-  const long long grid = static_cast<long long>(B) * ns;
-  if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (NQ == 64)
-    dsa_indexer_kernel<64><<<static_cast<unsigned>(grid), kThreads, IdxGeom<64>::kSmem, stream>>>(p);
-  else
-    dsa_indexer_kernel<128>
-        <<<static_cast<unsigned>(grid), kThreads, IdxGeom<128>::kSmem, stream>>>(p);
-  return cudaGetLastError();
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // batches of at most kMaxBatch requests (the tile prefix lives in smem)
+  for (int b0 = 0; b0 < B; b0 += kMaxBatch) {
+    const int nb = B - b0 < kMaxBatch ? B - b0 : kMaxBatch;
+    IndexerParams p{};
+    const gqa_bf16* q0 = q_idx + static_cast<size_t>(b0) * NQ * 128;
+    if (!make_map128(&p.tm_k, k_idx, static_cast<uint64_t>(num_blocks) * kPage, kPage) ||
+        !make_map128(&p.tm_q, q0, static_cast<uint64_t>(nb) * NQ, static_cast<uint32_t>(NQ)))
+      return cudaErrorInvalidValue;
+    p.w = w_idx + static_cast<size_t>(b0) * NQ;
+    p.block_table = block_table + static_cast<size_t>(b0) * max_blocks;
+    p.seq_lens = seq_lens + b0;
+    p.scores = scores + static_cast<size_t>(b0) * s_q * scores_stride;
+    p.stride = scores_stride;
+    p.B = nb;
+    p.s_q = s_q;
+    p.H = n_heads;
+    p.max_blocks = max_blocks;
+    p.num_blocks = num_blocks;
+    p.causal = causal ? 1 : 0;
+    // one CTA per SM; fewer for small batches (at least one tile each)
+    const long long max_tiles = static_cast<long long>(nb) * ((max_blocks * kPage + kTile - 1) / kTile);
+    const int grid = static_cast<int>(max_tiles < sms ? max_tiles : sms);
+    if (NQ == 64)
+      dsa_indexer_kernel<64><<<grid, kThreads, IdxGeom<64>::kSmem, stream>>>(p);
+    else
+      dsa_indexer_kernel<128><<<grid, kThreads, IdxGeom<128>::kSmem, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const int* seq_lens,
@@ -483,7 +660,21 @@ cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const 
   if (!scores || !seq_lens || !indices) return cudaErrorInvalidValue;
   TopkParams p{scores, scores_stride, seq_lens, indices, counts, B, s_q, k, max_tokens,
                causal ? 1 : 0};
-  dsa_topk_kernel<<<static_cast<unsigned>(B * s_q), kTopkThreads, 0, stream>>>(p);
+  const unsigned grid = static_cast<unsigned>(B * s_q);
+  if (max_tokens <= kTopkSmemKeys) {
+    const int smem = max(max_tokens, 1) * 4;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+      attr_err = cudaFuncSetAttribute(dsa_topk_kernel<true>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      kTopkSmemKeys * 4);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    dsa_topk_kernel<true><<<grid, kTopkThreads, smem, stream>>>(p);
+  } else {
+    dsa_topk_kernel<false><<<grid, kTopkThreads, 0, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 

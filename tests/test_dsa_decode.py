@@ -174,3 +174,37 @@ def test_sparse_with_topk_above_length_is_dense():
     np.testing.assert_allclose(out.numpy(), dense_out.float().cpu().numpy(), atol=1e-2, rtol=1e-2)
     fin = torch.isfinite(dense_lse.cpu())
     np.testing.assert_allclose(lse[fin].numpy(), dense_lse.cpu()[fin].numpy(), atol=1e-3)
+
+
+def test_indexer_batches_above_one_launch():
+    # more requests than one launch takes (4096): the host splits the batch
+    gen = torch.Generator().manual_seed(21)
+    S = torch.randint(0, 200, (4100,), generator=gen).tolist()
+    S[0], S[-1] = 0, 129
+    case = cases.make_dsa_case(S, 1, 16, n_idx_heads=64, seed=21, pool_factor=1.2, poison=False)
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, False)
+    _check_status()
+    got = scores.cpu()
+    for b in (1, 2, 4095, 4096, 4097, 4099):
+        ref = oracle.dsa_scores(case[2][b:b + 1], case[3][b:b + 1], case[4], case[5][b:b + 1],
+                                case[6][b:b + 1], smax=max(1, S[b]))
+        np.testing.assert_allclose(got[b, 0, :S[b]].numpy(), ref[0, 0, :S[b]].numpy(),
+                                   rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_topk_long_rows_from_global_scores(causal):
+    # rows longer than the shared-memory key capacity (40960) read the scores
+    gen = torch.Generator().manual_seed(22)
+    B, s_q, Smax, k = 2, 2, 50000, 2048
+    sc = (torch.randint(0, 300, (B, s_q, Smax), generator=gen).float() - 150) * 0.25
+    sl = torch.tensor([50000, 41000], dtype=torch.int32)
+    idx, counts = dsa_decode.dsa_topk(sc.cuda(), sl.cuda(), k, causal)
+    _check_status()
+    vis = sc.clone()
+    for b in range(B):
+        for i in range(s_q):
+            v = int(sl[b]) - s_q + 1 + i if causal else int(sl[b])
+            vis[b, i, v:] = -math.inf
+    assert np.array_equal(idx.cpu().numpy(), oracle.dsa_topk(vis, k))
