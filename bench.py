@@ -847,18 +847,25 @@ def run_dsa(args, world, rank, local):
     # each stage alone, on the same inputs (stage times sum to about the step)
     st_scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t, causal)
     st_idx, st_counts = dsa_decode.dsa_topk(st_scores, sl_t, topk, causal)
-    st_pages = dsa_decode.dsa_gather(kv, bt, st_idx)
-    table = dsa_decode._identity_table(rows, kpad // 64, device)
-    q_rows = q.reshape(rows, 1, h_q, 576)
-    cnt_rows = st_counts.reshape(rows)
+    fused = h_q % 128 == 0
     stages = {
         "dsa_indexer_kernel": lambda: dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t,
                                                              causal),
         "dsa_topk_kernel": lambda: dsa_decode.dsa_topk(st_scores, sl_t, topk, causal),
-        "dsa_gather_kernel": lambda: dsa_decode.dsa_gather(kv, bt, st_idx),
-        "mla_decode_kernel": lambda: mla_decode.mla_decode(q_rows, st_pages, table, cnt_rows,
-                                                           scale, num_splits=ns),
     }
+    if fused:
+        # the MLA kernel fetches the selected rows itself
+        stages["mla_decode_rows_kernel"] = lambda: dsa_decode.sparse_mla_decode(
+            q, kv, bt, st_idx, st_counts, scale, ns)
+    else:
+        st_pages = dsa_decode.dsa_gather(kv, bt, st_idx)
+        table = dsa_decode._identity_table(rows, kpad // 64, device)
+        q_rows = q.reshape(rows, 1, h_q, 576)
+        cnt_rows = st_counts.reshape(rows)
+        stages["dsa_gather_kernel"] = lambda: dsa_decode.dsa_gather(kv, bt, st_idx)
+        stages["mla_decode_kernel"] = lambda: mla_decode.mla_decode(q_rows, st_pages, table,
+                                                                    cnt_rows, scale,
+                                                                    num_splits=ns)
     n_stage = max(3, min(args.steps, 200))
     stage_ms = {}
     for name, fn in stages.items():
@@ -872,9 +879,13 @@ def run_dsa(args, world, rank, local):
     stage_bytes = {
         "dsa_indexer_kernel": sum_S * 128 * 2 + rows * n_idx * (128 * 2 + 4) + s_q * sum_S * 4,
         "dsa_topk_kernel": sum(sum(v) for v in vis) * 4 + rows * topk * 4,
-        "dsa_gather_kernel": tok_sel * 1152 + rows * kpad * 1152 + rows * topk * 4,
-        "mla_decode_kernel": tok_sel * 1152 + rows * h_q * (576 + 512) * 2,
     }
+    if fused:
+        stage_bytes["mla_decode_rows_kernel"] = (tok_sel * 1152 + rows * topk * 4 +
+                                                 rows * h_q * (576 + 512) * 2)
+    else:
+        stage_bytes["dsa_gather_kernel"] = tok_sel * 1152 + rows * kpad * 1152 + rows * topk * 4
+        stage_bytes["mla_decode_kernel"] = tok_sel * 1152 + rows * h_q * (576 + 512) * 2
     bytes_local = sum(stage_bytes.values())
     bytes_total = sum_over_ranks(bytes_local, world, device)
 
@@ -900,7 +911,8 @@ def run_dsa(args, world, rank, local):
     achieved = stage_bytes[top] / (stage_ms[top] * 1e-3) / 1e9
     value = bytes_total / (ms_max * 1e-3) / 1e9
     line = {
-        "metric": "DSA sparse decode step: algorithmic GB/s (indexer + top-k + gather + MLA)",
+        "metric": "DSA sparse decode step: algorithmic GB/s (indexer + top-k + MLA over the "
+                  "selected rows)",
         "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max, 5),
         "median_us_per_step": round(median_us, 2),
@@ -921,13 +933,14 @@ def run_dsa(args, world, rank, local):
                 "h2d_bytes_per_step": int(e2e.h2d_bytes * world),
                 "d2h_bytes_per_step": int(e2e.d2h_bytes * world),
                 "path": "dsa_decode.sparse_decode -> C ABI dsa_indexer_launch, dsa_topk_launch, "
-                        "dsa_gather_launch, mla_decode_launch; q, q_idx, w_idx, block_table and "
-                        "seq_lens H2D, out D2H every step, double-buffered"},
+                        "mla_decode_sparse_launch (h_q % 128 == 0; else dsa_gather_launch + "
+                        "mla_decode_launch); q, q_idx, w_idx, block_table and seq_lens H2D, out "
+                        "D2H every step, double-buffered"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": peak_src, "kernel": top,
                      "algorithmic_bytes_per_launch": int(stage_bytes[top])},
-        "gpu_launches": int(args.steps * (4 if ns == 1 else 5)),
+        "gpu_launches": int(args.steps * ((3 if fused else 4) + (0 if ns == 1 else 1))),
         "clocks": clocks, "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)

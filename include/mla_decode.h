@@ -29,8 +29,10 @@ extern "C" {
 #endif
 
 /* Split count for B requests of up to max_pages 64-token pages on num_sms
- * SMs: enough (request, query-row group, page range) CTAs to fill the GPU,
- * at least two pages per split, at most 64. */
+ * SMs: the count (1..64, at least two pages per split) minimising a wave
+ * cost model of the 2-CTA work units (pages per split plus a fixed start
+ * per unit), e.g. 4 for 128 requests of ~8K tokens, 1 for 2K-token sparse
+ * selections. */
 int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms);
 
 /* Workspace bytes for num_splits > 1 (unnormalised partial states); 0 for
@@ -46,6 +48,21 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
                               int h_q, int page_size, int max_blocks, int num_blocks,
                               float softmax_scale, int causal, int num_splits, void* workspace,
                               size_t workspace_bytes, cudaStream_t stream);
+
+/* Sparse decode over selected tokens (the attention step of a DSA-style
+ * sparse decode, include/dsa_decode.h): query position i of request b
+ * attends to the cache rows of tokens indices[(b * s_q + i) * topk + 0 ..
+ * counts[b * s_q + i] - 1] (positions in the request's block_table), read
+ * directly from the paged cache.  Requires h_q a multiple of 128 (every
+ * 128-row group is one query position); otherwise as mla_decode_launch
+ * without causal masking (the selection applies it). */
+cudaError_t mla_decode_sparse_launch(const gqa_bf16* q, const gqa_bf16* kv_cache,
+                                     const int* block_table, const int* indices,
+                                     const int* counts, int topk, gqa_bf16* out, float* lse, int B,
+                                     int s_q, int h_q, int page_size, int max_blocks,
+                                     int num_blocks, float softmax_scale, int num_splits,
+                                     void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream);
 
 /* Device status word of the MLA kernels (bit 0: a bounded wait gave up,
  * bit 1: block id out of range); reset clears it.  Synchronises the device. */

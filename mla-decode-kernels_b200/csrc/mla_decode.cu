@@ -53,6 +53,9 @@ struct Params {
   CUtensorMap tm_kv;  // [num_blocks * 64, 576] bf16, box {64, 64}, 128B swizzle
   CUtensorMap tm_q_rope;   // the same rows, box {32, NH}, 64B swizzle (128-row groups)
   CUtensorMap tm_kv_rope;  // the same rows, box {32, 64}, 64B swizzle (128-row groups)
+  const int* sparse_idx;     // sparse: [B * s_q, topk] token positions per query position
+  const __nv_bfloat16* kv;   // sparse: the cache (rows copied by the producer warp)
+  int topk;                  // sparse: index row length
   const int* block_table;
   const int* seq_lens;
   __nv_bfloat16* out;  // [B, s_q, h_q, 512] (num_splits == 1)
@@ -644,7 +647,9 @@ struct Rows {
   static constexpr int kRing = 0;
   static constexpr int kX = kRing + kStages * kStageBytes;  // two tiles' partials
   static constexpr int kSmall = kX + 2 * kXBytes;
-  static constexpr int kSmem = kSmall + 256 + 3 * 2 * 128 * 4 + 1024;
+  static constexpr int kRowQ = kSmall + 256 + 3 * 2 * 128 * 4;  // sparse: resolved rows
+  static constexpr int kRowAhead = 4;                  // tiles resolved and prefetched ahead
+  static constexpr int kSmem = kRowQ + (kRowAhead + 1) * kPage * 4 + 1024;
   static constexpr int kThreads = 320;  // producer, MMA, eight softmax warps
   static constexpr int kQStage = kStages - 2;            // Q_r staged in stages 3-4
   static constexpr int kQLatBytes = 128 * 128;           // one 64-dim box of 128 rows
@@ -678,7 +683,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
   const int sp = (unit / p.n_hg) % p.num_splits;
   const int b = unit / (p.n_hg * p.num_splits);
   const int row0 = hg * 128;
-  const int S = max(0, min(p.seq_lens[b], p.max_blocks * kPage));
+  // sparse: the unit's tokens are the selection of its query position
+  // (seq_lens holds the selected counts, one per query position)
+  const int qpos = row0 / p.h_q;
+  const int S = p.sparse_idx ? max(0, min(p.seq_lens[b * p.s_q + qpos], p.topk))
+                             : max(0, min(p.seq_lens[b], p.max_blocks * kPage));
   const int pages = (S + kPage - 1) / kPage;
   const int chunk = (pages + p.num_splits - 1) / p.num_splits;
   const int pg0 = min(pages, sp * chunk), pg1 = min(pages, pg0 + chunk);
@@ -686,7 +695,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSt; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
+      // sparse: one cp.async completion arrival per producer lane
+      mbar_init(bar_full + 8 * s, p.sparse_idx ? 32 : 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_sfull, 1);
@@ -713,7 +723,100 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const int rope_x = 512 + 32 * static_cast<int>(rank);  // this CTA's rope dims
 
-  if (warp == 0) {
+  if (warp == 0 && p.sparse_idx) {
+    // -------------------- producer warp, gathered cache rows --------------------
+    // Tile t holds selected tokens (pg0 + t) * 64 .. + 63.  Lane L resolves
+    // slots 2L and 2L + 1 to cache rows (a shared queue kRowAhead tiles ahead
+    // of use, so the token -> page -> row lookups overlap the ring) and copies
+    // this CTA's half of both rows (four 128-byte latent box rows, one
+    // 64-byte rope row) with 16-byte cp.async into the swizzled stage layout
+    // TMA would have written.  TMA gather copies (four rows each) run into the
+    // per-SM TMA operation rate at 80 copies per tile; these do not.
+    if (ntiles > 0) {
+      const int* idx = p.sparse_idx + static_cast<size_t>(b * p.s_q + qpos) * p.topk;
+      const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar_q, G::kQBytes);
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(sQ + c * G::kQLatBytes, &p.tm_q, 64 * (4 * static_cast<int>(rank) + c),
+                      b * p.rows + row0, bar_q);
+        tma_load_2d(sQ + 4 * G::kQLatBytes, &p.tm_q_rope, rope_x, b * p.rows + row0, bar_q);
+      }
+      int* rowq = reinterpret_cast<int*>(smem + G::kRowQ);
+      auto resolve = [&](int t) {
+        if (t >= ntiles) return;
+        int* q_t = rowq + (t % (G::kRowAhead + 1)) * kPage;
+        #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int j = (pg0 + t) * kPage + 2 * lane + u;
+          int row = -1;
+          if (j < S) {
+            const int tok = __ldg(idx + j);
+            int page = tok >= 0 && tok < p.max_blocks * kPage ? __ldg(bt + (tok >> 6)) : -1;
+            if (page < 0 || page >= p.num_blocks) {
+              raise(kStatusBadPage);
+              page = 0;
+            }
+            row = page * kPage + (tok & (kPage - 1));
+            // this CTA's half of the row into L2 while the tile waits its turn
+            const char* r = reinterpret_cast<const char*>(p.kv) + static_cast<size_t>(row) * (kD * 2);
+            #pragma unroll
+            for (int l = 0; l < 4; ++l) prefetch_l2(r + 512 * rank + 128 * l);
+            prefetch_l2(r + 2 * rope_x);
+          }
+          q_t[2 * lane + u] = row;
+        }
+      };
+      for (int t = 0; t < G::kRowAhead; ++t) resolve(t);
+      const char* kvb = reinterpret_cast<const char*>(p.kv);
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % kSt;
+        resolve(t + G::kRowAhead);
+        const int* q_t = rowq + (t % (G::kRowAhead + 1)) * kPage;
+        bool ok = true;
+        if (lane == 0) {
+          if (t >= kSt)
+            ok = mbar_wait(bar_empty + 8 * s, ((t - kSt) / kSt) & 1);
+          else if (s >= G::kQStage)
+            ok = mbar_wait(bar_qready, 0);  // Q_r has left these stages
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          if (lane == 0) raise(kStatusWaitTimeout);
+          break;
+        }
+        __syncwarp();  // the queue entries other lanes wrote are visible
+        // slots past the selection take the tile's first row (zeroed before use)
+        const int first = q_t[0];
+        const uint32_t st = sRing + s * G::kStageBytes;
+        #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int r = 2 * lane + u;  // slot = row within the stage
+          const int row = q_t[r] < 0 ? first : q_t[r];
+          const char* src = kvb + static_cast<size_t>(row) * (kD * 2);
+          #pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            #pragma unroll
+            for (int k = 0; k < 8; ++k)
+              cp_async_16(st + c * kColBytes + r * 128 + ((k ^ (r & 7)) << 4),
+                          src + (256 * rank + 64 * c + 8 * k) * 2);
+          }
+          #pragma unroll
+          for (int k = 0; k < 4; ++k)
+            cp_async_16(st + 4 * kColBytes + r * 64 + ((k ^ ((r >> 1) & 3)) << 4),
+                        src + (rope_x + 8 * k) * 2);
+        }
+        cp_async_mbar_arrive(bar_full + 8 * s);  // one of the stage's 32 arrivals
+        issued = t + 1;
+      }
+      // every issued copy has landed before the CTA may exit
+      if (lane == 0) {
+        if (!mbar_wait(bar_q, 0)) raise(kStatusWaitTimeout);
+        for (int t = max(0, issued - kSt); t < issued; ++t)
+          if (!mbar_wait(bar_full + 8 * (t % kSt), (t / kSt) & 1)) raise(kStatusWaitTimeout);
+      }
+    }
+  } else if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && ntiles > 0) {
       tma_prefetch_desc(&p.tm_kv);
@@ -790,6 +893,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       }
       idle_since = global_timer_ns();
       tc_fence_after();
+      // stages written by cp.async (generic proxy) are read by the tensor core
+      if (p.sparse_idx) fence_proxy_async_smem();
       if (action == 2) {
         const uint32_t kv = sRing + (qk % kSt) * G::kStageBytes;
         // zero the cache rows past the request's end in its last page (they
@@ -1251,20 +1356,22 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
   const Layout L = layout_for(rows);
   if (L.NH == 0 || B <= 0 || num_sms <= 0) return 1;
   const long long units = static_cast<long long>(B) * L.n_hg;
-  // One CTA pair per two SMs at a time: the smallest split count whose pairs
-  // fill their last wave to >= 90 % (at least one full wave), keeping >= 4
-  // pages per split; else the best fill among those.
+  // Cost model over CTA-pair waves: each split is a pair that pays a fixed
+  // start (tensor memory, Q staging, the first pages' latency) worth about
+  // five page-times, and splits > 1 add partial states and a combine pass;
+  // measured on B200 (b = 128, h_q = 128) it picks 4 splits for ~8K-token
+  // requests and 1 for 2K-token sparse selections, the fastest of 1-16.
   const long long slots = std::max(1, num_sms / 2);
-  const long long cap = std::max(1, std::min(64, max_pages / 4));
+  const long long cap = std::max(1, std::min(64, max_pages / 2));
+  const long long pages = std::max(1, max_pages);
   long long best = 1;
-  double best_fill = 0.0;
+  double best_cost = 1e300;
   for (long long ns = 1; ns <= cap; ++ns) {
-    const long long ctas = units * ns;
-    const long long waves = (ctas + slots - 1) / slots;
-    const double fill = static_cast<double>(ctas) / (static_cast<double>(waves) * slots);
-    if (ctas >= slots && fill >= 0.9) return static_cast<int>(ns);
-    if (fill > best_fill + 1e-9) {
-      best_fill = fill;
+    const long long waves = (units * ns + slots - 1) / slots;
+    const double cost = static_cast<double>(waves) *
+                        (static_cast<double>((pages + ns - 1) / ns) + 5.0 + (ns > 1 ? 1.0 : 0.0));
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
       best = ns;
     }
   }
@@ -1276,15 +1383,23 @@ size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits) {
   return part_bytes(B, s_q * h_q, num_splits);
 }
 
-cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const int* block_table,
-                              const int* seq_lens, gqa_bf16* out, float* lse, int B, int s_q,
-                              int h_q, int page_size, int max_blocks, int num_blocks,
-                              float softmax_scale, int causal, int num_splits, void* workspace,
-                              size_t workspace_bytes, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// The dense launch and the sparse one (sparse_idx != null: seq_lens holds
+// the selected counts per query position, and h_q is a multiple of 128 so
+// that every 128-row group belongs to one query position).
+cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const int* block_table,
+                            const int* seq_lens, const int* sparse_idx, int topk, gqa_bf16* out,
+                            float* lse, int B, int s_q, int h_q, int page_size, int max_blocks,
+                            int num_blocks, float softmax_scale, int causal, int num_splits,
+                            void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   using namespace gqa::mla;
   if (B < 0 || s_q <= 0 || h_q <= 0 || page_size != kPage || max_blocks <= 0 || num_blocks <= 0 ||
       num_splits < 1 || num_splits > 64)
     return cudaErrorInvalidValue;
+  if (sparse_idx && (h_q % 128 != 0 || topk <= 0 || causal)) return cudaErrorInvalidValue;
   if (B == 0) return cudaSuccess;
   const int rows = s_q * h_q;
   const Layout L = layout_for(rows);
@@ -1292,6 +1407,10 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   if (!q || !kv_cache || !block_table || !seq_lens || !out || !lse) return cudaErrorInvalidValue;
   if (!aligned16(q) || !aligned16(kv_cache)) return cudaErrorMisalignedAddress;
   Params p{};
+  p.sparse_idx = sparse_idx;
+  p.kv = reinterpret_cast<const __nv_bfloat16*>(kv_cache);
+  p.topk = topk;
+
   if (!make_map(&p.tm_q, q, static_cast<uint64_t>(B) * rows, static_cast<uint32_t>(L.NH)) ||
       !make_map(&p.tm_kv, kv_cache, static_cast<uint64_t>(num_blocks) * kPage, kPage))
     return cudaErrorInvalidValue;
@@ -1359,6 +1478,33 @@ cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const
   const long long nrows = static_cast<long long>(B) * rows;
   mla_combine_kernel<<<static_cast<unsigned>((nrows + 3) / 4), 128, 0, stream>>>(c);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const int* block_table,
+                              const int* seq_lens, gqa_bf16* out, float* lse, int B, int s_q,
+                              int h_q, int page_size, int max_blocks, int num_blocks,
+                              float softmax_scale, int causal, int num_splits, void* workspace,
+                              size_t workspace_bytes, cudaStream_t stream) {
+  return mla_launch_impl(q, kv_cache, block_table, seq_lens, nullptr, 0, out, lse, B, s_q, h_q,
+                         page_size, max_blocks, num_blocks, softmax_scale, causal, num_splits,
+                         workspace, workspace_bytes, stream);
+}
+
+cudaError_t mla_decode_sparse_launch(const gqa_bf16* q, const gqa_bf16* kv_cache,
+                                     const int* block_table, const int* indices,
+                                     const int* counts, int topk, gqa_bf16* out, float* lse, int B,
+                                     int s_q, int h_q, int page_size, int max_blocks,
+                                     int num_blocks, float softmax_scale, int num_splits,
+                                     void* workspace, size_t workspace_bytes,
+                                     cudaStream_t stream) {
+  if (!indices) return cudaErrorInvalidValue;
+  return mla_launch_impl(q, kv_cache, block_table, counts, indices, topk, out, lse, B, s_q, h_q,
+                         page_size, max_blocks, num_blocks, softmax_scale, 0, num_splits,
+                         workspace, workspace_bytes, stream);
 }
 
 int mla_decode_get_status(int reset) {

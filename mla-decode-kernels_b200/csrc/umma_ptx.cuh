@@ -153,6 +153,24 @@ __device__ __forceinline__ void tma_prefetch_2d(const void* tmap, int x, int y) 
                : "memory");
 }
 
+// Prefetch of the 128-byte line holding a global address into L2 (a plain
+// load-store-unit hint, not a TMA operation).
+__device__ __forceinline__ void prefetch_l2(const void* a) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+
+// 16 bytes global -> shared, asynchronous (completion tracked with
+// cp_async_mbar_arrive).  Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+// Arrive on the mbarrier (counting as one of its expected arrivals) once
+// every cp.async this thread issued before has completed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

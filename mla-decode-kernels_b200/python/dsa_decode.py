@@ -1,4 +1,6 @@
-"""DSA-style sparse decode on B200: indexer -> top-k -> gather -> MLA decode.
+"""DSA-style sparse decode on B200: indexer -> top-k -> MLA decode over the
+selected cache rows (fetched by the MLA kernel itself for h_q a multiple of
+128, gathered into contiguous pages first otherwise).
 
 The reference lists this as roadmap kernel K3 ("DSA-style sparse decode:
 indexer + top-k + sparse gather", README.md "Roadmap") and ships no code for
@@ -66,17 +68,30 @@ def dsa_gather(k_cache, block_table, indices):
 
 
 def sparse_mla_decode(q, k_cache, block_table, indices, counts, softmax_scale=None,
-                      num_splits=0):
-    """Attention of each (b, i) over its selected tokens only: the rows are
-    gathered into contiguous pages and decoded by the MLA kernel as B * s_q
-    one-query requests of counts[b, i] tokens (the selection already applies
-    any causal mask)."""
+                      num_splits=0, fused=None):
+    """Attention of each (b, i) over its selected tokens only (the selection
+    already applies any causal mask).  With h_q a multiple of 128 (fused,
+    the default there) the MLA kernel fetches the selected cache rows itself
+    (TMA gather, four rows per copy); otherwise the rows are gathered into
+    contiguous pages and decoded as B * s_q one-query requests of
+    counts[b, i] tokens."""
     B, s_q, h_q = q.shape[0], q.shape[1], q.shape[2]
     if softmax_scale is None:
         softmax_scale = q.shape[-1] ** -0.5
     k = indices.shape[-1]
     kpad = (k + PAGE - 1) // PAGE * PAGE
     rows = B * s_q
+    if fused is None:
+        fused = h_q % 128 == 0
+    if fused:
+        if num_splits == 0:
+            num_splits = int(_ext.mla_pick_splits(rows, 1, h_q, kpad // PAGE,
+                                                  mla_decode._num_sms(q.device)))
+        nbytes = int(_ext.mla_workspace_bytes(B, s_q, h_q, num_splits))
+        ws = (mla_decode.workspace(q.device, nbytes) if nbytes
+              else torch.empty(0, dtype=torch.uint8, device=q.device))
+        return _ext.mla_decode_sparse(q, k_cache, block_table, indices, counts,
+                                      float(softmax_scale), int(num_splits), ws)
     pages = dsa_gather(k_cache, block_table, indices)
     table = _identity_table(rows, kpad // PAGE, q.device)
     out, lse = mla_decode.mla_decode(q.reshape(rows, 1, h_q, q.shape[3]), pages, table,

@@ -479,6 +479,62 @@ std::vector<torch::Tensor> mla_decode(torch::Tensor q, torch::Tensor kv_cache,
   return {out, lse};
 }
 
+// Sparse attention over selected tokens: indices [B, s_q, topk] int32 token
+// positions, counts [B, s_q] int32 -> (out [B, s_q, h_q, 512] bf16, lse [B, h_q, s_q]).
+std::vector<torch::Tensor> mla_decode_sparse(torch::Tensor q, torch::Tensor kv_cache,
+                                             torch::Tensor block_table, torch::Tensor indices,
+                                             torch::Tensor counts, double softmax_scale,
+                                             int64_t num_splits, torch::Tensor workspace) {
+  TORCH_CHECK(q.is_cuda() && kv_cache.is_cuda() && block_table.is_cuda() && indices.is_cuda() &&
+                  counts.is_cuda(),
+              "all tensors must be CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && kv_cache.scalar_type() == torch::kBFloat16,
+              "q and kv_cache must be bf16");
+  TORCH_CHECK(block_table.scalar_type() == torch::kInt32 && indices.scalar_type() == torch::kInt32 &&
+                  counts.scalar_type() == torch::kInt32,
+              "block_table, indices and counts must be int32");
+  TORCH_CHECK(q.is_contiguous() && kv_cache.is_contiguous() && block_table.is_contiguous() &&
+                  indices.is_contiguous() && counts.is_contiguous(),
+              "all tensors must be contiguous");
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 576, "q must be [B, s_q, h_q, 576]");
+  TORCH_CHECK(q.size(2) % 128 == 0, "the fused sparse decode takes h_q a multiple of 128");
+  TORCH_CHECK(kv_cache.dim() == 4 && kv_cache.size(1) == 64 && kv_cache.size(2) == 1 &&
+                  kv_cache.size(3) == 576,
+              "kv_cache must be [num_blocks, 64, 1, 576]");
+  const int64_t B = q.size(0), s_q = q.size(1), h_q = q.size(2);
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == B,
+              "block_table must be [B, max_blocks]");
+  TORCH_CHECK(indices.dim() == 3 && indices.size(0) == B && indices.size(1) == s_q,
+              "indices must be [B, s_q, topk]");
+  TORCH_CHECK(counts.dim() == 2 && counts.size(0) == B && counts.size(1) == s_q,
+              "counts must be [B, s_q]");
+  TORCH_CHECK(kv_cache.device() == q.device() && block_table.device() == q.device() &&
+                  indices.device() == q.device() && counts.device() == q.device(),
+              "all tensors must be on the same device");
+  TORCH_CHECK(num_splits >= 1 && num_splits <= 64, "num_splits must be in [1, 64]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty({B, s_q, h_q, 512}, q.options());
+  auto lse = torch::empty({B, h_q, s_q}, q.options().dtype(torch::kFloat32));
+  const size_t need = mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
+                                                 static_cast<int>(h_q), static_cast<int>(num_splits));
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  TORCH_CHECK(need == 0 || (workspace.is_cuda() && workspace.device() == q.device() &&
+                            workspace.is_contiguous() && ws_bytes >= need),
+              "workspace must be a contiguous CUDA tensor of at least ", need, " bytes");
+  check_launch(mla_decode_sparse_launch(
+                   reinterpret_cast<const gqa_bf16*>(q.data_ptr()),
+                   reinterpret_cast<const gqa_bf16*>(kv_cache.data_ptr()),
+                   block_table.data_ptr<int>(), indices.data_ptr<int>(), counts.data_ptr<int>(),
+                   static_cast<int>(indices.size(2)), reinterpret_cast<gqa_bf16*>(out.data_ptr()),
+                   lse.data_ptr<float>(), static_cast<int>(B), static_cast<int>(s_q),
+                   static_cast<int>(h_q), 64, static_cast<int>(block_table.size(1)),
+                   static_cast<int>(kv_cache.size(0)), static_cast<float>(softmax_scale),
+                   static_cast<int>(num_splits), need ? workspace.data_ptr() : nullptr, ws_bytes,
+                   at::cuda::getCurrentCUDAStream()),
+               "mla_decode_sparse");
+  return {out, lse};
+}
+
 int64_t mla_workspace_bytes(int64_t B, int64_t s_q, int64_t h_q, int64_t num_splits) {
   return static_cast<int64_t>(mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
                                                          static_cast<int>(h_q),
@@ -609,6 +665,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mla_decode", &mla_decode, "MLA latent-cache paged decode (tcgen05)", py::arg("q"),
         py::arg("kv_cache"), py::arg("block_table"), py::arg("seq_lens"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("num_splits"), py::arg("workspace"));
+  m.def("mla_decode_sparse", &mla_decode_sparse,
+        "MLA decode over selected tokens, rows gathered by TMA (tcgen05)", py::arg("q"),
+        py::arg("kv_cache"), py::arg("block_table"), py::arg("indices"), py::arg("counts"),
+        py::arg("softmax_scale"), py::arg("num_splits"), py::arg("workspace"));
   m.def("mla_workspace_bytes", &mla_workspace_bytes, "MLA split workspace bytes");
   m.def("mla_pick_splits", &mla_pick_splits, "MLA split count heuristic");
   m.def("mla_get_status", &mla_get_status, "MLA device status word", py::arg("clear") = false);

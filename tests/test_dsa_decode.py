@@ -208,3 +208,20 @@ def test_topk_long_rows_from_global_scores(causal):
             v = int(sl[b]) - s_q + 1 + i if causal else int(sl[b])
             vis[b, i, v:] = -math.inf
     assert np.array_equal(idx.cpu().numpy(), oracle.dsa_topk(vis, k))
+
+
+@pytest.mark.parametrize("s_q,causal", [(1, False), (2, True)])
+def test_fused_row_gather_equals_gathered_pages(s_q, causal):
+    # the MLA kernel fetching the selected rows itself (TMA gather) and the
+    # same kernel over pre-gathered pages run identical tiles in the same
+    # order: bit-identical results
+    case = cases.make_dsa_case([3000, 700, 100, 2], s_q, 128, seed=23)
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, causal)
+    idx, counts = dsa_decode.dsa_topk(scores, sl, 640, causal)
+    fo, fl = dsa_decode.sparse_mla_decode(q, kv, bt, idx, counts, SCALE, fused=True)
+    go, gl = dsa_decode.sparse_mla_decode(q, kv, bt, idx, counts, SCALE, fused=False)
+    _check_status()
+    assert torch.equal(fo, go)
+    assert torch.equal(torch.isfinite(fl), torch.isfinite(gl))
+    assert torch.equal(fl[torch.isfinite(fl)], gl[torch.isfinite(gl)])
