@@ -650,7 +650,7 @@ struct Rows {
   static constexpr int kRowQ = kSmall + 256 + 3 * 2 * 128 * 4;  // sparse: resolved rows
   static constexpr int kRowAhead = 4;                  // tiles resolved and prefetched ahead
   static constexpr int kSmem = kRowQ + (kRowAhead + 1) * kPage * 4 + 1024;
-  static constexpr int kThreads = 320;  // producer, MMA, eight softmax warps
+  static constexpr int kThreads = 448;  // producer, MMA, eight softmax, four sender warps
   static constexpr int kQStage = kStages - 2;            // Q_r staged in stages 3-4
   static constexpr int kQLatBytes = 128 * 128;           // one 64-dim box of 128 rows
   static constexpr int kQBytes = 4 * kQLatBytes + 128 * 64;  // = 2 stages
@@ -700,7 +700,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       mbar_init(bar_empty + 8 * s, 1);
     }
     mbar_init(bar_sfull, 1);
-    mbar_init(bar_sfree, 8);   // one arrival per softmax warp
+    mbar_init(bar_sfree, 12);  // one arrival per softmax and sender warp
     mbar_init(bar_pfull, 8);
     mbar_init(bar_pv, 1);
     for (int j = 0; j < 2; ++j) {
@@ -952,6 +952,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     if (lane == 0) umma_commit(bar_fin);
     __syncwarp();
     if (!wait_warp(bar_fin, 0)) raise(kStatusWaitTimeout);
+  } else if (warp >= 10) {
+    // -------------------- sender warps 10..13: partials out -------------------
+    // Warp w (TMEM lane quadrant w % 4) reads this CTA's partial scores of
+    // its 32 rows, all 64 tokens, and stores them into the peer's exchange
+    // buffer: the ~16 bytes per cycle the pair's link moves no longer stall
+    // the softmax warps.
+    const int qs = warp & 3;
+    const int hs = 32 * qs + lane;
+    const uint32_t lane_base_s = static_cast<uint32_t>(32 * qs) << 16;
+    const uint32_t peer_x = mapa_shared(sX, peer);
+    const uint32_t peer_xfull = mapa_shared(bar_xfull, peer);
+    bool ok = true;
+    auto wait_cluster = [&](uint32_t bar, uint32_t parity) {
+      if (!ok) return;
+      bool done = mbar_try_wait_cluster(bar, parity);
+      if (!done) {
+        const unsigned long long t_start = global_timer_ns();
+        while (!(done = mbar_try_wait_cluster(bar, parity)))
+          if (global_timer_ns() - t_start > kWaitLimitNs) break;
+      }
+      if (!__all_sync(0xffffffffu, done)) ok = false;
+    };
+    for (int t = 0; t < ntiles; ++t) {
+      const int j = t & 1;
+      if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
+      tc_fence_after();
+      uint32_t r[4][16];
+      #pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lane_base_s + G::kSCol + 16 * c, r[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree);
+      // the peer's softmax warps have read what we put in X[j] two tiles ago
+      if (t >= 2) wait_cluster(bar_xfree + 8 * j, ((t - 2) >> 1) & 1);
+      #pragma unroll
+      for (int g = 0; g < 16; ++g)
+        st_async_v4(peer_x + j * G::kXBytes + (g * 128 + hs) * 16, r[g >> 2][4 * (g & 3)],
+                    r[g >> 2][4 * (g & 3) + 1], r[g >> 2][4 * (g & 3) + 2],
+                    r[g >> 2][4 * (g & 3) + 3], peer_xfull + 8 * j);
+    }
+    // the peer has read our last two partials before either CTA may exit
+    for (int t = max(0, ntiles - 2); t < ntiles; ++t)
+      wait_cluster(bar_xfree + 8 * (t & 1), (t >> 1) & 1);
+    if (!ok) raise(kStatusWaitTimeout);
   } else {
     // ------------------------- softmax warps 2..9 ----------------------------
     // Warp w owns query rows h = 32 (w % 4) + lane (TMEM lane quadrant w % 4)
@@ -1019,12 +1064,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_qready);
     }
-    // Software pipeline over tiles: iteration t reads S(t + 1) (freeing it
-    // for QK(t + 2)) and sends it to the peer before the softmax of tile t,
-    // whose partial the peer sent one iteration earlier, so the exchange
-    // overlaps a tile of softmax work.  Partials of tiles t and t + 1 sit in
-    // the two exchange buffers X[t & 1], each [16][128] 16-byte chunks (4
-    // tokens of one row): conflict-free for the writes and the reads.
+    // The sender warps push this CTA's partial of every tile into the peer's
+    // exchange buffer X[t & 1] (two tiles deep).  Here iteration t reads this
+    // CTA's partial of tile t + 1 out of tensor memory first (freeing S for
+    // QK(t + 2)), then adds the peer's partial of tile t and runs its
+    // softmax.  X layout: [16 token quads][128 rows] of 16-byte chunks.
     auto read_s = [&](int t, float (&x)[32]) {
       if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
       tc_fence_after();
@@ -1041,16 +1085,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_sfree);
     };
-    auto send = [&](int t, const float (&x)[32]) {
-      const int j = t & 1;
-      if (t >= 2) wait_cluster(bar_xfree + 8 * j, ((t - 2) >> 1) & 1);
-      #pragma unroll
-      for (int g = 0; g < 8; ++g)
-        st_async_v4(peer_x + j * G::kXBytes + ((8 * hf + g) * 128 + h) * 16,
-                    __float_as_uint(x[4 * g]), __float_as_uint(x[4 * g + 1]),
-                    __float_as_uint(x[4 * g + 2]), __float_as_uint(x[4 * g + 3]),
-                    peer_xfull + 8 * j);
-    };
     float m_ref = -INFINITY, l = 0.f;
     float xn[32];
     if (ntiles > 0) {
@@ -1059,16 +1093,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         if (ntiles > 1) mbar_arrive_expect_tx(bar_xfull + 8, G::kXBytes);
       }
       read_s(0, xn);
-      send(0, xn);
     }
     for (int t = 0; t < ntiles; ++t) {
       float x[32];
       #pragma unroll
       for (int k = 0; k < 32; ++k) x[k] = xn[k];
-      if (t + 1 < ntiles) {
-        read_s(t + 1, xn);
-        send(t + 1, xn);
-      }
+      if (t + 1 < ntiles) read_s(t + 1, xn);
       const int j = t & 1;
       wait_cluster(bar_xfull + 8 * j, (t >> 1) & 1);
       uint32_t dep = 0;
@@ -1147,9 +1177,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_pfull);
     }
-    // the peer has read our last two partials before either CTA may exit
-    for (int t = max(0, ntiles - 2); t < ntiles; ++t)
-      wait_cluster(bar_xfree + 8 * (t & 1), (t >> 1) & 1);
     // ------------------------------ epilogue ---------------------------------
     wait_pv(ntiles - 1);
     tc_fence_after();
