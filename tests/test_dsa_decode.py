@@ -225,3 +225,20 @@ def test_fused_row_gather_equals_gathered_pages(s_q, causal):
     assert torch.equal(fo, go)
     assert torch.equal(torch.isfinite(fl), torch.isfinite(gl))
     assert torch.equal(fl[torch.isfinite(fl)], gl[torch.isfinite(gl)])
+
+
+@pytest.mark.parametrize("h_q,num_splits", [(128, 3), (256, 2)])
+def test_fused_row_gather_splits_and_wide_heads(h_q, num_splits):
+    # split selections (partial states + combine) and two 128-row groups per
+    # query position: still bit-identical to decoding gathered pages, and
+    # within tolerance of the oracle
+    case = cases.make_dsa_case([5000, 900, 70], 1, h_q, seed=24)
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, False)
+    idx, counts = dsa_decode.dsa_topk(scores, sl, 1024, False)
+    fo, fl = dsa_decode.sparse_mla_decode(q, kv, bt, idx, counts, SCALE, num_splits, fused=True)
+    go, gl = dsa_decode.sparse_mla_decode(q, kv, bt, idx, counts, SCALE, num_splits, fused=False)
+    _check_status()
+    assert torch.equal(fo, go)
+    assert torch.equal(fl, gl)
+    _check_attention(case, fo.float().cpu(), fl.cpu(), idx.cpu())
