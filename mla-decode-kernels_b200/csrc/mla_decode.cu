@@ -7,20 +7,21 @@
 // dims; one latent "kv head"), t < S_b, or t < S_b - s_q + 1 + i when causal;
 // lse[b, h, i] = ln sum_t exp(score_t).
 //
-// One CTA = (request, group of NH <= 64 query rows, page range).  Tokens are
-// the MMA M dimension and query rows the N dimension, so small head counts
-// waste no tensor-core work and one page read serves all NH rows:
-//   S^T[64 tok, NH]  = C[64 tok, 576] . Q[NH, 576]^T     (M = 64, 36 MMAs)
-//   O^T[512, NH]    += C[64 tok, 0:512]^T . P^T[64, NH]  (M = 128, 4 x 4 MMAs)
-// with S^T and O^T in tensor memory.
-//
-// Warps: 0 = TMA producer (one 64-token page per stage: nine 64-column boxes
-// of a 128-byte-swizzled tensor map), 1 = MMA issuer + TMEM owner, 2-5 =
-// softmax / correction / epilogue (warp w reads TMEM lanes 32 (w % 4) ..).
+// Two kernels, both 2-CTA clusters: CTA r of a pair multiplies latent dims
+// 256 r .. 256 r + 255 and half of the rope dims (the pair exchanges partial
+// scores over distributed shared memory) and owns value dims 256 r ..
+// 256 r + 255 of the output.
+//   mla_decode_kernel<NH>    groups of NH <= 64 query rows: tokens on the MMA
+//                            M dimension, query rows on N (no padding waste at
+//                            small head counts), S^T / O^T in tensor memory.
+//   mla_decode_rows_kernel   groups of 128 query rows: rows on M, Q and P as
+//                            tensor-memory A operands, one softmax thread per
+//                            row, sender warps for the exchange; also the
+//                            sparse mode (rows of selected tokens).
 // Online softmax in the log2 domain with a lazily raised reference max: P is
-// computed against the current reference m_ref[h] and O^T / l are only
-// rescaled when a tile's score exceeds m_ref by more than 2^8 (the bound on
-// exp2 growth kept in fp32 / bf16 range), which after the first tiles is rare.
+// computed against the current reference m_ref and O / l are only rescaled
+// when a tile's score exceeds m_ref by more than 2^8 (the bound on exp2
+// growth kept in fp32 / bf16 range), which after the first tiles is rare.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -95,7 +96,8 @@ __device__ __forceinline__ int visible(const Params& p, int S, int row) {
   return max(0, min(S, S - p.s_q + 1 + i));
 }
 
-// Compile-time geometry of the 2-CTA kernel for NH query rows per pair.
+// Compile-time geometry of the 2-CTA heads-on-N kernel for NH <= 64 query
+// rows per pair.
 template <int NH>
 struct Pair {
   static constexpr int kHalf = NH / 4;               // S^T values per softmax thread
@@ -103,8 +105,8 @@ struct Pair {
   static constexpr int kChunk = kWarpCols < 16 ? kWarpCols : 16;  // TMEM columns per load
   static constexpr int kCols = 5;                    // 64-dim boxes a CTA loads per row
   static constexpr int kStageBytes = kCols * kColBytes;  // 40 KB per page
-  static constexpr int kStages = NH == 128 ? 2 : (NH == 64 ? 3 : 4);
-  static constexpr int kNP = NH == 128 ? 1 : 2;      // P^T buffers
+  static constexpr int kStages = NH == 64 ? 3 : 4;
+  static constexpr int kNP = 2;                      // P^T buffers
   static constexpr int kAtomN = NH < 64 ? NH : 64;   // heads per P^T swizzle atom
   static constexpr int kRowB = 2 * kAtomN;           // P^T row bytes inside an atom
   static constexpr int kAtoms = NH / kAtomN;
@@ -126,7 +128,7 @@ struct Pair {
   static_assert(kSmem <= 232448, "shared memory");
 };
 
-// One CTA pair (a 2-CTA cluster) = (request, NH <= 128 query rows, page
+// One CTA pair (a 2-CTA cluster) = (request, NH <= 64 query rows, page
 // range).  CTA r loads, per 64-token page, latent columns 4r..4r+3 and the
 // rope column (five 64-dim boxes, 40 KB): it computes the partial
 //   S^T_r[64 tok, NH] over its 256 latent dims + half of the 64 rope dims
@@ -1362,7 +1364,7 @@ Layout layout_for(int rows) {
   L.smem = L.NH == 16    ? gqa::mla::Pair<16>::kSmem
            : L.NH == 32  ? gqa::mla::Pair<32>::kSmem
            : L.NH == 64  ? gqa::mla::Pair<64>::kSmem
-                         : gqa::mla::Pair<128>::kSmem;
+                         : gqa::mla::Rows::kSmem;  // 128-row groups: the rows kernel
   return L;
 }
 
@@ -1473,15 +1475,13 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    const cudaError_t e[5] = {
+    const cudaError_t e[4] = {
         cudaFuncSetAttribute(mla_decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<16>::kSmem),
         cudaFuncSetAttribute(mla_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<32>::kSmem),
         cudaFuncSetAttribute(mla_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<64>::kSmem),
-        cudaFuncSetAttribute(mla_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Pair<128>::kSmem),
         cudaFuncSetAttribute(mla_decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Rows::kSmem)};
     for (cudaError_t x : e)
