@@ -56,6 +56,13 @@ struct Params {
   CUtensorMap tm_kv_rope;  // the same rows, box {32, 64}, 64B swizzle (128-row groups)
   const int* sparse_idx;     // sparse: [B * s_q, topk] token positions per query position
   const __nv_bfloat16* kv;   // sparse: the cache (rows copied by the producer warp)
+  const __nv_bfloat16* q;    // 128-row groups: q rows (loaded straight into tensor memory)
+  int* hdr;                  // 128-row groups: [2] total tiles T and working pairs Pe (0: one unit per pair)
+  int per_unit;              // 128-row groups: pair c takes unit c whole (no balancing, no partials)
+  int2* unit_info;           // 128-row groups: [units] first tile and tile count
+  float* slot_m;             // 128-row groups: [2 P][128] partial max (log2 domain)
+  float* slot_l;             // 128-row groups: [2 P][128] partial sums
+  float* slot_acc;           // 128-row groups: [2 P][128][512] unnormalised partial O
   int topk;                  // sparse: index row length
   const int* block_table;
   const int* seq_lens;
@@ -649,11 +656,13 @@ struct Rows {
   static constexpr int kRing = 0;
   static constexpr int kX = kRing + kStages * kStageBytes;  // two tiles' partials
   static constexpr int kSmall = kX + 2 * kXBytes;
-  static constexpr int kRowQ = kSmall + 256 + 3 * 2 * 128 * 4;  // sparse: resolved rows
+  // small region: barriers and scan scratch [0, 256), row max / sum exchange
+  // [3][2][128] floats, the sparse row queue
+  static constexpr int kRed = 256, kRowQ = kRed + 3 * 2 * 128 * 4;
   static constexpr int kRowAhead = 4;                  // tiles resolved and prefetched ahead
-  static constexpr int kSmem = kRowQ + (kRowAhead + 1) * kPage * 4 + 1024;
+  static constexpr int kSmem = kSmall + kRowQ + (kRowAhead + 1) * kPage * 4 + 1024;
   static constexpr int kThreads = 448;  // producer, MMA, eight softmax, four sender warps
-  static constexpr int kQStage = kStages - 2;            // Q_r staged in stages 3-4
+  static constexpr int kQStage = kStages - 2;            // first unit's Q_r staged in stages 2-3
   static constexpr int kQLatBytes = 128 * 128;           // one 64-dim box of 128 rows
   static constexpr int kQBytes = 4 * kQLatBytes + 128 * 64;  // = 2 stages
   static constexpr uint32_t kOCol = 0, kQCol = 256, kPCol = 416, kSCol = 448;
@@ -661,6 +670,57 @@ struct Rows {
   static_assert(kSmem <= 232448, "shared memory");
 };
 
+// Tiles (64-token pages, or 64 selected tokens) of work unit u = (request
+// b = u / n_hg, 128-row group hg = u % n_hg).
+__device__ __forceinline__ int unit_tokens(const Params& p, int u) {
+  const int b = u / p.n_hg, hg = u % p.n_hg;
+  if (p.sparse_idx) {
+    const int qpos = (hg * 128) / p.h_q;
+    return max(0, min(p.seq_lens[b * p.s_q + qpos], p.topk));
+  }
+  return max(0, min(p.seq_lens[b], p.max_blocks * kPage));
+}
+
+// A walk over the pair's range of the batch's tiles, unit by unit (every
+// role of the CTA walks the same sequence).
+struct TileWalk {
+  int u, i, n, S, start;  // unit, tile within it, its tiles, its tokens, its first tile
+  __device__ void init(const Params& p, int u0, int start0, int g0) {
+    u = u0;
+    start = start0;
+    S = unit_tokens(p, u);
+    n = (S + kPage - 1) / kPage;
+    i = g0 - start0;
+  }
+  // to the next tile; past a unit's last tile, the next unit with tiles
+  __device__ void next(const Params& p) {
+    if (++i < n) return;
+    const int U = p.B * p.n_hg;
+    start += n;
+    i = 0;
+    n = 0;
+    while (n == 0 && u + 1 < U) {
+      ++u;
+      S = unit_tokens(p, u);
+      n = (S + kPage - 1) / kPage;
+    }
+  }
+};
+
+// Pair of tile g under the proportional split [c T / P, (c + 1) T / P).
+__device__ __forceinline__ int pair_of(long long g, long long T, int P) {
+  return static_cast<int>(((g + 1) * P - 1) / T);
+}
+
+__device__ __forceinline__ int pair_start(int c, long long T, int P) {
+  return static_cast<int>(static_cast<long long>(c) * T / P);
+}
+
+// Persistent: P = gridDim.x / 2 CTA pairs, pair c takes tiles [c T / Pe,
+// (c + 1) T / Pe) of the batch's T tiles (unit by unit, in order; Pe =
+// min(P, T) working pairs), so every pair does the same work whatever the
+// lengths; a unit split between pairs leaves one partial state per pair,
+// merged by mla_rows_combine_kernel.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     mla_decode_rows_kernel(const __grid_constant__ Params p) {
   using G = Rows;
@@ -670,30 +730,84 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const uint32_t s_base = smem_u32(smem);
   const uint32_t sRing = s_base + G::kRing, sX = s_base + G::kX;
-  const uint32_t sQ = sRing + G::kQStage * G::kStageBytes;
   const uint32_t bars = s_base + G::kSmall;
-  const uint32_t bar_full = bars, bar_empty = bars + 40, bar_sfull = bars + 80,
-                 bar_sfree = bars + 88, bar_pfull = bars + 96, bar_pv = bars + 104,
-                 bar_xfull = bars + 112, bar_xfree = bars + 128, bar_q = bars + 144,
-                 bar_qready = bars + 152, bar_fin = bars + 160;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kSmall + 176);
+  const uint32_t bar_full = bars, bar_empty = bars + 32, bar_sfull = bars + 64,
+                 bar_sfree = bars + 72, bar_pfull = bars + 80, bar_pv = bars + 88,
+                 bar_xfull = bars + 96, bar_xfree = bars + 112, bar_qready = bars + 128,
+                 bar_fin = bars + 136, bar_q = bars + 144, bar_qfree = bars + 152;
+  const uint32_t sQ = sRing + G::kQStage * G::kStageBytes;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kSmall + 160);
+  int* wk = reinterpret_cast<int*>(smem + G::kSmall + 168);  // [0] u0 [1] start0
+  int* wsum = reinterpret_cast<int*>(smem + G::kSmall + 192);  // [16] warp sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank(), peer = rank ^ 1u;
-  const int unit = blockIdx.x >> 1;
-  const int hg = unit % p.n_hg;
-  const int sp = (unit / p.n_hg) % p.num_splits;
-  const int b = unit / (p.n_hg * p.num_splits);
-  const int row0 = hg * 128;
-  // sparse: the unit's tokens are the selection of its query position
-  // (seq_lens holds the selected counts, one per query position)
-  const int qpos = row0 / p.h_q;
-  const int S = p.sparse_idx ? max(0, min(p.seq_lens[b * p.s_q + qpos], p.topk))
-                             : max(0, min(p.seq_lens[b], p.max_blocks * kPage));
-  const int pages = (S + kPage - 1) / kPage;
-  const int chunk = (pages + p.num_splits - 1) / p.num_splits;
-  const int pg0 = min(pages, sp * chunk), pg1 = min(pages, pg0 + chunk);
-  const int ntiles = pg1 - pg0;
+  const int P = static_cast<int>(gridDim.x >> 1), c = static_cast<int>(blockIdx.x >> 1);
+  const int U = p.B * p.n_hg;
+  constexpr int kW = G::kThreads / 32;
+
+  // ---- the pair's tile range: T over the batch, then the unit holding g0 ----
+  // (block-wide scans over the units in chunks of the block size)
+  auto block_excl_scan = [&](int v, int& total) {
+    int x = v;
+    #pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    int before = 0, all = 0;
+    #pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      const int s = wsum[w];
+      before += w < warp ? s : 0;
+      all += s;
+    }
+    __syncthreads();
+    total = all;
+    return before + x - v;
+  };
+  long long T = 0;
+  for (int base = 0; base < (p.per_unit ? 0 : U); base += blockDim.x) {
+    const int u = base + threadIdx.x;
+    const int n = u < U ? (unit_tokens(p, u) + kPage - 1) / kPage : 0;
+    int tot = 0;
+    block_excl_scan(n, tot);
+    T += tot;
+  }
+  // pairs beyond the tile count stay idle, so every working pair owns at
+  // least one tile and the pairs of a unit are consecutive working pairs
+  const int Pe = static_cast<int>(T < P ? T : P);
+  if (blockIdx.x == 0 && threadIdx.x == 0) {  // for the combine pass
+    p.hdr[0] = static_cast<int>(T);
+    p.hdr[1] = p.per_unit ? 0 : Pe;
+  }
+  // one unit per pair: unit c whole, its tiles counted from 0
+  const int n_own = p.per_unit && c < U ? (unit_tokens(p, c) + kPage - 1) / kPage : 0;
+  const int g0 = p.per_unit ? 0 : (c < Pe ? pair_start(c, T, Pe) : 0);
+  const int g1 = p.per_unit ? n_own : (c < Pe ? pair_start(c + 1, T, Pe) : 0);
+  const int ntiles = g1 - g0;
+  if (threadIdx.x == 0) {
+    wk[0] = p.per_unit ? c : 0;
+    wk[1] = 0;
+  }
+  __syncthreads();
+  if (ntiles > 0 && !p.per_unit) {
+    int carry = 0;
+    for (int base = 0; base < U; base += blockDim.x) {
+      const int u = base + threadIdx.x;
+      const int n = u < U ? (unit_tokens(p, u) + kPage - 1) / kPage : 0;
+      int tot = 0;
+      const int excl = carry + block_excl_scan(n, tot);
+      if (n > 0 && excl <= g0 && g0 < excl + n) {
+        wk[0] = u;
+        wk[1] = excl;
+      }
+      carry += tot;
+      if (carry > g0) break;  // uniform: every thread has the same carry
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSt; ++s) {
@@ -709,8 +823,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       mbar_init(bar_xfull + 8 * j, 1);  // armed with the byte count here, bytes from the peer
       mbar_init(bar_xfree + 8 * j, 8);  // the peer's eight softmax warps have read our partial
     }
-    mbar_init(bar_q, 1);
-    mbar_init(bar_qready, 8);  // Q_r is in tensor memory and out of the ring
+    mbar_init(bar_qready, 8);  // a unit's Q_r is in tensor memory
+    mbar_init(bar_q, 1);       // the first unit's Q_r has landed in the ring
+    mbar_init(bar_qfree, 8);   // ... and has been copied out of it
     mbar_init(bar_fin, 1);
     fence_mbar_init();
   }
@@ -724,35 +839,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int rope_x = 512 + 32 * static_cast<int>(rank);  // this CTA's rope dims
+  const int u0 = wk[0], start0 = wk[1];
+  // the first unit's Q_r by TMA into ring stages kQStage.. (they take pages
+  // once the softmax warps have copied it into tensor memory)
+  auto stage_q = [&]() {
+    const int b = u0 / p.n_hg, row0 = (u0 % p.n_hg) * 128;
+    mbar_arrive_expect_tx(bar_q, G::kQBytes);
+    for (int cc = 0; cc < 4; ++cc)
+      tma_load_2d(sQ + cc * G::kQLatBytes, &p.tm_q, 64 * (4 * static_cast<int>(rank) + cc),
+                  b * p.rows + row0, bar_q);
+    tma_load_2d(sQ + 4 * G::kQLatBytes, &p.tm_q_rope, rope_x, b * p.rows + row0, bar_q);
+  };
 
   if (warp == 0 && p.sparse_idx) {
     // -------------------- producer warp, gathered cache rows --------------------
-    // Tile t holds selected tokens (pg0 + t) * 64 .. + 63.  Lane L resolves
-    // slots 2L and 2L + 1 to cache rows (a shared queue kRowAhead tiles ahead
-    // of use, so the token -> page -> row lookups overlap the ring) and copies
-    // this CTA's half of both rows (four 128-byte latent box rows, one
-    // 64-byte rope row) with 16-byte cp.async into the swizzled stage layout
-    // TMA would have written.  TMA gather copies (four rows each) run into the
-    // per-SM TMA operation rate at 80 copies per tile; these do not.
+    // Tile t holds selected tokens i * 64 .. + 63 of its unit.  Lane L
+    // resolves slots 2L and 2L + 1 to cache rows (a shared queue kRowAhead
+    // tiles ahead of use, so the token -> page -> row lookups overlap the
+    // ring) and copies this CTA's half of both rows (four 128-byte latent box
+    // rows, one 64-byte rope row) with 16-byte cp.async into the swizzled
+    // stage layout TMA would have written.  TMA gather copies (four rows each)
+    // run into the per-SM TMA operation rate at 80 copies per tile; these do
+    // not.
     if (ntiles > 0) {
-      const int* idx = p.sparse_idx + static_cast<size_t>(b * p.s_q + qpos) * p.topk;
-      const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(bar_q, G::kQBytes);
-        for (int c = 0; c < 4; ++c)
-          tma_load_2d(sQ + c * G::kQLatBytes, &p.tm_q, 64 * (4 * static_cast<int>(rank) + c),
-                      b * p.rows + row0, bar_q);
-        tma_load_2d(sQ + 4 * G::kQLatBytes, &p.tm_q_rope, rope_x, b * p.rows + row0, bar_q);
-      }
-      int* rowq = reinterpret_cast<int*>(smem + G::kRowQ);
+      int* rowq = reinterpret_cast<int*>(smem + G::kSmall + G::kRowQ);
+      if (lane == 0) stage_q();
+      TileWalk wa;  // kRowAhead tiles ahead
+      wa.init(p, u0, start0, g0);
       auto resolve = [&](int t) {
         if (t >= ntiles) return;
+        const int b = wa.u / p.n_hg, hg = wa.u % p.n_hg;
+        const int qpos = (hg * 128) / p.h_q;
+        const int* idx = p.sparse_idx + static_cast<size_t>(b * p.s_q + qpos) * p.topk;
+        const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
         int* q_t = rowq + (t % (G::kRowAhead + 1)) * kPage;
         #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          const int j = (pg0 + t) * kPage + 2 * lane + u;
+          const int j = wa.i * kPage + 2 * lane + u;
           int row = -1;
-          if (j < S) {
+          if (j < wa.S) {
             const int tok = __ldg(idx + j);
             int page = tok >= 0 && tok < p.max_blocks * kPage ? __ldg(bt + (tok >> 6)) : -1;
             if (page < 0 || page >= p.num_blocks) {
@@ -761,13 +886,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
             }
             row = page * kPage + (tok & (kPage - 1));
             // this CTA's half of the row into L2 while the tile waits its turn
-            const char* r = reinterpret_cast<const char*>(p.kv) + static_cast<size_t>(row) * (kD * 2);
+            const char* rp =
+                reinterpret_cast<const char*>(p.kv) + static_cast<size_t>(row) * (kD * 2);
             #pragma unroll
-            for (int l = 0; l < 4; ++l) prefetch_l2(r + 512 * rank + 128 * l);
-            prefetch_l2(r + 2 * rope_x);
+            for (int l = 0; l < 4; ++l) prefetch_l2(rp + 512 * rank + 128 * l);
+            prefetch_l2(rp + 2 * rope_x);
           }
           q_t[2 * lane + u] = row;
         }
+        wa.next(p);
       };
       for (int t = 0; t < G::kRowAhead; ++t) resolve(t);
       const char* kvb = reinterpret_cast<const char*>(p.kv);
@@ -781,14 +908,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
           if (t >= kSt)
             ok = mbar_wait(bar_empty + 8 * s, ((t - kSt) / kSt) & 1);
           else if (s >= G::kQStage)
-            ok = mbar_wait(bar_qready, 0);  // Q_r has left these stages
+            ok = mbar_wait(bar_qfree, 0);  // the first Q_r has left these stages
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
           if (lane == 0) raise(kStatusWaitTimeout);
           break;
         }
         __syncwarp();  // the queue entries other lanes wrote are visible
-        // slots past the selection take the tile's first row (zeroed before use)
+        // slots past the selection take the tile's first row (their scores are
+        // masked, so P = 0 there)
         const int first = q_t[0];
         const uint32_t st = sRing + s * G::kStageBytes;
         #pragma unroll
@@ -797,11 +925,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
           const int row = q_t[r] < 0 ? first : q_t[r];
           const char* src = kvb + static_cast<size_t>(row) * (kD * 2);
           #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int cc = 0; cc < 4; ++cc) {
             #pragma unroll
             for (int k = 0; k < 8; ++k)
-              cp_async_16(st + c * kColBytes + r * 128 + ((k ^ (r & 7)) << 4),
-                          src + (256 * rank + 64 * c + 8 * k) * 2);
+              cp_async_16(st + cc * kColBytes + r * 128 + ((k ^ (r & 7)) << 4),
+                          src + (256 * rank + 64 * cc + 8 * k) * 2);
           }
           #pragma unroll
           for (int k = 0; k < 4; ++k)
@@ -822,12 +950,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && ntiles > 0) {
       tma_prefetch_desc(&p.tm_kv);
-      mbar_arrive_expect_tx(bar_q, G::kQBytes);
-      for (int c = 0; c < 4; ++c)
-        tma_load_2d(sQ + c * G::kQLatBytes, &p.tm_q, 64 * (4 * static_cast<int>(rank) + c),
-                    b * p.rows + row0, bar_q);
-      tma_load_2d(sQ + 4 * G::kQLatBytes, &p.tm_q_rope, rope_x, b * p.rows + row0, bar_q);
-      const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
+      stage_q();
+      TileWalk w, wp;  // this tile, and the tile kSt ahead (L2 prefetch)
+      w.init(p, u0, start0, g0);
+      wp.init(p, u0, start0, g0);
+      for (int k = 0; k < kSt && k + 1 < ntiles; ++k) wp.next(p);
       int issued = 0;
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % kSt;
@@ -835,20 +962,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         if (t >= kSt)
           ok = mbar_wait(bar_empty + 8 * s, ((t - kSt) / kSt) & 1);
         else if (s >= G::kQStage)
-          ok = mbar_wait(bar_qready, 0);  // Q_r has left these stages
+          ok = mbar_wait(bar_qfree, 0);  // the first Q_r has left these stages
         if (!ok) {
           raise(kStatusWaitTimeout);
           break;
         }
-        int page = __ldg(bt + pg0 + t);
+        const int* bt = p.block_table + static_cast<size_t>(w.u / p.n_hg) * p.max_blocks;
+        int page = __ldg(bt + w.i);
         if (page < 0 || page >= p.num_blocks) {
           raise(kStatusBadPage);
           page = 0;
         }
         const uint32_t st = sRing + s * G::kStageBytes;
         mbar_arrive_expect_tx(bar_full + 8 * s, G::kStageBytes);
-        for (int c = 0; c < 4; ++c)
-          tma_load_2d(st + c * kColBytes, &p.tm_kv, 64 * (4 * static_cast<int>(rank) + c),
+        for (int cc = 0; cc < 4; ++cc)
+          tma_load_2d(st + cc * kColBytes, &p.tm_kv, 64 * (4 * static_cast<int>(rank) + cc),
                       page * kPage, bar_full + 8 * s);
         tma_load_2d(st + 4 * kColBytes, &p.tm_kv_rope, rope_x, page * kPage, bar_full + 8 * s);
         issued = t + 1;
@@ -856,13 +984,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         // until its PV completes, so the ring alone would expose the full
         // DRAM latency once per kSt tiles.
         if (t + kSt < ntiles) {
-          const int pf = __ldg(bt + pg0 + t + kSt);
+          const int* btp = p.block_table + static_cast<size_t>(wp.u / p.n_hg) * p.max_blocks;
+          const int pf = __ldg(btp + wp.i);
           if (pf >= 0 && pf < p.num_blocks) {
-            for (int c = 0; c < 4; ++c)
-              tma_prefetch_2d(&p.tm_kv, 64 * (4 * static_cast<int>(rank) + c), pf * kPage);
+            for (int cc = 0; cc < 4; ++cc)
+              tma_prefetch_2d(&p.tm_kv, 64 * (4 * static_cast<int>(rank) + cc), pf * kPage);
             tma_prefetch_2d(&p.tm_kv_rope, rope_x, pf * kPage);
           }
+          if (t + kSt + 1 < ntiles) wp.next(p);
         }
+        if (t + 1 < ntiles) w.next(p);
       }
       // every issued copy has landed before the CTA may exit
       if (!mbar_wait(bar_q, 0)) raise(kStatusWaitTimeout);
@@ -874,16 +1005,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     constexpr uint32_t idesc_qk = umma_idesc_bf16(128, 64, false, false);
     constexpr uint32_t idesc_pv = umma_idesc_bf16(128, 256, false, true);
     bool ok = true;
-    if (ntiles > 0) ok = wait_warp(bar_qready, 0);
-    int qk = 0, pv = 0;
+    int qk = 0, pv = 0, qseg = 0;
+    TileWalk wq, wv;  // the next QK's tile, the next PV's tile
+    if (ntiles > 0) {
+      wq.init(p, u0, start0, g0);
+      wv.init(p, u0, start0, g0);
+    }
     unsigned long long idle_since = global_timer_ns();
     while (ok && pv < ntiles) {
       int action = 0;  // 1 = PV(pv), 2 = QK(qk)
       if (lane == 0) {
+        // the first QK of a unit waits for its Q_r in tensor memory
+        const bool q_first = qk == 0 || wq.i == 0;
         if (pv < qk && mbar_test_wait(bar_pfull, pv & 1)) {
           action = 1;
         } else if (qk < ntiles && mbar_test_wait(bar_full + 8 * (qk % kSt), (qk / kSt) & 1) &&
-                   (qk == 0 || mbar_test_wait(bar_sfree, (qk - 1) & 1))) {
+                   (qk == 0 || mbar_test_wait(bar_sfree, (qk - 1) & 1)) &&
+                   (!q_first || mbar_test_wait(bar_qready, qseg & 1))) {
           action = 2;
         }
       }
@@ -899,9 +1037,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       if (p.sparse_idx) fence_proxy_async_smem();
       if (action == 2) {
         const uint32_t kv = sRing + (qk % kSt) * G::kStageBytes;
-        // zero the cache rows past the request's end in its last page (they
-        // may hold anything, NaN included): 0 * NaN would poison O
-        const int nv = min(kPage, S - (pg0 + qk) * kPage);
+        // zero the cache rows past the unit's end in its last tile (they may
+        // hold anything, NaN included): 0 * NaN would poison O
+        const int nv = min(kPage, wq.S - wq.i * kPage);
         if (nv < kPage) {
           const int zrows = kPage - nv;
           for (int i = lane; i < 36 * zrows; i += 32) {
@@ -932,8 +1070,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
           umma_commit(bar_sfull);
         }
         __syncwarp();
+        if (qk == 0 || wq.i == 0) ++qseg;
         ++qk;
+        if (qk < ntiles) wq.next(p);
       } else {
+        // the first PV of a unit starts O afresh
+        const bool first = pv == 0 || wv.i == 0;
         if (lane == 0) {
           const uint32_t kv = sRing + (pv % kSt) * G::kStageBytes;
           const uint64_t bv = umma_smem_desc(kv, kColBytes, 1024, kSwizzle128);
@@ -941,12 +1083,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
           for (int kk = 0; kk < 4; ++kk)
             umma_bf16_ts(tmem + G::kOCol, tmem + G::kPCol + 8 * kk,
                          bv + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_pv,
-                         (pv | kk) != 0);
+                         (first ? kk : 1) != 0);
           umma_commit(bar_pv);
           umma_commit(bar_empty + 8 * (pv % kSt));
         }
         __syncwarp();
         ++pv;
+        if (pv < ntiles) wv.next(p);
       }
     }
     if (!ok) raise(kStatusWaitTimeout);
@@ -982,7 +1125,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       tc_fence_after();
       uint32_t r[4][16];
       #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lane_base_s + G::kSCol + 16 * c, r[c]);
+      for (int cc = 0; cc < 4; ++cc) tmem_ld16(tmem + lane_base_s + G::kSCol + 16 * cc, r[cc]);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -1001,21 +1144,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     if (!ok) raise(kStatusWaitTimeout);
   } else {
     // ------------------------- softmax warps 2..9 ----------------------------
-    // Warp w owns query rows h = 32 (w % 4) + lane (TMEM lane quadrant w % 4)
-    // and token columns 32 hf .. 32 hf + 31 of every tile, hf = (w - 2) / 4;
-    // the two warps of a quadrant agree on each tile's row max through
-    // shared memory.  Every softmax warp runs the same named-barrier
-    // sequence whatever happens (a failed wait only clears `ok`).
+    // Warp w owns TMEM lane quadrant w % 4 (rows h = 32 (w % 4) + lane) and
+    // tokens 32 hf .. 32 hf + 31 of every tile, hf = (w - 2) / 4; the two
+    // warps of a quadrant agree on each tile's row max through shared memory.
+    // Every softmax warp runs the same barrier sequence whatever happens (a
+    // failed wait only clears `ok`).
     const int q4 = warp & 3, hf = (warp - 2) >> 2;
     const int h = 32 * q4 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
-    const int row = row0 + h;
-    const bool valid = row < p.rows;
-    const int vis = valid ? visible(p, S, row) : 0;
-    const uint32_t peer_x = mapa_shared(sX, peer);
-    const uint32_t peer_xfull = mapa_shared(bar_xfull, peer);
     const uint32_t peer_xfree = mapa_shared(bar_xfree, peer);
-    float* red = reinterpret_cast<float*>(smem + G::kSmall + 256);  // [2 tiles][2 halves][128]
+    float* red = reinterpret_cast<float*>(smem + G::kSmall + G::kRed);  // [3][2][128]
     bool ok = true;
     auto wait_pv = [&](int k) {  // completion of PV(k): phase k of bar_pv
       if (k >= 0 && ok && !wait_warp(bar_pv, k & 1)) ok = false;
@@ -1030,21 +1168,98 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       }
       if (!__all_sync(0xffffffffu, done)) ok = false;
     };
-    // Q_r row h: staged (swizzled) in the ring -> tensor memory columns
-    // kQCol.. (two bf16 per column); padding rows are zero.  Chunks j of 16
-    // columns: 0-4 by the first warp of the quadrant, 5-8 by the second.
+    // this CTA's partial scores of tile t, this warp's rows and tokens
+    auto read_s = [&](int t, float (&x)[32]) {
+      if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
+      tc_fence_after();
+      uint32_t r[2][16];
+      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf, r[0]);
+      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf + 16, r[1]);
+      tmem_wait_ld();
+      #pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        x[k] = __uint_as_float(r[0][k]);
+        x[16 + k] = __uint_as_float(r[1][k]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree);
+    };
+    if (ntiles > 0 && warp == 2 && lane == 0) {
+      mbar_arrive_expect_tx(bar_xfull, G::kXBytes);
+      if (ntiles > 1) mbar_arrive_expect_tx(bar_xfull + 8, G::kXBytes);
+    }
+    // Q_r of unit uq's row h into tensor memory columns kQCol.. (two bf16 per
+    // column; padding rows zero); chunks j of 16 columns: 0-4 by the first
+    // warp of the quadrant, 5-8 by the second.  Called once every QK of the
+    // previous unit has completed (its last partial scores were read).
+    auto load_q = [&](int uq) {
+      const int bq = uq / p.n_hg, rowq = (uq % p.n_hg) * 128 + h;
+      const bool validq = rowq < p.rows;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          p.q + (static_cast<size_t>(bq) * p.rows + (validq ? rowq : 0)) * kD);
+      // two groups of chunks (3 + 2), each loaded in full before it is stored
+      #pragma unroll
+      for (int grp = 0; grp < 2; ++grp) {
+        uint4 v[3][4];
+        #pragma unroll
+        for (int jj = 0; jj < 3; ++jj) {
+          const int j = 5 * hf + 3 * grp + jj;
+          #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int u16 = j < 8 ? (256 * static_cast<int>(rank) + 32 * j) / 8 + k
+                                  : (512 + 32 * static_cast<int>(rank)) / 8 + k;
+            v[jj][k] = validq && j < 9 && 3 * grp + jj < 5 ? __ldg(src + u16)
+                                                            : make_uint4(0, 0, 0, 0);
+          }
+        }
+        #pragma unroll
+        for (int jj = 0; jj < 3; ++jj) {
+          const int j = 5 * hf + 3 * grp + jj;
+          if (j < 9 && 3 * grp + jj < 5) {
+            uint32_t r[16];
+            #pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              r[4 * k] = v[jj][k].x;
+              r[4 * k + 1] = v[jj][k].y;
+              r[4 * k + 2] = v[jj][k].z;
+              r[4 * k + 3] = v[jj][k].w;
+            }
+            tmem_st16(tmem + lane_base + G::kQCol + 16 * j, r);
+          }
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_qready);
+    };
+    TileWalk w;
+    if (ntiles == 0 && p.per_unit) {
+      // one unit per pair and no selected token: zero rows, lse = -inf
+      const int b = u0 / p.n_hg, row = (u0 % p.n_hg) * 128 + h;
+      if (row < p.rows) {
+        uint4* dst = reinterpret_cast<uint4*>(
+            p.out + (static_cast<size_t>(b) * p.rows + row) * kDV + 256 * rank + 128 * hf);
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) dst[e] = make_uint4(0, 0, 0, 0);
+        if (rank == 0 && hf == 0)
+          p.lse[(static_cast<size_t>(b) * p.h_q + row % p.h_q) * p.s_q + row / p.h_q] = -INFINITY;
+      }
+    }
     if (ntiles > 0) {
+      w.init(p, u0, start0, g0);
+      // the first unit's Q_r from the ring (128-byte swizzled latent boxes,
+      // 64-byte swizzled rope box) into tensor memory
       if (ok && !wait_warp(bar_q, 0)) ok = false;
+      const bool valid0 = (u0 % p.n_hg) * 128 + h < p.rows;
       #pragma unroll 1
       for (int j = 5 * hf; j < (hf ? 9 : 5); ++j) {
         uint32_t r[16];
         #pragma unroll
         for (int k = 0; k < 4; ++k) {
           uint4 v = make_uint4(0, 0, 0, 0);
-          if (valid) {
-            // j < 8: latent box j / 2, 16-byte chunks 4 (j % 2) + k of the
-            // 128-byte row (swizzle: chunk ^ (h & 7)); j = 8: the 64-byte
-            // rope row (swizzle: chunk ^ ((h >> 1) & 3))
+          if (valid0) {
             const uint32_t a =
                 j < 8 ? sQ + (j >> 1) * G::kQLatBytes + h * 128 +
                             (((4 * (j & 1) + k) ^ (h & 7)) << 4)
@@ -1064,174 +1279,189 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       fence_proxy_async_smem();  // our reads precede the TMA writes into these stages
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_qready);
+      if (lane == 0) {
+        mbar_arrive(bar_qfree);
+        mbar_arrive(bar_qready);
+      }
     }
-    // The sender warps push this CTA's partial of every tile into the peer's
-    // exchange buffer X[t & 1] (two tiles deep).  Here iteration t reads this
-    // CTA's partial of tile t + 1 out of tensor memory first (freeing S for
-    // QK(t + 2)), then adds the peer's partial of tile t and runs its
-    // softmax.  X layout: [16 token quads][128 rows] of 16-byte chunks.
-    auto read_s = [&](int t, float (&x)[32]) {
-      if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
-      tc_fence_after();
-      uint32_t r[2][16];
-      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf, r[0]);
-      tmem_ld16(tmem + lane_base + G::kSCol + 32 * hf + 16, r[1]);
-      tmem_wait_ld();
-      #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        x[k] = __uint_as_float(r[0][k]);
-        x[16 + k] = __uint_as_float(r[1][k]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_sfree);
-    };
-    float m_ref = -INFINITY, l = 0.f;
-    float xn[32];
-    if (ntiles > 0) {
-      if (warp == 2 && lane == 0) {
-        mbar_arrive_expect_tx(bar_xfull, G::kXBytes);
-        if (ntiles > 1) mbar_arrive_expect_tx(bar_xfull + 8, G::kXBytes);
-      }
-      read_s(0, xn);
-    }
-    for (int t = 0; t < ntiles; ++t) {
-      float x[32];
-      #pragma unroll
-      for (int k = 0; k < 32; ++k) x[k] = xn[k];
-      if (t + 1 < ntiles) read_s(t + 1, xn);
-      const int j = t & 1;
-      wait_cluster(bar_xfull + 8 * j, (t >> 1) & 1);
-      uint32_t dep = 0;
-      #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        float4 o;
-        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                     : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
-                     : "r"(sX + j * G::kXBytes + ((8 * hf + g) * 128 + h) * 16)
-                     : "memory");
-        // S_0 + S_1 in both CTAs (addition commutes: identical bits)
-        x[4 * g] += o.x;
-        x[4 * g + 1] += o.y;
-        x[4 * g + 2] += o.z;
-        x[4 * g + 3] += o.w;
-        dep ^= __float_as_uint(o.x) ^ __float_as_uint(o.w);
-      }
-      // every lane's reads are complete once all lanes produced dep; then the
-      // peer may overwrite the buffer (with tile t + 2, armed here)
-      dep = __reduce_xor_sync(0xffffffffu, dep);
-      if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree + 8 * j, dep);
-      if (warp == 2 && lane == 0 && t + 2 < ntiles)
-        mbar_arrive_expect_tx(bar_xfull + 8 * j, G::kXBytes);
-      // scores in the log2 domain, masked past the row's visible range
-      const int nvis = min(32, max(0, vis - (pg0 + t) * kPage - 32 * hf));
-      float mt = -INFINITY;
-      #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        x[k] = k < nvis ? x[k] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, x[k]);
-      }
-      // the row max over both halves of the tile
-      red[(j * 2 + hf) * 128 + h] = mt;
-      named_bar_sync(1 + q4, 64);
-      mt = fmaxf(mt, red[(j * 2 + (hf ^ 1)) * 128 + h]);
-      const bool need = mt > m_ref + kRescaleLog2;
-      if (__any_sync(0xffffffffu, need)) {
-        float alpha = 1.f;
-        if (need) {
-          alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
-          m_ref = mt;
-          l *= alpha;
+    int t = 0;
+    while (t < ntiles) {
+      // ---- a segment: tiles i0 .. i0 + len - 1 of unit w.u ----
+      const int u = w.u, b = u / p.n_hg, hg = u % p.n_hg, S = w.S, n_u = w.n;
+      const int i0 = w.i, len = min(n_u - i0, ntiles - t);
+      const int row0 = hg * 128, row = row0 + h;
+      const bool valid = row < p.rows;
+      const int vis = valid ? visible(p, S, row) : 0;
+      if (i0 == 0 && rank == 0 && warp == 2 && lane == 0) p.unit_info[u] = make_int2(w.start, n_u);
+      // the next unit (if the range goes on) and its Q rows into L2 now, a
+      // whole segment before they are loaded
+      const bool has_next = t + len < ntiles;
+      TileWalk wn = w;
+      if (has_next) {
+        for (int k = 0; k < len; ++k) wn.next(p);
+        const int rown = (wn.u % p.n_hg) * 128 + h;
+        if (rown < p.rows) {
+          const char* qr = reinterpret_cast<const char*>(
+              p.q + (static_cast<size_t>(wn.u / p.n_hg) * p.rows + rown) * kD);
+          #pragma unroll
+          for (int l = 0; l < 4; ++l) prefetch_l2(qr + 512 * rank + 128 * l);
+          prefetch_l2(qr + 2 * rope_x);
         }
-        if (t >= 1) {
-          // this warp's 128 of the row's O columns *= alpha once every
-          // earlier PV has accumulated into them
-          wait_pv(t - 1);
-          tc_fence_after();
-          #pragma unroll 1
-          for (int c = 0; c < 8; ++c) {
-            uint32_t r[16];
-            const uint32_t a = tmem + lane_base + G::kOCol + 128 * hf + 16 * c;
-            tmem_ld16(a, r);
-            tmem_wait_ld();
-            #pragma unroll
-            for (int k = 0; k < 16; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * alpha);
-            tmem_st16(a, r);
+      }
+      // the unit's online softmax over the segment; iteration k reads its
+      // partial of the next tile of the segment first (freeing S for the
+      // QK after it), then adds the peer's partial of tile t + k
+      float m_ref = -INFINITY, l = 0.f;
+      float xn[32];
+      read_s(t, xn);
+      for (int k = 0; k < len; ++k) {
+        const int tt = t + k, i = i0 + k;
+        float x[32];
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) x[e] = xn[e];
+        if (k + 1 < len) read_s(tt + 1, xn);
+        const int j = tt & 1;
+        wait_cluster(bar_xfull + 8 * j, (tt >> 1) & 1);
+        uint32_t dep = 0;
+        #pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float4 o;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(o.x), "=f"(o.y), "=f"(o.z), "=f"(o.w)
+                       : "r"(sX + j * G::kXBytes + ((8 * hf + g) * 128 + h) * 16)
+                       : "memory");
+          // S_0 + S_1 in both CTAs (addition commutes: identical bits)
+          x[4 * g] += o.x;
+          x[4 * g + 1] += o.y;
+          x[4 * g + 2] += o.z;
+          x[4 * g + 3] += o.w;
+          dep ^= __float_as_uint(o.x) ^ __float_as_uint(o.w);
+        }
+        // every lane's reads are complete once all lanes produced dep; then
+        // the peer may overwrite the buffer (with tile tt + 2, armed here)
+        dep = __reduce_xor_sync(0xffffffffu, dep);
+        if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree + 8 * j, dep);
+        if (warp == 2 && lane == 0 && tt + 2 < ntiles)
+          mbar_arrive_expect_tx(bar_xfull + 8 * j, G::kXBytes);
+        // scores in the log2 domain, masked past the row's visible range
+        const int nvis = min(32, max(0, vis - i * kPage - 32 * hf));
+        float mt = -INFINITY;
+        #pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          x[e] = e < nvis ? x[e] * p.scale_log2 : -INFINITY;
+          mt = fmaxf(mt, x[e]);
+        }
+        // the row max over both halves of the tile
+        red[(j * 2 + hf) * 128 + h] = mt;
+        named_bar_sync(1 + q4, 64);
+        mt = fmaxf(mt, red[(j * 2 + (hf ^ 1)) * 128 + h]);
+        const bool need = mt > m_ref + kRescaleLog2;
+        if (__any_sync(0xffffffffu, need)) {
+          float alpha = 1.f;
+          if (need) {
+            alpha = m_ref == -INFINITY ? 0.f : exp2f(m_ref - mt);
+            m_ref = mt;
+            l *= alpha;
           }
-          tmem_wait_st();
+          if (k >= 1) {
+            // this warp's 128 of the row's O columns *= alpha once every
+            // earlier PV has accumulated into them
+            wait_pv(tt - 1);
+            tc_fence_after();
+            #pragma unroll 1
+            for (int cc = 0; cc < 8; ++cc) {
+              uint32_t r[16];
+              const uint32_t a = tmem + lane_base + G::kOCol + 128 * hf + 16 * cc;
+              tmem_ld16(a, r);
+              tmem_wait_ld();
+              #pragma unroll
+              for (int e = 0; e < 16; ++e)
+                r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+              tmem_st16(a, r);
+            }
+            tmem_wait_st();
+          }
         }
+        // P = 2^(x - m_ref) as bf16 pairs; the buffer is free once PV(tt - 1)
+        // (of this unit or the previous one) is done
+        uint32_t pk[16];
+        #pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float p0 = x[2 * e] == -INFINITY ? 0.f : fast_exp2(x[2 * e] - m_ref);
+          const float p1 = x[2 * e + 1] == -INFINITY ? 0.f : fast_exp2(x[2 * e + 1] - m_ref);
+          l += p0 + p1;
+          pk[e] = pack2(p0, p1);
+        }
+        wait_pv(tt - 1);
+        tc_fence_after();
+        tmem_st16(tmem + lane_base + G::kPCol + 16 * hf, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_pfull);
       }
-      // P = 2^(x - m_ref) as bf16 pairs; the buffer is free once PV(t - 1) is done
-      uint32_t pk[16];
-      #pragma unroll
-      for (int k = 0; k < 16; ++k) {
-        const float p0 = x[2 * k] == -INFINITY ? 0.f : fast_exp2(x[2 * k] - m_ref);
-        const float p1 = x[2 * k + 1] == -INFINITY ? 0.f : fast_exp2(x[2 * k + 1] - m_ref);
-        l += p0 + p1;
-        pk[k] = pack2(p0, p1);
-      }
-      wait_pv(t - 1);
+      // the next unit's Q now: its QK and partial-score exchange overlap
+      // this unit's epilogue (every QK of this unit is done: its last
+      // partial scores were read above)
+      if (has_next) load_q(wn.u);
+      // ---- the segment's epilogue ----
+      const int t_last = t + len - 1;
+      wait_pv(t_last);
       tc_fence_after();
-      tmem_st16(tmem + lane_base + G::kPCol + 16 * hf, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_pfull);
-    }
-    // ------------------------------ epilogue ---------------------------------
-    wait_pv(ntiles - 1);
-    tc_fence_after();
-    if (!ok) raise(kStatusWaitTimeout);
-    // the row sum over both halves
-    red[(2 * 2 + hf) * 128 + h] = l;
-    named_bar_sync(1 + q4, 64);
-    l += red[(2 * 2 + (hf ^ 1)) * 128 + h];
-    const bool final_out = p.num_splits == 1;
-    const int dv0 = 256 * static_cast<int>(rank) + 128 * hf;
-    const size_t grow = static_cast<size_t>(b) * p.rows + (valid ? row : 0);
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
-      uint32_t r[16];
-      if (ntiles > 0) {
-        tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * c, r);
-        tmem_wait_ld();
-      } else {
-        #pragma unroll
-        for (int k = 0; k < 16; ++k) r[k] = 0u;
-      }
-      if (!valid) continue;
-      if (final_out) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out + grow * kDV + dv0 + 16 * c);
-        uint32_t w[8];
-        #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          w[k] = pack2(__uint_as_float(r[2 * k]) * inv, __uint_as_float(r[2 * k + 1]) * inv);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      } else {
-        float4* dst = reinterpret_cast<float4*>(p.part_acc + (grow * p.num_splits + sp) * kDV +
-                                                dv0 + 16 * c);
-        #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          dst[k] = l > 0.f ? make_float4(__uint_as_float(r[4 * k]), __uint_as_float(r[4 * k + 1]),
-                                         __uint_as_float(r[4 * k + 2]),
-                                         __uint_as_float(r[4 * k + 3]))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
-    if (rank == 0 && hf == 0 && valid) {
+      red[(2 * 2 + hf) * 128 + h] = l;
+      named_bar_sync(1 + q4, 64);
+      l += red[(2 * 2 + (hf ^ 1)) * 128 + h];
       const float m = l > 0.f ? m_ref : -INFINITY;
-      if (final_out) {
-        const int i = row / p.h_q, hq = row % p.h_q;
-        p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + i] =
-            l > 0.f ? (m + log2f(l)) * 0.69314718056f : -INFINITY;
+      const int dv0 = 256 * static_cast<int>(rank) + 128 * hf;
+      const size_t grow = static_cast<size_t>(b) * p.rows + (valid ? row : 0);
+      const int qi = row / p.h_q, hq = row % p.h_q;
+      if (i0 == 0 && len == n_u) {
+        // the whole unit in this pair: the final rows
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        #pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * cc, r);
+          tmem_wait_ld();
+          if (!valid) continue;
+          uint4* dst = reinterpret_cast<uint4*>(p.out + grow * kDV + dv0 + 16 * cc);
+          uint32_t wv[8];
+          #pragma unroll
+          for (int e = 0; e < 8; ++e)
+            wv[e] = pack2(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
+          dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        }
+        if (rank == 0 && hf == 0 && valid)
+          p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + qi] =
+              l > 0.f ? (m + log2f(l)) * 0.69314718056f : -INFINITY;
       } else {
-        p.part_m[grow * p.num_splits + sp] = m;
-        p.part_l[grow * p.num_splits + sp] = l;
+        // a partial state in this pair's slot (its first or its last unit)
+        const int slot = 2 * c + (t == 0 ? 0 : 1);  // c < Pe <= P
+        float* acc = p.slot_acc + (static_cast<size_t>(slot) * 128 + h) * kDV;
+        #pragma unroll 1
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t r[16];
+          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * cc, r);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(acc + dv0 + 16 * cc);
+          #pragma unroll
+          for (int e = 0; e < 4; ++e)
+            dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                 __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+        }
+        if (rank == 0 && hf == 0) {  // identical in both CTAs of the pair
+          p.slot_m[static_cast<size_t>(slot) * 128 + h] = m;
+          p.slot_l[static_cast<size_t>(slot) * 128 + h] = l;
+        }
+        // mla_rows_combine_kernel merges the unit's partial states
       }
+      tc_fence_before();
+      // next segment: the next unit's first tile
+      t += len;
+      w = wn;
     }
+    if (!ok) raise(kStatusWaitTimeout);
   }
   tc_fence_before();
   __syncthreads();
@@ -1240,6 +1470,75 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     tmem_dealloc(tmem, 512);
   }
   cluster_sync();  // no CTA leaves while its peer may still address its shared memory
+}
+
+// Units of the persistent 128-row kernel that were split between pairs:
+// merge their partial states (one per pair) into out and lse; also the
+// output of units with no tokens, which no pair visits.  Block = (unit, 16
+// rows), warp = 4 rows, lane = 16 of the 512 value dims.
+__global__ void __launch_bounds__(128)
+    mla_rows_combine_kernel(const __grid_constant__ Params p) {
+  const int u = blockIdx.x >> 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long T = p.hdr[0];
+  const int Pe = p.hdr[1];
+  const int n_u = (unit_tokens(p, u) + kPage - 1) / kPage;
+  int start = 0, c_first = 0, nseg = 0;
+  if (n_u > 0 && Pe == 0) return;  // one unit per pair: written by its pair
+  if (n_u > 0) {
+    const int2 info = p.unit_info[u];
+    start = info.x;
+    c_first = pair_of(start, T, Pe);
+    nseg = pair_of(static_cast<long long>(start) + n_u - 1, T, Pe) - c_first + 1;
+    if (nseg <= 1) return;  // written by its pair
+  }
+  const int b = u / p.n_hg, hg = u % p.n_hg;
+  for (int rr = 0; rr < 4; ++rr) {
+    const int h = (blockIdx.x & 7) * 16 + warp * 4 + rr;
+    const int row = hg * 128 + h;
+    if (row >= p.rows) continue;
+    float M = -INFINITY, L = 0.f;
+    float a[16];
+    #pragma unroll
+    for (int e = 0; e < 16; ++e) a[e] = 0.f;
+    for (int k = 0; k < nseg; ++k) {
+      const int ck = c_first + k;
+      const int sk = 2 * ck + (pair_start(ck, T, Pe) >= start ? 0 : 1);
+      M = fmaxf(M, __ldcg(p.slot_m + static_cast<size_t>(sk) * 128 + h));
+    }
+    for (int k = 0; k < nseg; ++k) {
+      const int ck = c_first + k;
+      const int sk = 2 * ck + (pair_start(ck, T, Pe) >= start ? 0 : 1);
+      const float mk = __ldcg(p.slot_m + static_cast<size_t>(sk) * 128 + h);
+      if (mk == -INFINITY) continue;
+      const float w = exp2f(mk - M);
+      L += w * __ldcg(p.slot_l + static_cast<size_t>(sk) * 128 + h);
+      const float4* src =
+          reinterpret_cast<const float4*>(p.slot_acc + (static_cast<size_t>(sk) * 128 + h) * kDV) +
+          4 * lane;
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 v = __ldcg(src + e);
+        a[4 * e] += w * v.x;
+        a[4 * e + 1] += w * v.y;
+        a[4 * e + 2] += w * v.z;
+        a[4 * e + 3] += w * v.w;
+      }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(b) * p.rows + row) * kDV) +
+                 2 * lane;
+    uint32_t wv[8];
+    #pragma unroll
+    for (int e = 0; e < 8; ++e) wv[e] = pack2(a[2 * e] * inv, a[2 * e + 1] * inv);
+    dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+    if (lane == 0) {
+      const int i = row / p.h_q, hq = row % p.h_q;
+      p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + i] =
+          L > 0.f ? (M + log2f(L)) * 0.69314718056f : -INFINITY;
+    }
+  }
 }
 
 // Merge of the num_splits partial states of every (request, query row):
@@ -1368,6 +1667,32 @@ Layout layout_for(int rows) {
   return L;
 }
 
+// 128-row groups run persistent on half the SMs' worth of CTA pairs.
+int rows_pairs() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms / 2 > 0 ? sms / 2 : 1;
+}
+
+// Workspace of the persistent 128-row kernel: the tile count and working
+// pairs, per-unit first tile and tile count, partial max and sum [2 P][128],
+// partial O [2 P][128][512].
+struct RowsWs {
+  size_t hdr, info, m, l, acc, total;
+};
+RowsWs rows_ws(int units, int P) {
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  RowsWs w{};
+  w.hdr = 0;
+  w.info = 256;
+  w.m = w.info + up(static_cast<size_t>(units) * sizeof(int2));
+  w.l = w.m + up(static_cast<size_t>(2) * P * 128 * sizeof(float));
+  w.acc = w.l + up(static_cast<size_t>(2) * P * 128 * sizeof(float));
+  w.total = w.acc + static_cast<size_t>(2) * P * 128 * kDV * sizeof(float);
+  return w;
+}
+
 size_t part_bytes(int B, int rows, int ns) {
   const size_t states = static_cast<size_t>(B) * rows * ns;
   const size_t acc = states * kDV * sizeof(float);
@@ -1384,6 +1709,7 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
   const int rows = s_q * h_q;
   const Layout L = layout_for(rows);
   if (L.NH == 0 || B <= 0 || num_sms <= 0) return 1;
+  if (L.NH == 128) return 1;  // persistent, balanced by tiles: no splits
   const long long units = static_cast<long long>(B) * L.n_hg;
   // Cost model over CTA-pair waves: each split is a pair that pays a fixed
   // start (tensor memory, Q staging, the first pages' latency) worth about
@@ -1408,7 +1734,10 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
 }
 
 size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits) {
-  if (B <= 0 || s_q <= 0 || h_q <= 0 || num_splits <= 1) return 0;
+  if (B <= 0 || s_q <= 0 || h_q <= 0) return 0;
+  const Layout L = layout_for(s_q * h_q);
+  if (L.NH == 128) return rows_ws(B * L.n_hg, rows_pairs()).total;  // persistent, any num_splits
+  if (num_splits <= 1) return 0;
   return part_bytes(B, s_q * h_q, num_splits);
 }
 
@@ -1458,10 +1787,27 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
   p.n_hg = L.n_hg;
   p.max_blocks = max_blocks;
   p.num_blocks = num_blocks;
-  p.num_splits = num_splits;
+  p.num_splits = L.NH == 128 ? 1 : num_splits;
   p.causal = causal ? 1 : 0;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  if (num_splits > 1) {
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  int P = L.NH == 128 ? rows_pairs() : 0;
+  // Sparse selections are near-uniform units: with at least as many units
+  // as pairs, whole units per pair (in waves) beat balanced ranges plus the
+  // partial-state merge (measured); otherwise and for dense caches the
+  // persistent balanced schedule.
+  p.per_unit = L.NH == 128 && sparse_idx && B * L.n_hg >= P ? 1 : 0;
+  if (L.NH == 128) {
+    const RowsWs wl = rows_ws(B * L.n_hg, P);
+    if (!workspace || workspace_bytes < wl.total || !aligned16(workspace))
+      return cudaErrorInvalidValue;
+    unsigned char* w = static_cast<unsigned char*>(workspace);
+    p.hdr = reinterpret_cast<int*>(w + wl.hdr);
+    p.unit_info = reinterpret_cast<int2*>(w + wl.info);
+    p.slot_m = reinterpret_cast<float*>(w + wl.m);
+    p.slot_l = reinterpret_cast<float*>(w + wl.l);
+    p.slot_acc = reinterpret_cast<float*>(w + wl.acc);
+  } else if (num_splits > 1) {
     const size_t need = part_bytes(B, rows, num_splits);
     if (!workspace || workspace_bytes < need || !aligned16(workspace)) return cudaErrorInvalidValue;
     const size_t states = static_cast<size_t>(B) * rows * num_splits;
@@ -1488,12 +1834,23 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
       if (x != cudaSuccess) attr_err = x;
   });
   if (attr_err != cudaSuccess) return attr_err;
+  if (L.NH == 128) {
+    // persistent pairs over the batch's tiles, then the split units' merge
+    const long long pairs = p.per_unit ? static_cast<long long>(B) * L.n_hg : P;
+    if (2 * pairs > 0x7fffffffLL) return cudaErrorInvalidValue;
+    mla_decode_rows_kernel<<<static_cast<unsigned>(2 * pairs), Rows::kThreads, Rows::kSmem,
+                             stream>>>(p);
+    const cudaError_t e1 = cudaGetLastError();
+    if (e1 != cudaSuccess || p.per_unit) return e1;  // one unit per pair: nothing to merge
+    const long long blocks = static_cast<long long>(B) * L.n_hg * 8;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+    mla_rows_combine_kernel<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(p);
+    return cudaGetLastError();
+  }
   const long long grid = 2LL * B * L.n_hg * num_splits;  // 2-CTA clusters
   if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
   const unsigned g = static_cast<unsigned>(grid);
-  if (L.NH == 128)
-    mla_decode_rows_kernel<<<g, Rows::kThreads, Rows::kSmem, stream>>>(p);
-  else if (L.NH == 64)
+  if (L.NH == 64)
     mla_decode_kernel<64><<<g, kThreads, L.smem, stream>>>(p);
   else if (L.NH == 32)
     mla_decode_kernel<32><<<g, kThreads, L.smem, stream>>>(p);
