@@ -17,7 +17,14 @@
 //   mla_decode_rows_kernel   groups of 128 query rows: rows on M, Q and P as
 //                            tensor-memory A operands, one softmax thread per
 //                            row, sender warps for the exchange; also the
-//                            sparse mode (rows of selected tokens).
+//                            sparse mode (rows of selected tokens).  Dense:
+//                            persistent, one pair per two SMs, each pair an
+//                            equal share of the batch's 64-token tiles (a
+//                            unit cut between pairs leaves one partial state
+//                            per pair, merged by mla_rows_combine_kernel).
+//                            Sparse: also one whole unit per pair (no
+//                            merge) when a measured cost fit predicts that
+//                            faster (near-uniform selections, full waves).
 // Online softmax in the log2 domain with a lazily raised reference max: P is
 // computed against the current reference m_ref and O / l are only rescaled
 // when a tile's score exceeds m_ref by more than 2^8 (the bound on exp2
@@ -28,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <mutex>
@@ -59,7 +67,7 @@ struct Params {
   const __nv_bfloat16* q;    // 128-row groups: q rows (loaded straight into tensor memory)
   int* hdr;                  // 128-row groups: [2] total tiles T and working pairs Pe (0: one unit per pair)
   int per_unit;              // 128-row groups: pair c takes unit c whole (no balancing, no partials)
-  int2* unit_info;           // 128-row groups: [units] first tile and tile count
+  int4* unit_info;           // 128-row groups: [units] first slot, first pair, pairs
   float* slot_m;             // 128-row groups: [2 P][128] partial max (log2 domain)
   float* slot_l;             // 128-row groups: [2 P][128] partial sums
   float* slot_acc;           // 128-row groups: [2 P][128][512] unnormalised partial O
@@ -672,13 +680,17 @@ struct Rows {
 
 // Tiles (64-token pages, or 64 selected tokens) of work unit u = (request
 // b = u / n_hg, 128-row group hg = u % n_hg).
-__device__ __forceinline__ int unit_tokens(const Params& p, int u) {
+__device__ __forceinline__ const int* unit_len_ptr(const Params& p, int u) {
   const int b = u / p.n_hg, hg = u % p.n_hg;
-  if (p.sparse_idx) {
-    const int qpos = (hg * 128) / p.h_q;
-    return max(0, min(p.seq_lens[b * p.s_q + qpos], p.topk));
-  }
-  return max(0, min(p.seq_lens[b], p.max_blocks * kPage));
+  return p.sparse_idx ? p.seq_lens + b * p.s_q + (hg * 128) / p.h_q : p.seq_lens + b;
+}
+
+__device__ __forceinline__ int unit_clamp(const Params& p, int len) {
+  return max(0, min(len, p.sparse_idx ? p.topk : p.max_blocks * kPage));
+}
+
+__device__ __forceinline__ int unit_tokens(const Params& p, int u) {
+  return unit_clamp(p, *unit_len_ptr(p, u));
 }
 
 // A walk over the pair's range of the batch's tiles, unit by unit (every
@@ -823,9 +835,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       mbar_init(bar_xfull + 8 * j, 1);  // armed with the byte count here, bytes from the peer
       mbar_init(bar_xfree + 8 * j, 8);  // the peer's eight softmax warps have read our partial
     }
-    mbar_init(bar_qready, 8);  // a unit's Q_r is in tensor memory
+    mbar_init(bar_qready, 4);  // a unit's Q_r is in tensor memory (one arrival per sender warp)
     mbar_init(bar_q, 1);       // the first unit's Q_r has landed in the ring
-    mbar_init(bar_qfree, 8);   // ... and has been copied out of it
+    mbar_init(bar_qfree, 4);   // ... and has been copied out of it
     mbar_init(bar_fin, 1);
     fence_mbar_init();
   }
@@ -916,25 +928,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         }
         __syncwarp();  // the queue entries other lanes wrote are visible
         // slots past the selection take the tile's first row (their scores are
-        // masked, so P = 0 there)
+        // masked, so P = 0 there).  Lane L holds rows 2L and 2L + 1; one warp
+        // instruction then copies 512 contiguous bytes of one row (the CTA's
+        // latent half: lane -> box lane / 8, 16-byte chunk lane % 8), four
+        // 128-byte lines instead of one line per lane, with the row index
+        // broadcast by shuffle; the 64-byte rope halves go eight rows per
+        // instruction.
         const int first = q_t[0];
+        const int ra = q_t[2 * lane] < 0 ? first : q_t[2 * lane];
+        const int rb = q_t[2 * lane + 1] < 0 ? first : q_t[2 * lane + 1];
         const uint32_t st = sRing + s * G::kStageBytes;
+        const uint32_t dl = st + (lane >> 3) * kColBytes;
+        const int cl = lane & 7;
+        const char* kvl = kvb + 512 * rank + 16 * lane;
         #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int r = 2 * lane + u;  // slot = row within the stage
-          const int row = q_t[r] < 0 ? first : q_t[r];
-          const char* src = kvb + static_cast<size_t>(row) * (kD * 2);
-          #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              cp_async_16(st + cc * kColBytes + r * 128 + ((k ^ (r & 7)) << 4),
-                          src + (256 * rank + 64 * cc + 8 * k) * 2);
-          }
-          #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            cp_async_16(st + 4 * kColBytes + r * 64 + ((k ^ ((r >> 1) & 3)) << 4),
-                        src + (rope_x + 8 * k) * 2);
+        for (int r = 0; r < kPage; ++r) {
+          const int row = __shfl_sync(0xffffffffu, (r & 1) ? rb : ra, r >> 1);
+          cp_async_16(dl + r * 128 + ((cl ^ (r & 7)) << 4),
+                      kvl + static_cast<size_t>(row) * (kD * 2));
+        }
+        #pragma unroll
+        for (int i = 0; i < kPage / 8; ++i) {
+          const int r = 8 * i + (lane >> 2), k = lane & 3;
+          const int xa = __shfl_sync(0xffffffffu, ra, r >> 1);
+          const int xb = __shfl_sync(0xffffffffu, rb, r >> 1);
+          const int row = (r & 1) ? xb : xa;
+          cp_async_16(st + 4 * kColBytes + r * 64 + ((k ^ ((r >> 1) & 3)) << 4),
+                      kvb + static_cast<size_t>(row) * (kD * 2) + 2 * rope_x + 16 * k);
         }
         cp_async_mbar_arrive(bar_full + 8 * s);  // one of the stage's 32 arrivals
         issued = t + 1;
@@ -1098,11 +1118,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
     __syncwarp();
     if (!wait_warp(bar_fin, 0)) raise(kStatusWaitTimeout);
   } else if (warp >= 10) {
-    // -------------------- sender warps 10..13: partials out -------------------
+    // -------------------- sender warps 10..13: partials out, Q_r in ----------
     // Warp w (TMEM lane quadrant w % 4) reads this CTA's partial scores of
     // its 32 rows, all 64 tokens, and stores them into the peer's exchange
     // buffer: the ~16 bytes per cycle the pair's link moves no longer stall
-    // the softmax warps.
+    // the softmax warps.  The same warps put each unit's Q_r rows of their
+    // quadrant into tensor memory: the first unit's from the ring stages
+    // TMA filled, every later one straight from global memory (prefetched
+    // into L2 four tiles earlier) as soon as the previous unit's last QK is
+    // done, while the softmax warps finish that unit.
     const int qs = warp & 3;
     const int hs = 32 * qs + lane;
     const uint32_t lane_base_s = static_cast<uint32_t>(32 * qs) << 16;
@@ -1119,8 +1143,105 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       }
       if (!__all_sync(0xffffffffu, done)) ok = false;
     };
+    // Q_r of unit uq, row hs, from global memory: nine chunks of 16 columns
+    // (two bf16 each; chunks 0-7 this CTA's latent dims, 8 its rope dims),
+    // three chunks in flight at a time; padding rows zero
+    auto row_ptr = [&](int uq, bool& valid) {
+      const int rowq = (uq % p.n_hg) * 128 + hs;
+      valid = rowq < p.rows;
+      return reinterpret_cast<const uint4*>(
+          p.q + (static_cast<size_t>(uq / p.n_hg) * p.rows + (valid ? rowq : 0)) * kD);
+    };
+    auto col16 = [&](int j) {  // first 16-byte unit of chunk j in the row
+      return j < 8 ? (256 * static_cast<int>(rank) + 32 * j) / 8
+                   : (512 + 32 * static_cast<int>(rank)) / 8;
+    };
+    auto load_q = [&](int uq) {
+      bool valid;
+      const uint4* src = row_ptr(uq, valid);
+      #pragma unroll 1
+      for (int j0 = 0; j0 < 9; j0 += 3) {
+        uint4 v[3][4];
+        #pragma unroll
+        for (int jj = 0; jj < 3; ++jj)
+          #pragma unroll
+          for (int k = 0; k < 4; ++k)
+            v[jj][k] = valid ? __ldg(src + col16(j0 + jj) + k) : make_uint4(0, 0, 0, 0);
+        #pragma unroll
+        for (int jj = 0; jj < 3; ++jj) {
+          uint32_t r[16];
+          #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            r[4 * k] = v[jj][k].x;
+            r[4 * k + 1] = v[jj][k].y;
+            r[4 * k + 2] = v[jj][k].z;
+            r[4 * k + 3] = v[jj][k].w;
+          }
+          tmem_st16(tmem + lane_base_s + G::kQCol + 16 * (j0 + jj), r);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_qready);
+    };
+    auto prefetch_q = [&](int uq) {
+      bool valid;
+      const char* src = reinterpret_cast<const char*>(row_ptr(uq, valid));
+      if (!valid) return;
+      #pragma unroll
+      for (int l = 0; l < 4; ++l) prefetch_l2(src + 512 * rank + 128 * l);
+      prefetch_l2(src + 2 * rope_x);
+    };
+    TileWalk ws;  // the tile being sent
+    if (ntiles > 0) {
+      ws.init(p, u0, start0, g0);
+      // the first unit's Q_r from the ring (128-byte swizzled latent boxes,
+      // 64-byte swizzled rope box)
+      if (ok && !wait_warp(bar_q, 0)) ok = false;
+      const bool valid0 = (u0 % p.n_hg) * 128 + hs < p.rows;
+      #pragma unroll 1
+      for (int j = 0; j < 9; ++j) {
+        uint32_t r[16];
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (valid0) {
+            const uint32_t a =
+                j < 8 ? sQ + (j >> 1) * G::kQLatBytes + hs * 128 +
+                            (((4 * (j & 1) + k) ^ (hs & 7)) << 4)
+                      : sQ + 4 * G::kQLatBytes + hs * 64 + ((k ^ ((hs >> 1) & 3)) << 4);
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                         : "r"(a));
+          }
+          r[4 * k] = v.x;
+          r[4 * k + 1] = v.y;
+          r[4 * k + 2] = v.z;
+          r[4 * k + 3] = v.w;
+        }
+        tmem_st16(tmem + lane_base_s + G::kQCol + 16 * j, r);
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();  // our reads precede the TMA writes into these stages
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(bar_qfree);
+        mbar_arrive(bar_qready);
+      }
+    }
     for (int t = 0; t < ntiles; ++t) {
       const int j = t & 1;
+      // this tile ends its unit and the range goes on: the next unit
+      const bool unit_end = ws.i == ws.n - 1 && t + 1 < ntiles;
+      const int left = ws.n - 1 - ws.i;  // tiles of the unit after this one
+      if ((left == 4 || (t == 0 && left < 4)) && t + left + 1 < ntiles) {
+        TileWalk wn = ws;
+        wn.i = wn.n - 1;
+        wn.next(p);
+        prefetch_q(wn.u);
+      }
       if (ok && !wait_warp(bar_sfull, t & 1)) ok = false;
       tc_fence_after();
       uint32_t r[4][16];
@@ -1137,6 +1258,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         st_async_v4(peer_x + j * G::kXBytes + (g * 128 + hs) * 16, r[g >> 2][4 * (g & 3)],
                     r[g >> 2][4 * (g & 3) + 1], r[g >> 2][4 * (g & 3) + 2],
                     r[g >> 2][4 * (g & 3) + 3], peer_xfull + 8 * j);
+      if (t + 1 < ntiles) ws.next(p);
+      // every QK of the unit has completed (its last partials were read):
+      // the next unit's rows may replace Q_r
+      if (unit_end) load_q(ws.u);
     }
     // the peer has read our last two partials before either CTA may exit
     for (int t = max(0, ntiles - 2); t < ntiles; ++t)
@@ -1189,51 +1314,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       mbar_arrive_expect_tx(bar_xfull, G::kXBytes);
       if (ntiles > 1) mbar_arrive_expect_tx(bar_xfull + 8, G::kXBytes);
     }
-    // Q_r of unit uq's row h into tensor memory columns kQCol.. (two bf16 per
-    // column; padding rows zero); chunks j of 16 columns: 0-4 by the first
-    // warp of the quadrant, 5-8 by the second.  Called once every QK of the
-    // previous unit has completed (its last partial scores were read).
-    auto load_q = [&](int uq) {
-      const int bq = uq / p.n_hg, rowq = (uq % p.n_hg) * 128 + h;
-      const bool validq = rowq < p.rows;
-      const uint4* src = reinterpret_cast<const uint4*>(
-          p.q + (static_cast<size_t>(bq) * p.rows + (validq ? rowq : 0)) * kD);
-      // two groups of chunks (3 + 2), each loaded in full before it is stored
-      #pragma unroll
-      for (int grp = 0; grp < 2; ++grp) {
-        uint4 v[3][4];
-        #pragma unroll
-        for (int jj = 0; jj < 3; ++jj) {
-          const int j = 5 * hf + 3 * grp + jj;
-          #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int u16 = j < 8 ? (256 * static_cast<int>(rank) + 32 * j) / 8 + k
-                                  : (512 + 32 * static_cast<int>(rank)) / 8 + k;
-            v[jj][k] = validq && j < 9 && 3 * grp + jj < 5 ? __ldg(src + u16)
-                                                            : make_uint4(0, 0, 0, 0);
-          }
-        }
-        #pragma unroll
-        for (int jj = 0; jj < 3; ++jj) {
-          const int j = 5 * hf + 3 * grp + jj;
-          if (j < 9 && 3 * grp + jj < 5) {
-            uint32_t r[16];
-            #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              r[4 * k] = v[jj][k].x;
-              r[4 * k + 1] = v[jj][k].y;
-              r[4 * k + 2] = v[jj][k].z;
-              r[4 * k + 3] = v[jj][k].w;
-            }
-            tmem_st16(tmem + lane_base + G::kQCol + 16 * j, r);
-          }
-        }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_qready);
-    };
     TileWalk w;
     if (ntiles == 0 && p.per_unit) {
       // one unit per pair and no selected token: zero rows, lse = -inf
@@ -1247,43 +1327,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
           p.lse[(static_cast<size_t>(b) * p.h_q + row % p.h_q) * p.s_q + row / p.h_q] = -INFINITY;
       }
     }
-    if (ntiles > 0) {
-      w.init(p, u0, start0, g0);
-      // the first unit's Q_r from the ring (128-byte swizzled latent boxes,
-      // 64-byte swizzled rope box) into tensor memory
-      if (ok && !wait_warp(bar_q, 0)) ok = false;
-      const bool valid0 = (u0 % p.n_hg) * 128 + h < p.rows;
-      #pragma unroll 1
-      for (int j = 5 * hf; j < (hf ? 9 : 5); ++j) {
-        uint32_t r[16];
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (valid0) {
-            const uint32_t a =
-                j < 8 ? sQ + (j >> 1) * G::kQLatBytes + h * 128 +
-                            (((4 * (j & 1) + k) ^ (h & 7)) << 4)
-                      : sQ + 4 * G::kQLatBytes + h * 64 + ((k ^ ((h >> 1) & 3)) << 4);
-            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                         : "r"(a));
-          }
-          r[4 * k] = v.x;
-          r[4 * k + 1] = v.y;
-          r[4 * k + 2] = v.z;
-          r[4 * k + 3] = v.w;
-        }
-        tmem_st16(tmem + lane_base + G::kQCol + 16 * j, r);
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();  // our reads precede the TMA writes into these stages
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(bar_qfree);
-        mbar_arrive(bar_qready);
-      }
-    }
+    if (ntiles > 0) w.init(p, u0, start0, g0);
     int t = 0;
     while (t < ntiles) {
       // ---- a segment: tiles i0 .. i0 + len - 1 of unit w.u ----
@@ -1292,28 +1336,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       const int row0 = hg * 128, row = row0 + h;
       const bool valid = row < p.rows;
       const int vis = valid ? visible(p, S, row) : 0;
-      if (i0 == 0 && rank == 0 && warp == 2 && lane == 0) p.unit_info[u] = make_int2(w.start, n_u);
-      // the next unit (if the range goes on) and its Q rows into L2 now, a
-      // whole segment before they are loaded
+      // the unit's first tile is here: its partial-state layout for the
+      // combine pass (pairs c .. c + nseg - 1; this pair's slot for it)
+      if (i0 == 0 && !p.per_unit && rank == 0 && warp == 2 && lane == 0)
+        p.unit_info[u] = make_int4(2 * c + (t == 0 ? 0 : 1), c,
+                                   pair_of(static_cast<long long>(w.start) + n_u - 1, T, Pe) - c + 1,
+                                   0);
+      // the range goes on past this unit (then the segment runs to its end)
       const bool has_next = t + len < ntiles;
-      TileWalk wn = w;
-      if (has_next) {
-        for (int k = 0; k < len; ++k) wn.next(p);
-        const int rown = (wn.u % p.n_hg) * 128 + h;
-        if (rown < p.rows) {
-          const char* qr = reinterpret_cast<const char*>(
-              p.q + (static_cast<size_t>(wn.u / p.n_hg) * p.rows + rown) * kD);
-          #pragma unroll
-          for (int l = 0; l < 4; ++l) prefetch_l2(qr + 512 * rank + 128 * l);
-          prefetch_l2(qr + 2 * rope_x);
-        }
-      }
       // the unit's online softmax over the segment; iteration k reads its
       // partial of the next tile of the segment first (freeing S for the
       // QK after it), then adds the peer's partial of tile t + k
       float m_ref = -INFINITY, l = 0.f;
       float xn[32];
       read_s(t, xn);
+      // the following unit's length, loaded now so that moving on to it
+      // costs no memory round trip (nothing is added to the tile loop: its
+      // schedule is sensitive to extra work)
+      const int len_next = has_next ? __ldg(unit_len_ptr(p, w.u + 1)) : 0;
       for (int k = 0; k < len; ++k) {
         const int tt = t + k, i = i0 + k;
         float x[32];
@@ -1340,7 +1380,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         // every lane's reads are complete once all lanes produced dep; then
         // the peer may overwrite the buffer (with tile tt + 2, armed here)
         dep = __reduce_xor_sync(0xffffffffu, dep);
-        if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree + 8 * j, dep);
+        // (the segment's last buffer is released after the epilogue, which
+        // uses it as scratch)
+        if (lane == 0 && k + 1 < len) mbar_arrive_remote_relaxed(peer_xfree + 8 * j, dep);
         if (warp == 2 && lane == 0 && tt + 2 < ntiles)
           mbar_arrive_expect_tx(bar_xfull + 8 * j, G::kXBytes);
         // scores in the log2 domain, masked past the row's visible range
@@ -1400,11 +1442,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_pfull);
       }
-      // the next unit's Q now: its QK and partial-score exchange overlap
-      // this unit's epilogue (every QK of this unit is done: its last
-      // partial scores were read above)
-      if (has_next) load_q(wn.u);
-      // ---- the segment's epilogue ----
+      // ---- the segment's epilogue (the sender warps have meanwhile put the
+      // next unit's Q_r into tensor memory, so its first QK and exchange
+      // overlap this) ----
       const int t_last = t + len - 1;
       wait_pv(t_last);
       tc_fence_after();
@@ -1413,42 +1453,88 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
       l += red[(2 * 2 + (hf ^ 1)) * 128 + h];
       const float m = l > 0.f ? m_ref : -INFINITY;
       const int dv0 = 256 * static_cast<int>(rank) + 128 * hf;
-      const size_t grow = static_cast<size_t>(b) * p.rows + (valid ? row : 0);
       const int qi = row / p.h_q, hq = row % p.h_q;
+      // The rows leave through a 4 KB scratch area of this warp in the
+      // exchange buffer of the segment's last tile (read above; the peer
+      // refills it only after the release below): each lane writes its row's
+      // 128 bytes of a pass (16-byte chunks XOR-swizzled by row), then the
+      // warp stores four rows of 128 contiguous bytes per instruction
+      // instead of 32 rows of 16.
+      const uint32_t scr = sX + (t_last & 1) * G::kXBytes + (warp - 2) * 4096;
+      auto put = [&](int ch, uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                         scr + lane * 128 + ((ch ^ (lane & 7)) << 4)),
+                     "r"(x0), "r"(x1), "r"(x2), "r"(x3)
+                     : "memory");
+      };
+      uint32_t dep = 0;
+      // pass rows out: the eight 16-byte chunks of row rr of the scratch
+      auto drain = [&](auto&& store) {
+        __syncwarp();
+        #pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3), ch = lane & 7;
+          uint4 v;
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                       : "r"(scr + rr * 128 + ((ch ^ (rr & 7)) << 4))
+                       : "memory");
+          dep ^= v.x;
+          store(32 * q4 + rr, ch, v);
+        }
+        __syncwarp();
+      };
       if (i0 == 0 && len == n_u) {
-        // the whole unit in this pair: the final rows
+        // the whole unit in this pair: the final rows, 64 value dims a pass
         const float inv = l > 0.f ? 1.f / l : 0.f;
         #pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t r[16];
-          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * cc, r);
-          tmem_wait_ld();
-          if (!valid) continue;
-          uint4* dst = reinterpret_cast<uint4*>(p.out + grow * kDV + dv0 + 16 * cc);
-          uint32_t wv[8];
-          #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            wv[e] = pack2(__uint_as_float(r[2 * e]) * inv, __uint_as_float(r[2 * e + 1]) * inv);
-          dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+        for (int ps = 0; ps < 2; ++ps) {
+          #pragma unroll 1
+          for (int cc = 0; cc < 4; cc += 2) {
+            uint32_t r[2][16];
+            tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 64 * ps + 16 * cc, r[0]);
+            tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 64 * ps + 16 * cc + 16, r[1]);
+            tmem_wait_ld();
+            #pragma unroll
+            for (int x = 0; x < 2; ++x) {
+              uint32_t wv[8];
+              #pragma unroll
+              for (int e = 0; e < 8; ++e)
+                wv[e] = pack2(__uint_as_float(r[x][2 * e]) * inv,
+                              __uint_as_float(r[x][2 * e + 1]) * inv);
+              put(2 * (cc + x), wv[0], wv[1], wv[2], wv[3]);
+              put(2 * (cc + x) + 1, wv[4], wv[5], wv[6], wv[7]);
+            }
+          }
+          drain([&](int hr, int ch, uint4 v) {
+            const int orow = row0 + hr;
+            if (orow < p.rows)
+              *reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(b) * p.rows + orow) * kDV +
+                                        dv0 + 64 * ps + 8 * ch) = v;
+          });
         }
         if (rank == 0 && hf == 0 && valid)
           p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + qi] =
               l > 0.f ? (m + log2f(l)) * 0.69314718056f : -INFINITY;
       } else {
-        // a partial state in this pair's slot (its first or its last unit)
+        // a partial state in this pair's slot (its first or its last unit),
+        // 32 value dims a pass
         const int slot = 2 * c + (t == 0 ? 0 : 1);  // c < Pe <= P
-        float* acc = p.slot_acc + (static_cast<size_t>(slot) * 128 + h) * kDV;
+        float* acc = p.slot_acc + static_cast<size_t>(slot) * 128 * kDV;
         #pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t r[16];
-          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 16 * cc, r);
+        for (int ps = 0; ps < 4; ++ps) {
+          uint32_t r[2][16];
+          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 32 * ps, r[0]);
+          tmem_ld16(tmem + lane_base + G::kOCol + 128 * hf + 32 * ps + 16, r[1]);
           tmem_wait_ld();
-          float4* dst = reinterpret_cast<float4*>(acc + dv0 + 16 * cc);
           #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
-                                 __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+          for (int x = 0; x < 2; ++x)
+            #pragma unroll
+            for (int e = 0; e < 4; ++e)
+              put(4 * x + e, r[x][4 * e], r[x][4 * e + 1], r[x][4 * e + 2], r[x][4 * e + 3]);
+          drain([&](int hr, int ch, uint4 v) {
+            *reinterpret_cast<uint4*>(acc + static_cast<size_t>(hr) * kDV + dv0 + 32 * ps + 4 * ch) = v;
+          });
         }
         if (rank == 0 && hf == 0) {  // identical in both CTAs of the pair
           p.slot_m[static_cast<size_t>(slot) * 128 + h] = m;
@@ -1456,10 +1542,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         }
         // mla_rows_combine_kernel merges the unit's partial states
       }
+      // the scratch reads are done: the peer may refill the buffer
+      dep = __reduce_xor_sync(0xffffffffu, dep);
+      if (lane == 0) mbar_arrive_remote_relaxed(peer_xfree + 8 * (t_last & 1), dep);
       tc_fence_before();
       // next segment: the next unit's first tile
       t += len;
-      w = wn;
+      if (has_next) {
+        const int n_next = (unit_clamp(p, len_next) + kPage - 1) / kPage;
+        if (n_next > 0) {  // the usual case: the next unit has tiles
+          w.start += w.n;
+          ++w.u;
+          w.i = 0;
+          w.S = unit_clamp(p, len_next);
+          w.n = n_next;
+        } else {
+          w.i = w.n - 1;
+          w.next(p);
+        }
+      }
     }
     if (!ok) raise(kStatusWaitTimeout);
   }
@@ -1474,71 +1575,100 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
 
 // Units of the persistent 128-row kernel that were split between pairs:
 // merge their partial states (one per pair) into out and lse; also the
-// output of units with no tokens, which no pair visits.  Block = (unit, 16
-// rows), warp = 4 rows, lane = 16 of the 512 value dims.
-__global__ void __launch_bounds__(128)
+// output of units with no tokens, which no pair visits.  One warp per query
+// row (eight rows per block): lane k < nseg loads segment k's max and sum
+// (warp-reduced), then every lane merges 16 of the 512 value dims, four
+// segments' loads in flight at a time.  The unit's layout (first slot,
+// first pair, pairs) was recorded by the pair that ran its first tile:
+// segment 0 is in that slot, segment k > 0 in slot 2 (first pair + k),
+// where it opens that pair's range.
+__global__ void __launch_bounds__(256)
     mla_rows_combine_kernel(const __grid_constant__ Params p) {
-  const int u = blockIdx.x >> 3;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long T = p.hdr[0];
-  const int Pe = p.hdr[1];
+  const int u = blockIdx.x >> 4, h = (blockIdx.x & 15) * 8 + warp;
+  const int b = u / p.n_hg, row = (u % p.n_hg) * 128 + h;
+  const int4 info = __ldcg(p.unit_info + u);  // in flight with the token count
   const int n_u = (unit_tokens(p, u) + kPage - 1) / kPage;
-  int start = 0, c_first = 0, nseg = 0;
-  if (n_u > 0 && Pe == 0) return;  // one unit per pair: written by its pair
+  if (row >= p.rows) return;
+  int s0 = 0, c0 = 0, nseg = 0;
   if (n_u > 0) {
-    const int2 info = p.unit_info[u];
-    start = info.x;
-    c_first = pair_of(start, T, Pe);
-    nseg = pair_of(static_cast<long long>(start) + n_u - 1, T, Pe) - c_first + 1;
+    s0 = info.x;
+    c0 = info.y;
+    nseg = info.z;
     if (nseg <= 1) return;  // written by its pair
   }
-  const int b = u / p.n_hg, hg = u % p.n_hg;
-  for (int rr = 0; rr < 4; ++rr) {
-    const int h = (blockIdx.x & 7) * 16 + warp * 4 + rr;
-    const int row = hg * 128 + h;
-    if (row >= p.rows) continue;
-    float M = -INFINITY, L = 0.f;
-    float a[16];
+  auto slot = [&](int k) { return static_cast<size_t>(k == 0 ? s0 : 2 * (c0 + k)) * 128 + h; };
+  float M = -INFINITY, L = 0.f;
+  float4 a[4];
+  #pragma unroll
+  for (int d = 0; d < 4; ++d) a[d] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < nseg; k0 += 32) {
+    // this group's maxima and sums, one segment per lane
+    const int kl = k0 + lane;
+    const float ml = kl < nseg ? __ldcg(p.slot_m + slot(kl)) : -INFINITY;
+    const float ll = kl < nseg ? __ldcg(p.slot_l + slot(kl)) : 0.f;
+    float mg = ml;
     #pragma unroll
-    for (int e = 0; e < 16; ++e) a[e] = 0.f;
-    for (int k = 0; k < nseg; ++k) {
-      const int ck = c_first + k;
-      const int sk = 2 * ck + (pair_start(ck, T, Pe) >= start ? 0 : 1);
-      M = fmaxf(M, __ldcg(p.slot_m + static_cast<size_t>(sk) * 128 + h));
+    for (int off = 16; off > 0; off >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, off));
+    const float mn = fmaxf(M, mg);
+    // rescale what earlier groups merged (at most one group below 32 pairs)
+    const float r = M == -INFINITY ? 0.f : exp2f(M - mn);
+    L *= r;
+    #pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      a[d].x *= r;
+      a[d].y *= r;
+      a[d].z *= r;
+      a[d].w *= r;
     }
-    for (int k = 0; k < nseg; ++k) {
-      const int ck = c_first + k;
-      const int sk = 2 * ck + (pair_start(ck, T, Pe) >= start ? 0 : 1);
-      const float mk = __ldcg(p.slot_m + static_cast<size_t>(sk) * 128 + h);
-      if (mk == -INFINITY) continue;
-      const float w = exp2f(mk - M);
-      L += w * __ldcg(p.slot_l + static_cast<size_t>(sk) * 128 + h);
-      const float4* src =
-          reinterpret_cast<const float4*>(p.slot_acc + (static_cast<size_t>(sk) * 128 + h) * kDV) +
-          4 * lane;
+    M = mn;
+    const float wl = ml == -INFINITY ? 0.f : exp2f(ml - M);
+    float ls = wl * ll;
+    #pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+    L += ls;
+    const int ng = min(32, nseg - k0);
+    for (int e0 = 0; e0 < ng; e0 += 4) {
+      float4 v[4][4];
+      float w[4];
       #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float4 v = __ldcg(src + e);
-        a[4 * e] += w * v.x;
-        a[4 * e + 1] += w * v.y;
-        a[4 * e + 2] += w * v.z;
-        a[4 * e + 3] += w * v.w;
+        w[e] = __shfl_sync(0xffffffffu, wl, (e0 + e) & 31);
+        if (e0 + e < ng) {
+          const float4* src =
+              reinterpret_cast<const float4*>(p.slot_acc + slot(k0 + e0 + e) * kDV) + 4 * lane;
+          #pragma unroll
+          for (int d = 0; d < 4; ++d) v[e][d] = __ldcg(src + d);
+        } else {
+          w[e] = 0.f;
+          #pragma unroll
+          for (int d = 0; d < 4; ++d) v[e][d] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        #pragma unroll
+        for (int d = 0; d < 4; ++d) {
+          a[d].x += w[e] * v[e][d].x;
+          a[d].y += w[e] * v[e][d].y;
+          a[d].z += w[e] * v[e][d].z;
+          a[d].w += w[e] * v[e][d].w;
+        }
       }
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    uint4* dst = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(b) * p.rows + row) * kDV) +
-                 2 * lane;
-    uint32_t wv[8];
-    #pragma unroll
-    for (int e = 0; e < 8; ++e) wv[e] = pack2(a[2 * e] * inv, a[2 * e + 1] * inv);
-    dst[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-    dst[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
-    if (lane == 0) {
-      const int i = row / p.h_q, hq = row % p.h_q;
-      p.lse[(static_cast<size_t>(b) * p.h_q + hq) * p.s_q + i] =
-          L > 0.f ? (M + log2f(L)) * 0.69314718056f : -INFINITY;
-    }
   }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  uint4* dst =
+      reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(b) * p.rows + row) * kDV + 16 * lane);
+  #pragma unroll
+  for (int d = 0; d < 2; ++d)
+    dst[d] = make_uint4(pack2(a[2 * d].x * inv, a[2 * d].y * inv),
+                        pack2(a[2 * d].z * inv, a[2 * d].w * inv),
+                        pack2(a[2 * d + 1].x * inv, a[2 * d + 1].y * inv),
+                        pack2(a[2 * d + 1].z * inv, a[2 * d + 1].w * inv));
+  if (lane == 0)
+    p.lse[(static_cast<size_t>(b) * p.h_q + row % p.h_q) * p.s_q + row / p.h_q] =
+        L > 0.f ? (M + log2f(L)) * 0.69314718056f : -INFINITY;
 }
 
 // Merge of the num_splits partial states of every (request, query row):
@@ -1667,12 +1797,34 @@ Layout layout_for(int rows) {
   return L;
 }
 
-// 128-row groups run persistent on half the SMs' worth of CTA pairs.
+// 128-row groups run persistent on as many CTA pairs as fit on the device
+// at once: at most half the SMs, fewer when the GPCs' SM counts leave some
+// SMs without a cluster partner (cached per device).
 int rows_pairs() {
-  int dev = 0, sms = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms / 2 > 0 ? sms / 2 : 1;
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  v = sms / 2 > 0 ? sms / 2 : 1;
+  int n = 0;
+  using gqa::mla::Rows;
+  using gqa::mla::mla_decode_rows_kernel;
+  if (cudaFuncSetAttribute(mla_decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Rows::kSmem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * v);
+    cfg.blockDim = dim3(Rows::kThreads);
+    cfg.dynamicSmemBytes = Rows::kSmem;
+    if (cudaOccupancyMaxActiveClusters(&n, mla_decode_rows_kernel, &cfg) == cudaSuccess && n > 0 &&
+        n < v)
+      v = n;
+  }
+  cudaGetLastError();  // a failed query leaves the SM-count bound
+  cache[dev].store(v, std::memory_order_relaxed);
+  return v;
 }
 
 // Workspace of the persistent 128-row kernel: the tile count and working
@@ -1686,7 +1838,7 @@ RowsWs rows_ws(int units, int P) {
   RowsWs w{};
   w.hdr = 0;
   w.info = 256;
-  w.m = w.info + up(static_cast<size_t>(units) * sizeof(int2));
+  w.m = w.info + up(static_cast<size_t>(units) * sizeof(int4));
   w.l = w.m + up(static_cast<size_t>(2) * P * 128 * sizeof(float));
   w.acc = w.l + up(static_cast<size_t>(2) * P * 128 * sizeof(float));
   w.total = w.acc + static_cast<size_t>(2) * P * 128 * kDV * sizeof(float);
@@ -1792,18 +1944,29 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.q = reinterpret_cast<const __nv_bfloat16*>(q);
   int P = L.NH == 128 ? rows_pairs() : 0;
-  // Sparse selections are near-uniform units: with at least as many units
-  // as pairs, whole units per pair (in waves) beat balanced ranges plus the
-  // partial-state merge (measured); otherwise and for dense caches the
-  // persistent balanced schedule.
-  p.per_unit = L.NH == 128 && sparse_idx && B * L.n_hg >= P ? 1 : 0;
+  // Sparse selections make near-uniform units of up to ceil(topk / 64)
+  // tiles.  Whole units per pair (in waves) skip the partial states and
+  // the merge but idle pairs in a short last wave; the balanced split pays
+  // a fixed cost per launch (unit boundaries, the merge pass).  Measured on
+  // B200 (top-k 2048, 128 heads): about 3.3 us per tile + 6 us per wave of
+  // whole units, against 30 us + 3.7 us per tile of the balanced split, so
+  // choose whichever the two fits predict faster.  Dense caches always
+  // take the balanced split.
+  p.per_unit = 0;
+  if (L.NH == 128 && sparse_idx) {
+    const long long U = static_cast<long long>(B) * L.n_hg, nt = (topk + kPage - 1) / kPage;
+    const long long waves = (U + P - 1) / P;
+    const double whole = static_cast<double>(waves) * (3.3 * nt + 6.0);
+    const double balanced = 30.0 + 3.7 * static_cast<double>(U * nt) / P;
+    p.per_unit = whole <= balanced ? 1 : 0;
+  }
   if (L.NH == 128) {
     const RowsWs wl = rows_ws(B * L.n_hg, P);
     if (!workspace || workspace_bytes < wl.total || !aligned16(workspace))
       return cudaErrorInvalidValue;
     unsigned char* w = static_cast<unsigned char*>(workspace);
     p.hdr = reinterpret_cast<int*>(w + wl.hdr);
-    p.unit_info = reinterpret_cast<int2*>(w + wl.info);
+    p.unit_info = reinterpret_cast<int4*>(w + wl.info);
     p.slot_m = reinterpret_cast<float*>(w + wl.m);
     p.slot_l = reinterpret_cast<float*>(w + wl.l);
     p.slot_acc = reinterpret_cast<float*>(w + wl.acc);
@@ -1842,9 +2005,9 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
                              stream>>>(p);
     const cudaError_t e1 = cudaGetLastError();
     if (e1 != cudaSuccess || p.per_unit) return e1;  // one unit per pair: nothing to merge
-    const long long blocks = static_cast<long long>(B) * L.n_hg * 8;
+    const long long blocks = static_cast<long long>(B) * L.n_hg * 16;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
-    mla_rows_combine_kernel<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(p);
+    mla_rows_combine_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
     return cudaGetLastError();
   }
   const long long grid = 2LL * B * L.n_hg * num_splits;  // 2-CTA clusters
