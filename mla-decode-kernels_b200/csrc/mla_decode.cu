@@ -885,30 +885,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         const int* idx = p.sparse_idx + static_cast<size_t>(b * p.s_q + qpos) * p.topk;
         const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
         int* q_t = rowq + (t % (G::kRowAhead + 1)) * kPage;
-        // both token positions, then both block-table entries: two memory
-        // round trips for the lane's two rows, not four
-        int tok[2], pg[2];
-        bool live[2];
         #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int j = wa.i * kPage + 2 * lane + u;
-          live[u] = j < wa.S;
-          tok[u] = live[u] ? __ldg(idx + j) : 0;
-        }
-        #pragma unroll
-        for (int u = 0; u < 2; ++u)
-          pg[u] = live[u] && tok[u] >= 0 && tok[u] < p.max_blocks * kPage ? __ldg(bt + (tok[u] >> 6))
-                                                                        : -1;
-        #pragma unroll
-        for (int u = 0; u < 2; ++u) {
           int row = -1;
-          if (live[u]) {
-            int page = pg[u];
+          if (j < wa.S) {
+            const int tok = __ldg(idx + j);
+            int page = tok >= 0 && tok < p.max_blocks * kPage ? __ldg(bt + (tok >> 6)) : -1;
             if (page < 0 || page >= p.num_blocks) {
               raise(kStatusBadPage);
               page = 0;
             }
-            row = page * kPage + (tok[u] & (kPage - 1));
+            row = page * kPage + (tok & (kPage - 1));
             // this CTA's half of the row into L2 while the tile waits its turn
             const char* rp =
                 reinterpret_cast<const char*>(p.kv) + static_cast<size_t>(row) * (kD * 2);
