@@ -367,7 +367,16 @@ __global__ void __launch_bounds__(kTopkThreads) dsa_topk_kernel(const __grid_con
     return;
   }
   if (kSmemKeys) {
-    for (int t = tid; t < vis; t += blockDim.x) keys[t] = order_key(sc[t]);
+    // eight loads in flight per thread, then their keys
+    int t = tid;
+    for (; t + 7 * kTopkThreads < vis; t += 8 * kTopkThreads) {
+      float v[8];
+      #pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(sc + t + u * kTopkThreads);
+      #pragma unroll
+      for (int u = 0; u < 8; ++u) keys[t + u * kTopkThreads] = order_key(v[u]);
+    }
+    for (; t < vis; t += kTopkThreads) keys[t] = order_key(__ldg(sc + t));
   }
   auto key_at = [&](int t) -> uint32_t { return kSmemKeys ? keys[t] : order_key(sc[t]); };
   const int nch = (vis + blockDim.x - 1) / blockDim.x;
