@@ -31,17 +31,21 @@ extern "C" {
 /* Split count for B requests of up to max_pages 64-token pages on num_sms
  * SMs: the count (1..64, at least two pages per split) minimising a wave
  * cost model of the 2-CTA work units (pages per split plus a fixed start
- * per unit), e.g. 4 for 128 requests of ~8K tokens, 1 for 2K-token sparse
- * selections. */
+ * per unit); larger for few, long requests.  Always 1 when s_q * h_q is a
+ * multiple of 128: those query groups run a persistent kernel that spreads
+ * the batch's pages evenly over the SMs by itself. */
 int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms);
 
-/* Workspace bytes for num_splits > 1 (unnormalised partial states); 0 for
- * num_splits == 1. */
+/* Workspace bytes.  s_q * h_q a multiple of 128: the persistent kernel's
+ * partial states (two per CTA pair) and per-unit layout, whatever
+ * num_splits is (about 39 MB on 148 SMs).  Otherwise the unnormalised
+ * partial states of num_splits > 1, and 0 for num_splits == 1. */
 size_t mla_decode_workspace_bytes(int B, int s_q, int h_q, int num_splits);
 
 /* Decode.  Requirements: page_size == 64; 1 <= num_splits <= 64; q and
- * kv_cache 16-byte aligned; a 16-byte aligned workspace of
- * mla_decode_workspace_bytes() when num_splits > 1.  Block ids outside
+ * kv_cache 16-byte aligned; a 16-byte aligned workspace of at least
+ * mla_decode_workspace_bytes() whenever that is non-zero (calls sharing a
+ * workspace must not overlap on the GPU).  Block ids outside
  * [0, num_blocks) set bit 1 of mla_decode_get_status and read block 0. */
 cudaError_t mla_decode_launch(const gqa_bf16* q, const gqa_bf16* kv_cache, const int* block_table,
                               const int* seq_lens, gqa_bf16* out, float* lse, int B, int s_q,
