@@ -64,6 +64,9 @@ def workspace(device, nbytes):
 
     The balanced schedule's arrival counters live at its start and every
     launch leaves them at zero, so one zeroing serves all later launches.
+    Every stream of the device shares it: decodes that may run at the same
+    time on different streams must not both use it (pass each its own
+    workspace through the C ABI, or order the streams).
     """
     device = torch.device(device)
     key = (device.type, device.index)
