@@ -1863,11 +1863,12 @@ int mla_decode_pick_splits(int B, int s_q, int h_q, int max_pages, int num_sms) 
   if (L.NH == 0 || B <= 0 || num_sms <= 0) return 1;
   if (L.NH == 128) return 1;  // persistent, balanced by tiles: no splits
   const long long units = static_cast<long long>(B) * L.n_hg;
-  // Cost model over CTA-pair waves: each split is a pair that pays a fixed
-  // start (tensor memory, Q staging, the first pages' latency) worth about
-  // five page-times, and splits > 1 add partial states and a combine pass;
-  // measured on B200 (b = 128, h_q = 128) it picks 4 splits for ~8K-token
-  // requests and 1 for 2K-token sparse selections, the fastest of 1-16.
+  // Cost model over CTA-pair waves (groups of fewer than 128 rows): each
+  // split is a pair that pays a fixed start (tensor memory, Q staging, the
+  // first pages' latency) worth about five page-times, and splits > 1 add
+  // partial states and a combine pass.  Fitted on B200 when every group ran
+  // one pair per (unit, split): it picked the fastest of 1-16 splits for
+  // ~8K-token requests and 2K-token selections.
   const long long slots = std::max(1, num_sms / 2);
   const long long cap = std::max(1, std::min(64, max_pages / 2));
   const long long pages = std::max(1, max_pages);
