@@ -168,6 +168,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0 && ntiles > 0) {
       int b = b_first, ord = -1, prev = -1, issued = 0;
+      // page ids of the next tile, loaded while the current one is in flight
+      // (the request's length and table row only when the request changes)
+      int cur_b = -1, pages_b = 0, npg = 0, pid0 = 0, pid1 = 0;
+      const int* bt_b = p.block_table;
+      auto fetch_ids = [&](int t, int bb) {
+        if (bb != cur_b) {
+          cur_b = bb;
+          const int S = max(0, min(p.seq_lens[bb], max_tokens));
+          pages_b = (S + kPage - 1) / kPage;
+          bt_b = p.block_table + static_cast<size_t>(bb) * p.max_blocks;
+        }
+        const int pg = 2 * (g0 + t - tstart[bb]);
+        npg = min(2, pages_b - pg);  // the second page may not exist
+        pid0 = __ldg(bt_b + pg);
+        pid1 = npg > 1 ? __ldg(bt_b + pg + 1) : 0;
+      };
+      fetch_ids(0, b_first);
       for (int t = 0; t < ntiles; ++t) {
         const int g = g0 + t;
         b = req_of(g, b);
@@ -189,14 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           raise(1);
           break;
         }
-        const int S = max(0, min(p.seq_lens[b], max_tokens));
-        const int pages = (S + kPage - 1) / kPage;
-        const int pg = 2 * (g - tstart[b]);
-        const int npg = min(2, pages - pg);  // the second page may not exist
-        const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
-        mbar_arrive_expect_tx(bar_full + 8 * s, static_cast<uint32_t>(npg * 2 * kBox));
-        for (int h = 0; h < npg; ++h) {
-          int page = __ldg(bt + pg + h);
+        const int n = npg;
+        mbar_arrive_expect_tx(bar_full + 8 * s, static_cast<uint32_t>(n * 2 * kBox));
+        for (int h = 0; h < n; ++h) {
+          int page = h ? pid1 : pid0;
           if (page < 0 || page >= p.num_blocks) {
             raise(2);
             page = 0;
@@ -206,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         page * kPage, bar_full + 8 * s);
         }
         issued = t + 1;
+        if (t + 1 < ntiles) fetch_ids(t + 1, req_of(g + 1, b));
       }
       // every issued copy has landed before the CTA may exit
       for (int o = max(0, ord - 1); o <= ord; ++o)
