@@ -35,12 +35,13 @@ def lib():
 
 
 def declared_functions():
-    """Every function declared in include/*.h (gqa_decode_* and mla_decode_*)."""
+    """Every function declared in include/*.h (gqa_decode_*, mla_decode_*, dsa_*)."""
     names = set()
     for h in sorted(glob.glob(os.path.join(REPO, "include", "*.h"))):
         text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
-        names.update(re.findall(r"^\s*(?:const\s+)?[\w]+\s*\*?\s+((?:gqa|mla)_decode_\w+)\s*\(",
-                                text, flags=re.M))
+        names.update(re.findall(
+            r"^\s*(?:const\s+)?[\w]+\s*\*?\s+((?:gqa_decode|mla_decode|dsa)_\w+)\s*\(", text,
+            flags=re.M))
     return sorted(names)
 
 
@@ -142,6 +143,35 @@ def test_pick_splits(lib):
     # a batch that already fills the GPU several times: no split
     assert lib.gqa_decode_pick_splits(4096, 32, 8, 512, 148) == 1
     assert lib.gqa_decode_pick_splits(0, 32, 8, 512, 148) == 1
+
+
+def test_declares_every_header(lib):
+    names = declared_functions()
+    for expected in ("gqa_decode_launch", "mla_decode_launch", "mla_decode_sparse_launch",
+                     "dsa_indexer_launch", "dsa_topk_launch", "dsa_gather_launch",
+                     "dsa_decode_get_status"):
+        assert expected in names
+
+
+def test_mla_splits_and_workspace(lib):
+    lib.mla_decode_pick_splits.argtypes = [ctypes.c_int] * 5
+    lib.mla_decode_pick_splits.restype = ctypes.c_int
+    lib.mla_decode_workspace_bytes.argtypes = [ctypes.c_int] * 4
+    lib.mla_decode_workspace_bytes.restype = ctypes.c_size_t
+    # 128-row query groups run the persistent kernel: one split, and a
+    # workspace (partial states, unit layout) whatever num_splits is
+    assert lib.mla_decode_pick_splits(128, 1, 128, 128, 148) == 1
+    assert lib.mla_decode_pick_splits(4, 2, 64, 4096, 148) == 1  # s_q * h_q = 128
+    for ns in (1, 4):
+        assert lib.mla_decode_workspace_bytes(128, 1, 128, ns) > 0
+        assert lib.mla_decode_workspace_bytes(4, 2, 64, ns) > 0
+    # smaller groups: split partial states only for num_splits > 1
+    assert lib.mla_decode_workspace_bytes(128, 1, 16, 1) == 0
+    assert lib.mla_decode_workspace_bytes(128, 1, 16, 4) >= 128 * 16 * 4 * 512 * 4
+    # one long request with few heads is split; bad shapes fall back to 1
+    assert lib.mla_decode_pick_splits(1, 1, 16, 4096, 148) > 1
+    assert lib.mla_decode_pick_splits(0, 1, 16, 4096, 148) == 1
+    assert lib.mla_decode_workspace_bytes(0, 1, 128, 1) == 0
 
 
 def test_counter_region_grows_for_huge_batches(lib):
