@@ -764,10 +764,30 @@ def run_mla(args, world, rank, local):
                      "algorithmic_bytes_per_launch": int(kv_local),
                      "tensor_achieved_tflops": round(tflops, 1), "tensor_peak_tflops": tc_peak,
                      "tensor_frac": round(tflops / tc_peak, 4)},
-        "gpu_launches": int(args.steps * (1 if ns == 1 else 2)),
+        # 128-row query groups: the persistent kernel and its combine pass
+        "gpu_launches": int(args.steps * (2 if (s_q * h_q) % 128 == 0 or ns > 1 else 1)),
         "clocks": clocks, "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)
+
+
+def dsa_launches_per_step(B, s_q, h_q, topk, ns, sms):
+    """Kernels one sparse decode step launches: indexer, top-k, then for h_q
+    a multiple of 128 the MLA rows kernel over the selection, plus its
+    combine pass when it takes the balanced split (the choice
+    mla_launch_impl makes in mla_decode.cu: whole units per CTA pair in
+    waves, 3.3 us per 64-token tile + 6 us per wave, against 30 us + 3.7 us
+    per tile per pair); otherwise the gather and the MLA decode (+ its merge
+    for splits)."""
+    if h_q % 128 != 0:
+        return 4 + (1 if ns > 1 else 0)
+    units = B * s_q * h_q // 128
+    pairs = max(1, sms // 2)
+    nt = (topk + 63) // 64
+    waves = (units + pairs - 1) // pairs
+    whole = waves * (3.3 * nt + 6.0)
+    balanced = 30.0 + 3.7 * units * nt / pairs
+    return 3 if whole <= balanced else 4
 
 
 def run_dsa(args, world, rank, local):
@@ -940,7 +960,7 @@ def run_dsa(args, world, rank, local):
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": peak_src, "kernel": top,
                      "algorithmic_bytes_per_launch": int(stage_bytes[top])},
-        "gpu_launches": int(args.steps * ((3 if fused else 4) + (0 if ns == 1 else 1))),
+        "gpu_launches": int(args.steps * dsa_launches_per_step(B, s_q, h_q, topk, ns, sms)),
         "clocks": clocks, "cpu_baseline": None,
     }
     print(json.dumps(line), flush=True)
