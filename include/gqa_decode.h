@@ -17,11 +17,14 @@
  * q, k_cache, v_cache, out and any workspace must be 16-byte aligned.
  *
  * Every launcher is asynchronous on `stream`, allocates nothing and does not
- * synchronise.  The first three keep the reference's signatures exactly (a
- * caller compiled against the reference header links against this library
- * unchanged); they return void as the reference does, and report argument
- * errors through gqa_decode_last_error().  The remaining entry points are
- * additions and return cudaError_t.
+ * synchronise.  The first three keep the reference's signatures exactly; they
+ * return void as the reference does, and report argument errors through
+ * gqa_decode_last_error().  This header declares them with C linkage; the
+ * library also exports them with the C++ linkage of the reference header
+ * (include/gqa_decode.h:6-23 there, no extern "C"), so an object compiled
+ * against the reference header - e.g. the reference's own
+ * python/gqa_decode_ext.cpp - links against this library unchanged.  The
+ * remaining entry points are additions and return cudaError_t.
  */
 #ifndef GQA_DECODE_B200_H_
 #define GQA_DECODE_B200_H_
@@ -100,8 +103,9 @@ int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, i
 size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
 
 /* Zero a workspace before its first use.  The balanced schedule keeps
- * per-row arrival counters there and every launch returns them to zero, so
- * one initialisation serves any number of launches and shapes. */
+ * per-row arrival counters there and every launch returns them to zero -
+ * also a launch whose pipeline waits timed out (status bit 0) - so one
+ * initialisation serves any number of launches and shapes. */
 cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
                                       cudaStream_t stream);
 
@@ -242,7 +246,8 @@ cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
  *   B200 with Hkv = 8, up to ~860 requests at Hq = 32 or ~350 at Hq = 64.
  * - The first call on a device looks up the array's device address
  *   (cudaGetSymbolAddress) with that device current; make that first call
- *   before any stream capture.
+ *   before any stream capture.  A first call whose lookup fails returns that
+ *   error and keeps nothing, so a later call tries the lookup again.
  * - All calls on a device share the array and it keeps the previous call's
  *   contents; each call clears the counters it needs on `stream` before its
  *   kernel.  Calls that overlap on the GPU (other streams, other threads)
@@ -271,6 +276,21 @@ cudaError_t gqa_decode_get_status(int* status, int clear);
  * gqa_decode_get_status.  No reference counterpart (the reference has no
  * bounded waits). */
 cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream);
+
+/* Failure-detection self-test of a whole decode: gqa_decode_launch
+ * (num_splits == 0) with every pipeline wait limited to wait_limit_ns
+ * (0..1,000,000) instead of 4 s, so the waits give up while the copies are
+ * still on their way.  Status bit 0 is then set and the rows of the warps
+ * that gave up are wrong (NaN, or merged without their part), but the launch
+ * ends normally, no copy is left in flight, and the workspace's arrival
+ * counters are back at zero: the next gqa_decode_launch on the same
+ * workspace is correct.  No reference counterpart. */
+cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                               const gqa_bf16* v_cache, const int* block_table,
+                                               const int* seq_lens, gqa_bf16* out, int B, int Hq,
+                                               int Hkv, int block_size, int max_blocks,
+                                               float scale, int wait_limit_ns, void* workspace,
+                                               size_t workspace_bytes, cudaStream_t stream);
 
 /* Library version string. */
 const char* gqa_decode_version(void);

@@ -8,6 +8,7 @@
 
 #include "gqa_decode.h"
 #include "gqa_internal.h"
+#include "gqa_ptx.cuh"
 
 namespace gqa {
 
@@ -171,6 +172,7 @@ gqa::ScanParams base_params(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16
   p.stage_bytes = sp.stage_bytes;
   p.nstages = sp.nstages;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_ns = gqa::kWaitLimitNs;
   return p;
 }
 
@@ -282,7 +284,8 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
                          const int* sl, gqa_bf16* out, float* res_m, float* res_l,
                          float* res_acc, int B, int Hq, int Hkv, int bs, int max_blocks,
                          int num_blocks, float scale, void* ws, size_t ws_bytes,
-                         cudaStream_t stream, const Exchange* xchg = nullptr) {
+                         cudaStream_t stream, const Exchange* xchg = nullptr,
+                         unsigned long long wait_ns = gqa::kWaitLimitNs) {
   ShapePlan sp;
   const void* dst = out ? static_cast<const void*>(out) : static_cast<const void*>(res_acc);
   cudaError_t e = check_common(q, k, v, bt, sl, dst, B, Hq, Hkv, bs, max_blocks, &sp);
@@ -328,22 +331,26 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
   p.part_acc = reinterpret_cast<float*>(w + lay.acc);
   p.schedule = gqa::kBalanced;
   p.num_splits = 0;
+  p.wait_ns = wait_ns;
   return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
 }
 
 }  // namespace
 
-extern "C" {
+namespace gqa {
 
-void gqa_decode_v0_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
-                          const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
-                          int Hq, int Hkv, int block_size, int max_blocks, float scale,
-                          cudaStream_t stream) {
+// Bodies of the reference-signature launchers.  The C-linkage entry points
+// below and the C++-linkage ones in gqa_cxx_abi.cu both call these; each
+// records its status for gqa_decode_last_error().
+void compat_v0_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, cudaStream_t stream) {
   ShapePlan sp;
   cudaError_t e = check_common(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv,
                                block_size, max_blocks, &sp);
   if (e == cudaSuccess && B > 0) {
-    gqa::SimtParams p{};
+    SimtParams p{};
     p.q = q;
     p.k = k_cache;
     p.v = v_cache;
@@ -356,17 +363,47 @@ void gqa_decode_v0_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_
     p.bs = block_size;
     p.max_blocks = max_blocks;
     p.scale_log2 = scale * 1.4426950408889634f;
-    e = gqa::launch_simt(p, stream);
+    e = launch_simt(p, stream);
   }
   t_last_error = e;
+}
+
+void compat_v1_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, cudaStream_t stream) {
+  t_last_error = run_fixed(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv,
+                           block_size, max_blocks, 0, scale, 1, nullptr, nullptr, nullptr, stream);
+}
+
+void compat_v2_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, int num_splits, float* ws_acc, float* ws_m, float* ws_l,
+                      cudaStream_t stream) {
+  t_last_error = run_fixed(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv,
+                           block_size, max_blocks, 0, scale, num_splits, ws_acc, ws_m, ws_l,
+                           stream);
+}
+
+}  // namespace gqa
+
+extern "C" {
+
+void gqa_decode_v0_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+                          const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
+                          int Hq, int Hkv, int block_size, int max_blocks, float scale,
+                          cudaStream_t stream) {
+  gqa::compat_v0_launch(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv, block_size,
+                        max_blocks, scale, stream);
 }
 
 void gqa_decode_v1_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
                           const int* block_table, const int* seq_lens, gqa_bf16* out, int B,
                           int Hq, int Hkv, int block_size, int max_blocks, float scale,
                           cudaStream_t stream) {
-  t_last_error = run_fixed(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv,
-                           block_size, max_blocks, 0, scale, 1, nullptr, nullptr, nullptr, stream);
+  gqa::compat_v1_launch(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv, block_size,
+                        max_blocks, scale, stream);
 }
 
 void gqa_decode_v2_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
@@ -374,9 +411,8 @@ void gqa_decode_v2_launch(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_
                           int Hq, int Hkv, int block_size, int max_blocks, float scale,
                           int num_splits, float* ws_acc, float* ws_m, float* ws_l,
                           cudaStream_t stream) {
-  t_last_error = run_fixed(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv,
-                           block_size, max_blocks, 0, scale, num_splits, ws_acc, ws_m, ws_l,
-                           stream);
+  gqa::compat_v2_launch(q, k_cache, v_cache, block_table, seq_lens, out, B, Hq, Hkv, block_size,
+                        max_blocks, scale, num_splits, ws_acc, ws_m, ws_l, stream);
 }
 
 cudaError_t gqa_decode_last_error(void) {
@@ -631,6 +667,18 @@ cudaError_t gqa_decode_get_status(int* status, int clear) {
 cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream) {
   if (limit_us <= 0 || limit_us > 2000000) return cudaErrorInvalidValue;
   return gqa::launch_wait_selftest(static_cast<unsigned long long>(limit_us) * 1000ull, stream);
+}
+
+cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                               const gqa_bf16* v_cache, const int* block_table,
+                                               const int* seq_lens, gqa_bf16* out, int B, int Hq,
+                                               int Hkv, int block_size, int max_blocks,
+                                               float scale, int wait_limit_ns, void* workspace,
+                                               size_t workspace_bytes, cudaStream_t stream) {
+  if (wait_limit_ns < 0 || wait_limit_ns > 1000000) return cudaErrorInvalidValue;
+  return run_balanced(q, k_cache, v_cache, block_table, seq_lens, out, nullptr, nullptr, nullptr,
+                      B, Hq, Hkv, block_size, max_blocks, 0, scale, workspace, workspace_bytes,
+                      stream, nullptr, static_cast<unsigned long long>(wait_limit_ns));
 }
 
 const char* gqa_decode_version(void) { return "gqa_decode_b200 0.1.0 (sm_100a)"; }

@@ -105,6 +105,10 @@ struct ScanParams {
   int num_splits;                // FIXED
   int out_mode;                  // OutMode
   float scale_log2;              // softmax scale * log2(e)
+  // Limit of every pipeline wait, in ns of %globaltimer (kWaitLimitNs; the
+  // wait-timeout self-test passes a tiny one).  The producer's final drain of
+  // its own copies always uses kWaitLimitNs.
+  unsigned long long wait_ns;
   // kOutExchange
   int xworld, xrank;
   unsigned xepoch;               // != 0, identical on every rank for one decode
@@ -160,6 +164,22 @@ cudaError_t launch_plan(const ScanParams& p, long long* plan, long long* prefix,
 cudaError_t launch_block_table_to_csr(const int* block_table, const int* seq_lens, int B,
                                       int max_blocks, int page_size, int* indptr, int* indices,
                                       int* last_page_len, cudaStream_t s);
+// Bodies of the three reference-signature launchers (gqa_api.cu), shared by
+// their C-linkage and C++-linkage exports; each records its status for
+// gqa_decode_last_error().
+void compat_v0_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, cudaStream_t stream);
+void compat_v1_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, cudaStream_t stream);
+void compat_v2_launch(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+                      const __nv_bfloat16* v_cache, const int* block_table, const int* seq_lens,
+                      __nv_bfloat16* out, int B, int Hq, int Hkv, int block_size, int max_blocks,
+                      float scale, int num_splits, float* ws_acc, float* ws_m, float* ws_l,
+                      cudaStream_t stream);
 constexpr int kPlanHeader = 8;   // int64 header words of a plan
 constexpr int kPlanEntry = 4;    // int64 words per CTA entry
 

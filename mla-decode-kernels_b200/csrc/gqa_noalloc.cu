@@ -17,6 +17,7 @@
 
 #include "gqa_decode.h"
 #include "gqa_internal.h"
+#include "gqa_ptx.cuh"
 
 namespace {
 
@@ -30,9 +31,7 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct DeviceState {
-  std::once_flag once;
-  cudaError_t setup_error = cudaSuccess;
-  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+  unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch; null until set up
   int sms = 0;
   int smem_attr = 0;
   int occ_threads = 0, occ_smem = 0, occ = 0;
@@ -41,22 +40,21 @@ constexpr int kMaxDevices = 64;
 DeviceState g_state[kMaxDevices];
 std::mutex g_mu;
 
-// One-time set-up for the current device: the scratch array's device address
-// (in host code its name is only a stand-in, so it must be looked up) and the
-// SM count.
-void setup_device(DeviceState* st, int dev) {
+// Set-up for the current device (caller holds g_mu): the scratch array's
+// device address (in host code its name is only a stand-in, so it must be
+// looked up with this device current) and the SM count.  Only a successful
+// set-up is kept; after a failure (e.g. the first call came during a stream
+// capture that refused the lookup) the next call tries again.
+cudaError_t setup_device(DeviceState* st, int dev) {
   void* ptr = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-  if (e != cudaSuccess) {
-    st->setup_error = e;
-    return;
-  }
-  e = cudaDeviceGetAttribute(&st->sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) {
-    st->setup_error = e;
-    return;
-  }
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  st->sms = sms;
   st->scratch = static_cast<unsigned char*>(ptr);
+  return cudaSuccess;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -84,12 +82,15 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   DeviceState* st = &g_state[dev];
-  std::call_once(st->once, setup_device, st, dev);
-  if (st->setup_error != cudaSuccess) return st->setup_error;
-
   int grid = 0;
+  unsigned char* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
+    if (st->scratch == nullptr) {
+      e = setup_device(st, dev);
+      if (e != cudaSuccess) return e;
+    }
+    scratch = st->scratch;
     if (st->smem_attr < sp.smem_bytes) {
       e = gqa::scan_kernel_set_smem(sp.smem_bytes);
       if (e != cudaSuccess) return e;
@@ -120,7 +121,7 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
 
   // The arrival counters must start at zero; the scratch keeps whatever the
   // previous call left, so clear them on the same stream first.
-  e = cudaMemsetAsync(st->scratch, 0, counters_bytes, stream);
+  e = cudaMemsetAsync(scratch, 0, counters_bytes, stream);
   if (e != cudaSuccess) return e;
 
   gqa::ScanParams p{};
@@ -133,10 +134,10 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.kv_indices = block_table;
   p.kv_last = seq_lens;
   p.out = out;
-  p.counters = reinterpret_cast<int*>(st->scratch);
-  p.part_m = reinterpret_cast<float*>(st->scratch + off_m);
-  p.part_l = reinterpret_cast<float*>(st->scratch + off_l);
-  p.part_acc = reinterpret_cast<float*>(st->scratch + off_acc);
+  p.counters = reinterpret_cast<int*>(scratch);
+  p.part_m = reinterpret_cast<float*>(scratch + off_m);
+  p.part_l = reinterpret_cast<float*>(scratch + off_l);
+  p.part_acc = reinterpret_cast<float*>(scratch + off_acc);
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -156,5 +157,6 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.num_splits = 0;
   p.out_mode = gqa::kOutBf16;
   p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_ns = gqa::kWaitLimitNs;
   return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
 }

@@ -265,7 +265,10 @@ __device__ __forceinline__ void xput_lanes(const ScanParams& p, size_t bh, float
 
 // Publish this warp's states of unit `unit`, wait for every rank's, merge
 // heads [bh0, bh0 + cnt) and write bf16 out.  Rows empty on every rank give 0.
-__device__ __forceinline__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
+// The (m, l) of every rank (lane = rank) and the acc rows of kHeads heads of
+// every rank are loaded together, one L2 round trip per kHeads heads.
+template <int kHeads>
+__device__ __noinline__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
   __threadfence_system();
   __syncwarp();
   if (lane < p.xworld) st_release_sys(xflag(p, lane, p.xrank, unit), p.xepoch);
@@ -282,35 +285,48 @@ __device__ __forceinline__ void xfinish(const ScanParams& p, int unit, size_t bh
     if (lane == 0) raise_status(kStatusPeerTimeout);
     return;
   }
-  for (int i = 0; i < cnt; ++i) {
-    const size_t bh = bh0 + i;
-    float mk = -INFINITY, lk = 0.f;
-    if (lane < p.xworld) {
-      // source index clamped so the address is valid on every lane
-      const float* st = xstate(p, p.xrank, min(lane, p.xworld - 1), bh);
-      mk = __ldcg(st);
-      lk = __ldcg(st + 1);
-    }
-    float M = mk;
+  const int src = min(lane, p.xworld - 1);  // source rank clamped: valid on every lane
+  for (int i0 = 0; i0 < cnt; i0 += kHeads) {
+    const int hmax = min(kHeads, cnt - i0) - 1;
+    float mk[kHeads], lk[kHeads];
+    float4 x[kHeads][kMaxPeers];
     #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
-    const float w = (lane < p.xworld && M != -INFINITY) ? exp2f(mk - M) : 0.f;
-    float L = lk * w;
-    #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(kFull, L, off);
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int o = 0; o < p.xworld; ++o) {
-      const float f = __shfl_sync(kFull, w, o);
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(xstate(p, p.xrank, o, bh) + 4) + lane);
-      a.x += x.x * f;
-      a.y += x.y * f;
-      a.z += x.z * f;
-      a.w += x.w * f;
+    for (int i = 0; i < kHeads; ++i) {
+      const size_t bh = bh0 + i0 + min(i, hmax);
+      const float* st = xstate(p, p.xrank, src, bh);
+      mk[i] = __ldcg(st);
+      lk[i] = __ldcg(st + 1);
+      #pragma unroll
+      for (int o = 0; o < kMaxPeers; ++o)
+        x[i][o] = o < p.xworld
+                      ? __ldcg(reinterpret_cast<const float4*>(xstate(p, p.xrank, o, bh) + 4) +
+                               lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (M == -INFINITY) {
-      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, 0.f, 0.f, 0.f, 0.f);
-    } else {
-      store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a.x / L, a.y / L, a.z / L, a.w / L);
+    #pragma unroll
+    for (int i = 0; i < kHeads; ++i) {
+      if (i > hmax) continue;
+      float M = lane < p.xworld ? mk[i] : -INFINITY;
+      #pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
+      const float w = (lane < p.xworld && M != -INFINITY) ? exp2f(mk[i] - M) : 0.f;
+      float L = lk[i] * w;
+      #pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(kFull, L, off);
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      #pragma unroll
+      for (int o = 0; o < kMaxPeers; ++o) {
+        const float f = __shfl_sync(kFull, w, o);  // 0 for o >= xworld
+        a.x += x[i][o].x * f;
+        a.y += x[i][o].y * f;
+        a.z += x[i][o].z * f;
+        a.w += x[i][o].w * f;
+      }
+      __nv_bfloat16* o = p.out + (bh0 + i0 + i) * kHeadDim + 4 * lane;
+      if (M == -INFINITY)
+        store_bf16x4(o, 0.f, 0.f, 0.f, 0.f);
+      else
+        store_bf16x4(o, a.x / L, a.y / L, a.z / L, a.w / L);
     }
   }
 }
@@ -336,6 +352,7 @@ __device__ __forceinline__ void emit_final(const ScanParams& p, size_t bh, float
 // [hbase, hbase+cnt) of request b, which has no tokens on this rank.  The
 // reference's kernels divide by l = 0 there (docs/decisions/k1-004);
 // python/reference.py yields 0.  `unit` = row * ncw + warp (kOutExchange).
+template <int kXHeads>
 __device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int unit, int lane) {
   const size_t bh0 = static_cast<size_t>(b) * p.Hq + hbase;
   for (int n = 0; n < cnt; ++n) {
@@ -344,7 +361,7 @@ __device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbas
     else
       emit_final(p, bh0 + n, -INFINITY, 0.f, make_float4(0.f, 0.f, 0.f, 0.f), lane);
   }
-  if (p.out_mode == kOutExchange) xfinish(p, unit, bh0, cnt, lane);
+  if (p.out_mode == kOutExchange) xfinish<kXHeads>(p, unit, bh0, cnt, lane);
 }
 
 // Partial states merged in one step.  Rows cut into more parts than this are
@@ -352,99 +369,118 @@ __device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbas
 // consecutive CTAs merges the group into the group's first slot, and the
 // last of those merges the groups.
 constexpr int kMergeGroup = 16;
-constexpr int kMergeHeads = 4;  // q heads merged together (register budget)
-constexpr int kMergeBatch = 2;  // parts per batch of acc loads
 
 // Merge n unnormalised states of this warp's q heads [jj0, jj0 + cnt),
 // stored in slots first, first + stride, ...  With `final_` the result goes
 // to the output of q heads bh0 + i (see emit_final); otherwise it overwrites
 // slot `first`.
-// Loads are batched so that the whole merge costs a few L2 round trips:
-// lanes hold one part each for (m, l), and every lane accumulates 4 output
-// dims of all kMergeHeads heads over kMergeBatch parts per batch.
-__device__ __noinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n, int jj0,
-                            int cnt, int lane, bool final_, size_t bh0) {
+//
+// The merge is bound by L2 latency, not bandwidth, so loads are issued in
+// batches that are all in flight together: the (m, l) of up to 32 parts per
+// head (lane = part) and the acc rows of the first kBatch parts of kHeads
+// heads (lane = 4 output dims) go out before the first result is used, so a
+// row cut into at most kBatch parts costs one L2 round trip per kHeads heads.
+// Every address is clamped into range, so all loads are valid on every lane;
+// out-of-range parts get weight 0.
+template <int kHeads, int kBatch>
+__device__ __forceinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n,
+                                         int jj0, int cnt, int lane, bool final_, size_t bh0) {
   const int QHR = p.HG * p.G;
-  for (int i0 = 0; i0 < cnt; i0 += kMergeHeads) {
-    float M[kMergeHeads], L[kMergeHeads], m0[kMergeHeads], l0[kMergeHeads];
-    #pragma unroll
-    for (int i = 0; i < kMergeHeads; ++i) {
-      M[i] = -INFINITY;
-      L[i] = 0.f;
-      m0[i] = -INFINITY;
-      l0[i] = 0.f;
-    }
-    // pass 1: M per head over all parts (the first 32 parts stay in registers)
-    for (int c0 = 0; c0 < n; c0 += 32) {
-      // part index clamped into range: every address is valid on every lane
+  for (int i0 = 0; i0 < cnt; i0 += kHeads) {
+    const int hmax = min(kHeads, cnt - i0) - 1;
+    const size_t head0 = static_cast<size_t>(jj0) + i0;
+    // (m, l) of parts [0, 32) and acc of parts [0, kBatch), all in flight
+    float mk[kHeads], lk[kHeads];
+    float4 x[kHeads][kBatch];
+    {
       const size_t srow =
-          static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
-              QHR + jj0;
+          static_cast<size_t>(first + static_cast<long long>(min(lane, n - 1)) * stride) * QHR +
+          head0;
       #pragma unroll
-      for (int i = 0; i < kMergeHeads; ++i) {
-        float mk = -INFINITY, lk = 0.f;
-        if (i0 + i < cnt && c0 + lane < n) {
-          const size_t st = srow + min(i0 + i, cnt - 1);
-          mk = __ldcg(p.part_m + st);
-          lk = __ldcg(p.part_l + st);
-        }
-        if (c0 == 0) {
-          m0[i] = mk;
-          l0[i] = lk;
-        }
+      for (int i = 0; i < kHeads; ++i) {
+        mk[i] = __ldcg(p.part_m + srow + min(i, hmax));
+        lk[i] = __ldcg(p.part_l + srow + min(i, hmax));
+      }
+      #pragma unroll
+      for (int kk = 0; kk < kBatch; ++kk) {
+        const size_t sk =
+            static_cast<size_t>(first + static_cast<long long>(min(kk, n - 1)) * stride) * QHR +
+            head0;
         #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mk = fmaxf(mk, __shfl_xor_sync(kFull, mk, off));
-        M[i] = fmaxf(M[i], mk);
+        for (int i = 0; i < kHeads; ++i)
+          x[i][kk] = __ldcg(reinterpret_cast<const float4*>(
+                                p.part_acc + (sk + min(i, hmax)) * kHeadDim) + lane);
       }
     }
-    // pass 2: weights, L and acc
-    float4 a[kMergeHeads];
+    // M per head over all parts
+    float M[kHeads];
     #pragma unroll
-    for (int i = 0; i < kMergeHeads; ++i) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c0 = 0; c0 < n; c0 += 32) {
-      float w[kMergeHeads];
+    for (int i = 0; i < kHeads; ++i) {
+      float mv = lane < n ? mk[i] : -INFINITY;
+      #pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, off));
+      M[i] = mv;
+    }
+    for (int c0 = 32; c0 < n; c0 += 32) {  // rows cut into more than 32 parts
       const size_t srow =
           static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
-              QHR + jj0;
+              QHR + head0;
       #pragma unroll
-      for (int i = 0; i < kMergeHeads; ++i) {
-        float mk = m0[i], lk = l0[i];
-        if (c0 > 0) {
-          mk = -INFINITY;
-          lk = 0.f;
-          if (i0 + i < cnt && c0 + lane < n) {
-            const size_t st = srow + min(i0 + i, cnt - 1);
-            mk = __ldcg(p.part_m + st);
-            lk = __ldcg(p.part_l + st);
-          }
+      for (int i = 0; i < kHeads; ++i) {
+        float mv = c0 + lane < n ? __ldcg(p.part_m + srow + min(i, hmax)) : -INFINITY;
+        #pragma unroll
+        for (int off = 16; off > 0; off >>= 1) mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, off));
+        M[i] = fmaxf(M[i], mv);
+      }
+    }
+    // weights, L and acc, 32 parts per lane chunk
+    float L[kHeads];
+    float4 a[kHeads];
+    #pragma unroll
+    for (int i = 0; i < kHeads; ++i) {
+      L[i] = 0.f;
+      a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      if (c0 > 0) {
+        const size_t srow =
+            static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
+                QHR + head0;
+        #pragma unroll
+        for (int i = 0; i < kHeads; ++i) {
+          mk[i] = __ldcg(p.part_m + srow + min(i, hmax));
+          lk[i] = __ldcg(p.part_l + srow + min(i, hmax));
         }
-        w[i] = (c0 + lane < n && i0 + i < cnt) ? exp2f(mk - M[i]) : 0.f;
-        float lw = lk * w[i];
+      }
+      float w[kHeads];
+      #pragma unroll
+      for (int i = 0; i < kHeads; ++i) {
+        w[i] = (c0 + lane < n && M[i] != -INFINITY) ? exp2f(mk[i] - M[i]) : 0.f;
+        float lw = lk[i] * w[i];
         #pragma unroll
         for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(kFull, lw, off);
         L[i] += lw;
       }
       const int nc = min(32, n - c0);
-      for (int k0 = 0; k0 < nc; k0 += kMergeBatch) {
-        float4 x[kMergeHeads][kMergeBatch];
-        #pragma unroll
-        for (int i = 0; i < kMergeHeads; ++i) {
+      for (int k0 = 0; k0 < nc; k0 += kBatch) {
+        if (c0 > 0 || k0 > 0) {
           #pragma unroll
-          for (int kk = 0; kk < kMergeBatch; ++kk) {
-            x[i][kk] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i0 + i < cnt && k0 + kk < nc) {
-              const int kc = c0 + min(k0 + kk, nc - 1), ic = min(i0 + i, cnt - 1);
-              const size_t st =
-                  static_cast<size_t>(first + static_cast<long long>(kc) * stride) * QHR + jj0 + ic;
-              x[i][kk] = __ldcg(reinterpret_cast<const float4*>(p.part_acc + st * kHeadDim) + lane);
-            }
+          for (int kk = 0; kk < kBatch; ++kk) {
+            const size_t sk = static_cast<size_t>(
+                                  first + static_cast<long long>(min(c0 + k0 + kk, n - 1)) *
+                                              stride) * QHR + head0;
+            #pragma unroll
+            for (int i = 0; i < kHeads; ++i)
+              x[i][kk] = __ldcg(reinterpret_cast<const float4*>(
+                                    p.part_acc + (sk + min(i, hmax)) * kHeadDim) + lane);
           }
         }
         #pragma unroll
-        for (int i = 0; i < kMergeHeads; ++i) {
+        for (int kk = 0; kk < kBatch; ++kk) {
           #pragma unroll
-          for (int kk = 0; kk < kMergeBatch; ++kk) {
-            const float f = __shfl_sync(kFull, w[i], (k0 + kk) & 31);
+          for (int i = 0; i < kHeads; ++i) {
+            // weight of part c0 + k0 + kk (lane k0 + kk of the chunk); 0 past n
+            const float f = k0 + kk < nc ? __shfl_sync(kFull, w[i], (k0 + kk) & 31) : 0.f;
             a[i].x += x[i][kk].x * f;
             a[i].y += x[i][kk].y * f;
             a[i].z += x[i][kk].z * f;
@@ -454,12 +490,12 @@ __device__ __noinline__ void merge_parts(const ScanParams& p, long long first, i
       }
     }
     #pragma unroll
-    for (int i = 0; i < kMergeHeads; ++i) {
-      if (i0 + i >= cnt) continue;
+    for (int i = 0; i < kHeads; ++i) {
+      if (i > hmax) continue;
       if (final_) {
         emit_final(p, bh0 + i0 + i, M[i], L[i], a[i], lane);
       } else {
-        const size_t st = static_cast<size_t>(first) * QHR + jj0 + i0 + i;
+        const size_t st = static_cast<size_t>(first) * QHR + head0 + i;
         if (lane == 0) {
           p.part_m[st] = M[i];
           p.part_l[st] = L[i];
@@ -468,6 +504,24 @@ __device__ __noinline__ void merge_parts(const ScanParams& p, long long first, i
       }
     }
   }
+}
+
+// Register budget of a merge: kHeads x kBatch float4 acc loads in flight.
+// The register file is split between the SM's four schedulers, so a 9-warp
+// CTA (three warps on one scheduler) gets at most 168 registers a thread and
+// a 17-warp CTA at most 96.  The merge is one non-inlined function called
+// from one place; with 12 float4 loads in flight (2 heads x 6 parts) it
+// fits beside the streaming loop's live registers without spills, and a row
+// cut into up to 6 parts (the common case: a CTA's range is a sixth of a
+// rep-shape row) costs one L2 round trip per 2 heads.  The 17-warp kernel
+// keeps 8 in flight.
+template <int kMaxWarps>
+__device__ __noinline__ void merge_rows(const ScanParams& p, long long first, int stride, int n,
+                                        int jj0, int cnt, int lane, bool final_, size_t bh0) {
+  if constexpr (kMaxWarps <= 9)
+    merge_parts<2, 6>(p, first, stride, n, jj0, cnt, lane, final_, bh0);
+  else
+    merge_parts<4, 2>(p, first, stride, n, jj0, cnt, lane, final_, bh0);
 }
 
 // Count one arrival on *ctr; true (on every lane) for the warp whose arrival
@@ -582,7 +636,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         const unsigned char* src =
             base + ((static_cast<size_t>(page) * p.bs + sl) * p.Hkv + head_off) * (kHeadDim * 2);
         // Warp-uniform outcome: every lane polls, all must have seen the phase.
-        if (!__all_sync(kFull, mbar_wait(bars + 2 * ns8 + 8 * stage, phase ^ 1))) {
+        if (!__all_sync(kFull, mbar_wait(bars + 2 * ns8 + 8 * stage, phase ^ 1, p.wait_ns))) {
           raise_status(kStatusWaitTimeout);
           ok = false;
           break;
@@ -601,22 +655,25 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         }
       }
     }
-    if (!ok) {
-      // Abandoned: wait (bounded) for this CTA's copies still in flight so
-      // none lands in shared memory after the CTA has exited.
-      const long long inflight = min(issued, static_cast<long long>(p.nstages));
-      for (long long j = 1; j <= inflight; ++j) {
-        const long long idx = issued - j;
-        const int stg = static_cast<int>(idx % p.nstages);
-        const uint32_t ph = static_cast<uint32_t>((idx / p.nstages) & 1);
-        mbar_wait(bars + 8 * stg, ph);
-        mbar_wait(bars + ns8 + 8 * stg, ph);
-      }
+    // Wait (bounded) for this CTA's copies that may still be in flight - at
+    // most the last nstages issued - so none lands in shared memory after the
+    // CTA has exited.  Normally the consumers have already waited for them;
+    // not when a consumer warp gave up on a wait and skipped its remaining
+    // stages, or when this warp abandoned the pipeline.  No further phase of
+    // these barriers completes, so each wait sees its own phase.
+    const long long inflight = min(issued, static_cast<long long>(p.nstages));
+    for (long long j = 1; j <= inflight; ++j) {
+      const long long idx = issued - j;
+      const int stg = static_cast<int>(idx % p.nstages);
+      const uint32_t ph = static_cast<uint32_t>((idx / p.nstages) & 1);
+      mbar_wait(bars + 8 * stg, ph);
+      mbar_wait(bars + ns8 + 8 * stg, ph);
     }
     return;
   }
 
   // ------------------------------ consumers -------------------------------
+  constexpr int kXHeads = kMaxWarps <= 9 ? 2 : 1;  // heads per batch of the peer merge
   const int hl = warp / p.NT;
   const int qt = warp - hl * p.NT;
   const int j0 = qt * 8;
@@ -635,19 +692,26 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (req_len(p, b, cap) != 0) continue;
       for (int hg = 0; hg < p.NHG; ++hg)
-        write_empty(p, b, (hg * p.HG + hl) * p.G + j0, cnt, (b * p.NHG + hg) * p.ncw + warp,
-                    lane);
+        write_empty<kXHeads>(p, b, (hg * p.HG + hl) * p.G + j0, cnt,
+                             (b * p.NHG + hg) * p.ncw + warp, lane);
     }
   }
 
   int stage = 0;
   uint32_t phase = 0;
+  // Set when one of this warp's pipeline waits timed out.  The warp then
+  // stops reading the ring but still walks its segments, publishing an empty
+  // state (m = -inf, l = 0, acc = 0) for each, so every arrival counter is
+  // completed and re-armed and every peer flag is published exactly as in a
+  // normal launch: the workspace stays valid for the next launch, and only
+  // the rows this warp held are wrong (status bit 0 says so).
+  bool dead = false;
   Seg s;
   while (iter_next(it, p, cap, s)) {
     const int hk = s.hg * p.HG + hl;
     const int hbase = hk * p.G + j0;
     if (s.kind == kZero) {
-      write_empty(p, s.b, hbase, cnt, s.row * p.ncw + warp, lane);
+      write_empty<kXHeads>(p, s.b, hbase, cnt, s.row * p.ncw + warp, lane);
       continue;
     }
     uint32_t qf[8][2];
@@ -666,12 +730,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     #pragma unroll
     for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
 
-    for (int st = s.s0; st < s.s1; ++st) {
+    for (int st = s.s0; st < s.s1 && !dead; ++st) {
       const int nvalid = min(kStageTokens, s.S - st * kStageTokens);
       const uint32_t kb = ring + stage * p.stage_bytes;
-      if (!__all_sync(kFull, mbar_wait(bars + 8 * stage, phase))) {
-        raise_status(kStatusWaitTimeout);
-        return;
+      if (!__all_sync(kFull, mbar_wait(bars + 8 * stage, phase, p.wait_ns))) {
+        dead = true;
+        break;
       }
       // S^T = K q^T, two independent accumulation chains over d.
       float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -714,9 +778,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       // P^T as the B operand: (tokens 2 tig.., head g) from (token g, heads 2 tig..).
       const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
       const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
-      if (!__all_sync(kFull, mbar_wait(bars + ns8 + 8 * stage, phase))) {
-        raise_status(kStatusWaitTimeout);
-        return;
+      if (!__all_sync(kFull, mbar_wait(bars + ns8 + 8 * stage, phase, p.wait_ns))) {
+        dead = true;
+        break;
       }
       const uint32_t vb = kb + half;
       #pragma unroll
@@ -731,6 +795,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         stage = 0;
         phase ^= 1;
       }
+    }
+
+    if (dead) {
+      if (lane == 0) raise_status(kStatusWaitTimeout);
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+      #pragma unroll
+      for (int mt = 0; mt < 8; ++mt) acc[mt][0] = acc[mt][1] = acc[mt][2] = acc[mt][3] = 0.f;
     }
 
     // ---- segment epilogue ----
@@ -759,7 +831,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
           }
         }
       }
-      xfinish(p, s.row * p.ncw + warp, static_cast<size_t>(s.b) * p.Hq + hbase, cnt, lane);
+      xfinish<kXHeads>(p, s.row * p.ncw + warp, static_cast<size_t>(s.b) * p.Hq + hbase, cnt,
+                       lane);
       continue;
     }
     if (s.kind == kDirect && p.out_mode == kOutBf16) {
@@ -826,33 +899,30 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       int* row_ctr = p.counters + static_cast<size_t>(grid + rows + s.row) * p.ncw + warp;
       const int jj0 = hl * p.G + j0;
       const size_t bh0 = static_cast<size_t>(s.b) * p.Hq + hbase;
-      if (s.nparts <= kMergeGroup) {
-        if (arrive_last(row_ctr, s.nparts, lane)) {
-          merge_parts(p, s.cfirst + s.row, 1, s.nparts, jj0, cnt, lane, true, bh0);
-          if (lane == 0) *row_ctr = 0;
-          if (p.out_mode == kOutExchange) xfinish(p, s.row * p.ncw + warp, bh0, cnt, lane);
-        }
-      } else {
-        const long long gi = (static_cast<long long>(blockIdx.x) - s.cfirst) / kMergeGroup;
-        const long long g0 = s.cfirst + gi * kMergeGroup;
-        const long long clast = s.cfirst + s.nparts - 1;
-        const int gsz = static_cast<int>(min(static_cast<long long>(kMergeGroup), clast - g0 + 1));
-        const int ngroups = (s.nparts + kMergeGroup - 1) / kMergeGroup;
-        bool group_done = true;
-        if (gsz > 1) {
-          int* grp_ctr = p.counters + static_cast<size_t>(g0 + s.row) * p.ncw + warp;
-          group_done = arrive_last(grp_ctr, gsz, lane);
-          if (group_done) {
-            merge_parts(p, g0 + s.row, 1, gsz, jj0, cnt, lane, false, 0);
-            if (lane == 0) *grp_ctr = 0;
-          }
-        }
-        if (group_done && arrive_last(row_ctr, ngroups, lane)) {
-          merge_parts(p, s.cfirst + s.row, kMergeGroup, ngroups, jj0, cnt, lane, true, bh0);
-          if (lane == 0) *row_ctr = 0;
-          if (p.out_mode == kOutExchange) xfinish(p, s.row * p.ncw + warp, bh0, cnt, lane);
-        }
+      // Level 0 merges this CTA's group of kMergeGroup consecutive parts
+      // (rows cut into more parts than that), level 1 the row.  One merge
+      // call site, so the merge is inlined once.
+      const long long gi = (static_cast<long long>(blockIdx.x) - s.cfirst) / kMergeGroup;
+      const long long g0 = s.cfirst + gi * kMergeGroup;
+      const bool grouped = s.nparts > kMergeGroup;
+      const int gsz = grouped ? static_cast<int>(min(static_cast<long long>(kMergeGroup),
+                                                     s.cfirst + s.nparts - g0))
+                              : 1;
+      const int nrow = grouped ? (s.nparts + kMergeGroup - 1) / kMergeGroup : s.nparts;
+      bool finished = false;
+      for (int level = gsz > 1 ? 0 : 1; level < 2; ++level) {
+        int* ctr = level == 0 ? p.counters + static_cast<size_t>(g0 + s.row) * p.ncw + warp
+                              : row_ctr;
+        const int n = level == 0 ? gsz : nrow;
+        if (!arrive_last(ctr, n, lane)) break;
+        merge_rows<kMaxWarps>(p, level == 0 ? g0 + s.row : s.cfirst + s.row,
+                              level == 0 || !grouped ? 1 : kMergeGroup, n, jj0, cnt, lane,
+                              level == 1, bh0);
+        if (lane == 0) *ctr = 0;
+        finished = level == 1;
       }
+      if (finished && p.out_mode == kOutExchange)
+        xfinish<kXHeads>(p, s.row * p.ncw + warp, bh0, cnt, lane);
     }
   }
 }

@@ -8,6 +8,7 @@ tests/golden/.
 """
 
 import ctypes
+import json
 import os
 import subprocess
 
@@ -26,6 +27,26 @@ def _cpu_has_avx2_fma():
         return " avx2" in flags and " fma" in flags
     except OSError:
         return False
+
+
+def reference_checkout():
+    """Directory of a reference checkout to build checkers from, or None.
+
+    Taken from the GQA_REFERENCE_DIR environment variable, else from the
+    "reference_path" BASELINE.json records at the repository root; either
+    must be an existing directory holding include/gqa_decode.h.  On a
+    machine without the checkout this returns None and the callers skip.
+    """
+    cand = os.environ.get("GQA_REFERENCE_DIR")
+    if not cand:
+        try:
+            with open(os.path.join(os.path.dirname(ORACLE_DIR), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and os.path.isfile(os.path.join(cand, "include", "gqa_decode.h")):
+        return cand
+    return None
 
 
 def build(reference_dir=None):

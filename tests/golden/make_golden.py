@@ -23,6 +23,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "mla-decode-kernels_b200", "python"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
 
 import cases  # noqa: E402
 
@@ -75,9 +76,18 @@ def q_transform(name, q):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("GQA_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=None,
+                    help="reference checkout (default: GQA_REFERENCE_DIR, else the "
+                         "reference_path recorded in BASELINE.json)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
+    if args.reference is None:
+        import oracle
+
+        args.reference = oracle.reference_checkout()
+    if args.reference is None:
+        raise SystemExit("make_golden.py needs the reference checkout: pass --reference or set "
+                         "GQA_REFERENCE_DIR")
     sys.path.insert(0, os.path.join(args.reference, "python"))
     from reference import attention_ref  # the reference's own oracle
 

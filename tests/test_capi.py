@@ -57,14 +57,35 @@ def test_symbol_exported(lib, name):
     assert hasattr(lib, name), f"{name} declared in include/*.h but not exported"
 
 
-def test_symbols_are_c_linkage():
-    # extern "C": the dynamic symbol table holds the plain names.
+def _dynamic_symbols():
     import subprocess
     out = subprocess.run(["nm", "-D", "--defined-only", pkg_build.LIB_PATH], capture_output=True,
                          text=True, check=True).stdout
-    syms = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+# The C++-mangled names of the reference's three launchers as declared in its
+# include/gqa_decode.h:6-23 (C++ linkage): (const __nv_bfloat16*) x3,
+# (const int*) x2, __nv_bfloat16*, int x5, float, [int, float* x3,] cudaStream_t.
+CXX_LAUNCHERS = [
+    "_Z20gqa_decode_v0_launchPK13__nv_bfloat16S1_S1_PKiS3_PS_iiiiifP11CUstream_st",
+    "_Z20gqa_decode_v1_launchPK13__nv_bfloat16S1_S1_PKiS3_PS_iiiiifP11CUstream_st",
+    "_Z20gqa_decode_v2_launchPK13__nv_bfloat16S1_S1_PKiS3_PS_iiiiifiPfS5_S5_P11CUstream_st",
+]
+
+
+def test_declared_symbols_have_c_linkage():
+    # extern "C" in include/*.h: the dynamic symbol table holds the plain names.
+    syms = _dynamic_symbols()
     for name in declared_functions():
         assert name in syms
+
+
+def test_reference_launchers_also_have_cxx_linkage():
+    # An object compiled against the reference header references these.
+    syms = _dynamic_symbols()
+    for name in CXX_LAUNCHERS:
+        assert name in syms, f"{name} (C++ linkage) not exported"
 
 
 def test_version(lib):

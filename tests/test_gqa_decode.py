@@ -314,6 +314,52 @@ def test_bounded_wait_times_out_with_status():
     run_and_check(capi.auto, cases.ref_case("e_partial_blocks", seed=0))
 
 
+def test_timed_out_decode_leaves_workspace_valid():
+    # A whole decode whose pipeline waits give up at once (limit 0 ns, so they
+    # time out while the copies are still on their way): status bit 0, the
+    # launch ends normally, and the next decode on the SAME workspace must be
+    # bit-identical to one on a fresh workspace - the warps that gave up still
+    # completed and re-armed every arrival counter of the rows they held.
+    lib = capi.lib
+    lib.gqa_decode_selftest_decode_timeout.argtypes = (
+        [ctypes.c_void_p] * 6 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int,
+                                                      ctypes.c_void_p, ctypes.c_size_t,
+                                                      ctypes.c_void_p])
+    lib.gqa_decode_selftest_decode_timeout.restype = ctypes.c_int
+    # one long request (rows cut into many parts, two merge levels) and
+    # shorter ones (rows cut into a few parts or held whole)
+    q, k, v, bt, sl = to_gpu(cases.make_case([60000, 9000, 700, 33], 32, 8, 16, seed=27))
+    B, Hq, Hkv, bs, mb = q.shape[0], q.shape[1], k.shape[2], k.shape[1], bt.shape[1]
+    nbytes = lib.gqa_decode_workspace_bytes(B, Hq, Hkv, 0)
+
+    def launch(ws, wait_ns=None):
+        out = torch.full_like(q, float("nan"))
+        ptrs = [ctypes.c_void_p(t.data_ptr()) for t in (q, k, v, bt, sl, out)]
+        if wait_ns is None:
+            rc = lib.gqa_decode_launch(*ptrs, B, Hq, Hkv, bs, mb, k.shape[0], SCALE, 0,
+                                       ctypes.c_void_p(ws.data_ptr()), nbytes, capi.stream())
+        else:
+            rc = lib.gqa_decode_selftest_decode_timeout(*ptrs, B, Hq, Hkv, bs, mb, SCALE, wait_ns,
+                                                        ctypes.c_void_p(ws.data_ptr()), nbytes,
+                                                        capi.stream())
+        assert rc == 0
+        torch.cuda.synchronize()
+        return out
+
+    capi.status()
+    expect = launch(torch.zeros(nbytes, dtype=torch.uint8, device="cuda"))
+    assert capi.status() == 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        launch(ws, wait_ns=0)
+        assert capi.status() & 1, "the zero-limit waits did not time out"
+        again = launch(ws)
+        assert capi.status() == 0
+        assert torch.equal(again, expect)
+    ref = oracle.attention_ref(*(t.cpu() for t in (q, k, v, bt, sl)), SCALE)
+    assert_close(expect, ref)
+
+
 def test_cuda_graph_replay():
     q, k, v, bt, sl = to_gpu(cases.ref_case("a_base", seed=3))
     eager = binding.gqa_decode(q, k, v, bt, sl, SCALE)

@@ -6,8 +6,9 @@ library a workspace; this entry point keeps its scratch in a fixed 16 MiB
 device array instead.  The test calls it through the C ABI twice in a row
 (the second call reuses the array the first one left behind) and compares
 each output with the workspace-based gqa_decode_launch at the suite's
-tolerance.  The file name sorts last so a stop-at-first-failure run has
-already run every other test.
+tolerance, and bit for bit (both run the same kernel, grid and schedule).
+The file name sorts last so a stop-at-first-failure run has already run
+every other test.
 """
 
 import ctypes
@@ -58,6 +59,8 @@ def test_noalloc_matches_workspace_entry_point_twice(which):
         assert torch.isfinite(out.float()).all(), f"call {call}: unwritten or non-finite output"
         assert torch.allclose(out.float(), expect.float(), atol=ATOL, rtol=RTOL), \
             f"call {call}: max-abs {(out.float() - expect.float()).abs().max().item():.3e}"
+        # same kernel, grid and schedule as the workspace entry point: same bits
+        assert torch.equal(out, expect), f"call {call}: not bit-identical to gqa_decode_launch"
     assert capi.status() == 0
 
 
