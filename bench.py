@@ -347,9 +347,35 @@ class E2ELoop:
         self.compute.wait_stream(self.d2h_stream)
         self.compute.wait_stream(self.h2d_stream)
 
+    def serial_step(self, decode):
+        """One step with nothing overlapped: this step's H2D copies, the
+        decode and the D2H copy of its output, in that order on the compute
+        stream, so the time per step is the host-to-host latency of a step."""
+        with torch.cuda.stream(self.compute):
+            for d, h in zip(self.dev_in[0], self.host_in[0]):
+                d.copy_(h, non_blocking=True)
+            decode(*self.dev_in[0], self.dev_out[0])
+            self.host_out[0].copy_(self.dev_out[0], non_blocking=True)
+
     def last_output(self):
         torch.cuda.synchronize()
         return self.host_out[(self.i - 1) % 2].to(self.dev_out[0].device)
+
+
+def serial_e2e(e2e, decode, steps, world, stream, device):
+    """Mean ms per step of E2ELoop.serial_step over min(steps, 200) steps,
+    max over ranks (after the pipelined loop has drained)."""
+    torch.cuda.synchronize()
+    for _ in range(3):
+        e2e.serial_step(decode)
+    n = max(1, min(steps, 200))
+    return max_over_ranks(time_loop(lambda: e2e.serial_step(decode), n, world, stream), world,
+                          device)
+
+
+SERIAL_NOTE = ("serial_*: the same step with nothing overlapped (H2D of the step's inputs, the "
+               "decode, D2H of its output, in order on one stream): the per-step host-to-host "
+               "latency; value/ms_per_step above are the pipelined serving loop")
 
 
 def per_step_median_us(step, n, stream):
@@ -405,6 +431,55 @@ def cpu_baseline(budget_s):
             "ms_per_full_step_extrapolated": round(mean * 1e3 * 32 / n_req, 3)}
 
 
+REF_PY = os.path.join(REPO, "baseline", "_ref", "reference.py")
+
+
+def reference_py_baseline(budget_s):
+    """The reference's own CPU oracle, python/reference.py:attention_ref, on a
+    bounded sample of rep requests on all host cores (torch CPU threads).
+
+    The reference has no installable package, so __graft_entry__.build()
+    stages an unmodified copy of that file in the git-ignored baseline/_ref/
+    when a reference checkout is present; None when the copy is absent.
+    """
+    if not os.path.exists(REF_PY):
+        return None
+    import importlib.util
+
+    import cases
+    import oracle
+
+    spec = importlib.util.spec_from_file_location("reference_py", REF_PY)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    threads = oracle.default_threads()
+    saved = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        n_req = 1
+        case = cpu_sample_case(n_req)
+        mod.attention_ref(*case, SCALE)  # warm (page-in, thread pool)
+        t0 = time.perf_counter()
+        mod.attention_ref(*case, SCALE)
+        one = time.perf_counter() - t0
+        reps = max(2, min(50, int(budget_s / max(one, 1e-6))))
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            mod.attention_ref(*case, SCALE)
+            ts.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(saved)
+    mean = statistics.mean(ts)
+    kv = cases.kv_bytes([8192] * n_req, 8)
+    return {"value": round(kv / mean / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"{n_req} of the 32 requests of config 2 (S=8192, Hq=32, Hkv=8, bs=16), "
+                      f"{reps} runs, mean {mean * 1e3:.1f} ms; python/reference.py:attention_ref "
+                      f"(the reference's own code, unmodified), torch CPU with {threads} threads",
+            "ms_per_full_step_extrapolated": round(mean * 1e3 * 32 / n_req, 1)}
+
+
 # ---------------------------------------------------------------- arms
 
 def run_reference(args, world, rank):
@@ -445,6 +520,8 @@ def run_reference(args, world, rank):
                                    "oracle/gqa_oracle.c restating python/reference.py"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        # the reference's own python/reference.py on the same cores, beside the port
+        "reference_py": reference_py_baseline(10.0),
     }
     print(json.dumps(line), flush=True)
 
@@ -478,12 +555,12 @@ def run_ours(args, world, rank, local):
         if args.api == "csr":
             def step():
                 wrapper.run(q, (k, v), out=out)
-            launches_per_step = 1
+            launches_per_step = 2  # scan + cut-row merge
         else:
             def step():
                 plan(*csr)
                 wrapper.run(q, (k, v), out=out)
-            launches_per_step = 2
+            launches_per_step = 3  # plan, scan, cut-row merge
     elif kind == "batch" and args.kernel != "auto":
         if args.kernel == "v2":
             ns2 = 8 if ns == 0 else ns
@@ -499,16 +576,17 @@ def run_ours(args, world, rank, local):
     elif kind == "batch":
         def step():
             binding.gqa_decode(q, k, v, bt, sl, SCALE, num_splits=ns, out=out)
-        launches_per_step = 1 if ns in (0, 1) else 2
+        # balanced: scan + cut-row merge; one split: scan; fixed splits: scan + merge
+        launches_per_step = 1 if ns == 1 else 2
     else:
         import sharding
 
         if args.exchange == "p2p":
             dec = sharding.P2PKVRangeDecoder(q.shape[0], q.shape[1], k.shape[2], device)
-            launches_per_step = 1
+            launches_per_step = 2  # scan + merge/exchange kernel
         else:
             dec = sharding.KVRangeDecoder()
-            launches_per_step = 2
+            launches_per_step = 3  # scan + cut-row merge (states), state merge after NCCL
 
         def step():
             out.copy_(dec.decode(q, k, v, bt, sl, SCALE))
@@ -586,6 +664,7 @@ def run_ours(args, world, rank, local):
                                       finish=e2e.drain), world, device)
     if not torch.equal(e2e.last_output(), out):
         raise SystemExit("e2e output differs from the device-resident output")
+    ms_serial = serial_e2e(e2e, decode, args.steps, world, stream, device)
     status = binding.get_status(True)
     if status:
         raise SystemExit(f"device status {status} after timing")
@@ -618,7 +697,10 @@ def run_ours(args, world, rank, local):
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": int(h2d * world),
                 "d2h_bytes_per_step": int(d2h * world),
                 "path": E2E_PATHS[args.api] + "; double-buffered on two copy streams "
-                        "overlapping the previous / next decode"},
+                        "overlapping the previous / next decode",
+                "serial_ms_per_step": round(ms_serial, 5),
+                "serial_value": round(kv_total / (ms_serial * 1e-3) / 1e9, 2),
+                "serial_note": SERIAL_NOTE},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": profiled_traffic(capture, kv_local), "peak_source": peak_src,
@@ -632,6 +714,7 @@ def run_ours(args, world, rank, local):
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        line["cpu_baseline"]["reference_py"] = reference_py_baseline(min(10.0, args.cpu_seconds))
     else:
         line["cpu_baseline"] = None
     print(json.dumps(line), flush=True)
@@ -721,6 +804,7 @@ def run_mla(args, world, rank, local):
     e2e.drain()
     ms_e2e = max_over_ranks(time_loop(lambda: e2e.step(decode), args.steps, world, stream,
                                       finish=e2e.drain), world, device)
+    ms_serial = serial_e2e(e2e, decode, args.steps, world, stream, device)
     if mla_decode.get_status(True):
         raise SystemExit("mla device status set after timing")
     if rank != 0:
@@ -757,7 +841,14 @@ def run_mla(args, world, rank, local):
                 "h2d_bytes_per_step": int(e2e.h2d_bytes * world),
                 "d2h_bytes_per_step": int(e2e.d2h_bytes * world),
                 "path": "mla_decode.mla_decode -> C ABI mla_decode_launch; q, block_table and "
-                        "seq_lens H2D, out D2H every step, double-buffered"},
+                        "seq_lens H2D, out D2H every step, double-buffered",
+                "serial_ms_per_step": round(ms_serial, 5),
+                "serial_value": round(kv_total / (ms_serial * 1e-3) / 1e9, 2),
+                "serial_note": SERIAL_NOTE,
+                "copy_note": "q [B, s_q, h_q, 576] and out [B, s_q, h_q, 512] bf16 cross PCIe "
+                             "every step (18.9 + 16.8 MB at b=128, h_q=128): at ~50 GB/s that "
+                             "is ~0.7 ms of copies against a ~0.5 ms decode, so the pipelined "
+                             "loop is bound by the copies, not the kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": peak_src, "kernel": "mla_decode_kernel",
@@ -866,18 +957,22 @@ def run_dsa(args, world, rank, local):
 
     # each stage alone, on the same inputs (stage times sum to about the step)
     st_scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t, causal)
-    st_idx, st_counts = dsa_decode.dsa_topk(st_scores, sl_t, topk, causal)
     fused = h_q % 128 == 0
     stages = {
         "dsa_indexer_kernel": lambda: dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl_t,
                                                              causal),
-        "dsa_topk_kernel": lambda: dsa_decode.dsa_topk(st_scores, sl_t, topk, causal),
     }
     if fused:
-        # the MLA kernel fetches the selected rows itself
-        stages["mla_decode_rows_kernel"] = lambda: dsa_decode.sparse_mla_decode(
-            q, kv, bt, st_idx, st_counts, scale, ns)
+        # top-k also resolves the selected rows; the MLA kernel fetches them
+        st_idx, st_counts, st_rows = dsa_decode.dsa_topk_rows(st_scores, sl_t, topk, bt,
+                                                              kv.shape[0], causal)
+        stages["dsa_topk_kernel"] = lambda: dsa_decode.dsa_topk_rows(
+            st_scores, sl_t, topk, bt, kv.shape[0], causal)
+        stages["mla_decode_rows_kernel"] = lambda: dsa_decode.sparse_mla_decode_rows(
+            q, kv, st_rows, st_counts, scale, ns)
     else:
+        st_idx, st_counts = dsa_decode.dsa_topk(st_scores, sl_t, topk, causal)
+        stages["dsa_topk_kernel"] = lambda: dsa_decode.dsa_topk(st_scores, sl_t, topk, causal)
         st_pages = dsa_decode.dsa_gather(kv, bt, st_idx)
         table = dsa_decode._identity_table(rows, kpad // 64, device)
         q_rows = q.reshape(rows, 1, h_q, 576)
@@ -898,7 +993,9 @@ def run_dsa(args, world, rank, local):
     sum_S = sum(sl)
     stage_bytes = {
         "dsa_indexer_kernel": sum_S * 128 * 2 + rows * n_idx * (128 * 2 + 4) + s_q * sum_S * 4,
-        "dsa_topk_kernel": sum(sum(v) for v in vis) * 4 + rows * topk * 4,
+        # scores read, indices written (and, fused, the selected rows' block
+        # ids read and their cache rows written)
+        "dsa_topk_kernel": sum(sum(v) for v in vis) * 4 + rows * topk * 4 * (3 if fused else 1),
     }
     if fused:
         stage_bytes["mla_decode_rows_kernel"] = (tok_sel * 1152 + rows * topk * 4 +
@@ -922,6 +1019,7 @@ def run_dsa(args, world, rank, local):
     e2e.drain()
     ms_e2e = max_over_ranks(time_loop(lambda: e2e.step(decode), args.steps, world, stream,
                                       finish=e2e.drain), world, device)
+    ms_serial = serial_e2e(e2e, decode, args.steps, world, stream, device)
     if dsa_decode.get_status(True) or mla_decode.get_status(True):
         raise SystemExit("dsa device status set after timing")
     if rank != 0:
@@ -955,7 +1053,13 @@ def run_dsa(args, world, rank, local):
                 "path": "dsa_decode.sparse_decode -> C ABI dsa_indexer_launch, dsa_topk_launch, "
                         "mla_decode_sparse_launch (h_q % 128 == 0; else dsa_gather_launch + "
                         "mla_decode_launch); q, q_idx, w_idx, block_table and seq_lens H2D, out "
-                        "D2H every step, double-buffered"},
+                        "D2H every step, double-buffered",
+                "serial_ms_per_step": round(ms_serial, 5),
+                "serial_value": round(bytes_total / (ms_serial * 1e-3) / 1e9, 2),
+                "serial_note": SERIAL_NOTE,
+                "copy_note": "q [B, s_q, h_q, 576] (18.9 MB at b=128) and the index queries go up "
+                             "and out [B, s_q, h_q, 512] (16.8 MB) comes back over PCIe every "
+                             "step, more time than the ~0.3 ms decode itself"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": peak_src, "kernel": top,

@@ -46,6 +46,19 @@ cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const 
                             int B, int s_q, int k, int max_tokens, int causal, int* indices,
                             int* counts, cudaStream_t stream);
 
+/* dsa_topk_launch plus, for every selected token, its physical row in the
+ * paged caches, rows[(b * s_q + i) * k + j] = block_table[b, t / 64] * 64 +
+ * t % 64 for token t (-1 padded), so the sparse MLA decode can fetch the row
+ * with one load instead of the token -> block -> row chain
+ * (mla_decode_sparse_rows_launch).  max_tokens <= max_blocks * 64; a block id
+ * outside [0, num_blocks) sets status bit 1 and reads block 0.  No reference
+ * counterpart (roadmap kernel K3). */
+cudaError_t dsa_topk_rows_launch(const float* scores, long long scores_stride,
+                                 const int* seq_lens, int B, int s_q, int k, int max_tokens,
+                                 int causal, const int* block_table, int max_blocks,
+                                 int num_blocks, int* indices, int* counts, int* rows,
+                                 cudaStream_t stream);
+
 /* Latent rows of the selected tokens into gathered[((b * s_q + i) * kpad + slot) * 576],
  * kpad = k rounded up to 64; -1 slots are zero rows. */
 cudaError_t dsa_gather_launch(const gqa_bf16* kv_cache, const int* block_table,

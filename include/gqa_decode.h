@@ -102,10 +102,10 @@ int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, i
  * reference extension allocates per call, python/gqa_decode_ext.cpp:106-109). */
 size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int num_splits);
 
-/* Zero a workspace before its first use.  The balanced schedule keeps
- * per-row arrival counters there and every launch returns them to zero -
- * also a launch whose pipeline waits timed out (status bit 0) - so one
- * initialisation serves any number of launches and shapes. */
+/* Zero a workspace.  Optional: every launch writes each workspace record it
+ * reads (the balanced schedule's per-row and per-CTA records and partial
+ * states), so a workspace needs no initialisation; kept for callers that
+ * clear workspaces as a habit. */
 cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
                                       cudaStream_t stream);
 
@@ -116,10 +116,15 @@ cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
  * launch.  num_blocks > 0 makes the kernel check every block id against
  * [0, num_blocks) (a bad id sets status bit 1, value 2, and reads block 0
  * instead).
- * Workspace: gqa_decode_workspace_bytes, zeroed once with
- * gqa_decode_workspace_init.  Concurrent launches must not share one
- * workspace.  Additive to the reference API (its extension exposes
- * num_splits only on v2, python/gqa_decode_ext.cpp:97-123). */
+ * The balanced schedule is two kernels on `stream`: the scan (one
+ * persistent CTA per SM; rows held whole by a CTA are written out there) and
+ * a small merge of the rows cut between CTAs, launched with programmatic
+ * dependent launch so that it is resident before the scan ends and merges
+ * every cut row across all SMs.
+ * Workspace: gqa_decode_workspace_bytes (no initialisation needed).
+ * Concurrent launches must not share one workspace.  Additive to the
+ * reference API (its extension exposes num_splits only on v2,
+ * python/gqa_decode_ext.cpp:97-123). */
 cudaError_t gqa_decode_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
                               const gqa_bf16* v_cache, const int* block_table,
                               const int* seq_lens, gqa_bf16* out, int B, int Hq, int Hkv,
@@ -173,7 +178,7 @@ cudaError_t gqa_decode_block_table_to_csr(const int* block_table, const int* seq
 
 /* Plan half of the plan/run split (the reference's FlashInfer baseline
  * times only run(), docs/decisions/k1-007): computes on the GPU, into the
- * workspace (gqa_decode_workspace_bytes(B, Hq, Hkv, 0), zeroed once), every
+ * workspace (gqa_decode_workspace_bytes(B, Hq, Hkv, 0)), every
  * CTA's share of the balanced schedule for this batch's lengths.  No host
  * synchronisation.  The plan stays valid for any number of runs - e.g. all
  * layers of a decode step - while the lengths, B, Hq and Hkv stay the same. */
@@ -193,20 +198,22 @@ cudaError_t gqa_decode_run(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa
  * world ranks (1..8); 0 for invalid dims. */
 size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world);
 
-/* KV-range sharded decode with the cross-rank merge fused into the kernel
- * (one launch per rank, no collective library).  Every rank holds the same
- * q, block_table rows for its own contiguous page range of each request,
- * and seq_lens = its tokens per request.  peer_buffers[r] is rank r's
- * exchange buffer (gqa_decode_kvshard_buffer_bytes, zeroed once before the
- * first call, 16-byte aligned) as mapped into this process (CUDA IPC;
- * peer_buffers[rank] is this rank's own buffer).  The warp that finishes a
- * request's state on this rank stores it into every rank's buffer with
- * plain peer stores, publishes it with a system-scope release flag, waits
- * (bounded, 4 s; on timeout status bit 2, value 4, and that output is left
- * unwritten) for every rank's state and merges them into out, identical on
- * all ranks.  epoch: non-zero, the same on every rank for one decode, +1 per
- * decode (states are double-buffered by its parity).  Each rank must run on
- * its own GPU: the ranks' kernels wait for one another.  The reference has no
+/* KV-range sharded decode with the cross-rank merge fused into the decode's
+ * own merge kernel (no collective library).  Every rank holds the same q,
+ * block_table rows for its own contiguous page range of each request, and
+ * seq_lens = its tokens per request.  peer_buffers[r] is rank r's exchange
+ * buffer (gqa_decode_kvshard_buffer_bytes, zeroed once before the first
+ * call, 16-byte aligned) as mapped into this process (CUDA IPC;
+ * peer_buffers[rank] is this rank's own buffer).  After the scan, the merge
+ * kernel merges this rank's state of every (request, q head, 8-dim slice),
+ * stores it into every rank's buffer with plain peer stores, publishes it
+ * with a system-scope release flag, waits (bounded, 4 s; on timeout status
+ * bit 2, value 4, and that slice of out is left unwritten) for every rank's
+ * state of the slice and merges them into out, identical on all ranks.
+ * epoch: non-zero, the same on every rank for one decode, +1 per decode
+ * (states are double-buffered by its parity).  Each rank must run on its own
+ * GPU, and all ranks' GPUs must have the same number of SMs (their merge
+ * kernels wait for one another, item by item).  The reference has no
  * multi-GPU path; the merge is its split identity
  * (kernels/gqa_decode/v2_splitkv.cu:97-107). */
 cudaError_t gqa_decode_kvshard_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
@@ -242,15 +249,16 @@ cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
  * - Shapes whose scratch need exceeds it are rejected with
  *   cudaErrorInvalidValue before anything is launched.  The need is about
  *   (grid / rows_per_request + B) * Hq * 520 bytes (grid = one CTA per SM,
- *   rows_per_request = Hkv / heads_per_row of gqa_decode_plan_info): on a 148-SM
- *   B200 with Hkv = 8, up to ~860 requests at Hq = 32 or ~350 at Hq = 64.
+ *   rows_per_request = Hkv / heads_per_row of gqa_decode_plan_info), the
+ *   gqa_decode_workspace_bytes figure: on a 148-SM B200 with Hkv = 8, up to
+ *   ~860 requests at Hq = 32 or ~350 at Hq = 64.
  * - The first call on a device looks up the array's device address
  *   (cudaGetSymbolAddress) with that device current; make that first call
  *   before any stream capture.  A first call whose lookup fails returns that
  *   error and keeps nothing, so a later call tries the lookup again.
  * - All calls on a device share the array and it keeps the previous call's
- *   contents; each call clears the counters it needs on `stream` before its
- *   kernel.  Calls that overlap on the GPU (other streams, other threads)
+ *   contents; each call writes every record it reads, so nothing needs
+ *   clearing.  Calls that overlap on the GPU (other streams, other threads)
  *   race on the array and must be serialised by the caller. */
 cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf16* k_cache,
                                       const gqa_bf16* v_cache, const int* block_table,
@@ -278,18 +286,18 @@ cudaError_t gqa_decode_get_status(int* status, int clear);
 cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream);
 
 /* Failure-detection self-test of a whole decode: gqa_decode_launch
- * (num_splits == 0) with every pipeline wait limited to wait_limit_ns
- * (0..1,000,000) instead of 4 s, so the waits give up while the copies are
- * still on their way.  Status bit 0 is then set and the rows of the warps
- * that gave up are wrong (NaN, or merged without their part), but the launch
- * ends normally, no copy is left in flight, and the workspace's arrival
- * counters are back at zero: the next gqa_decode_launch on the same
- * workspace is correct.  No reference counterpart. */
+ * (num_splits == 0) in which the copy warp issues no copy, so every pipeline
+ * wait of the tensor-core warps runs out, each after wait_limit_us
+ * (1..1,000,000) instead of 4 s - a stuck pipeline without any fault.  Status
+ * bit 0 is then set and out holds no result (NaN / garbage rows), but the
+ * launch ends normally and every arrival counter in the workspace is back at
+ * zero: the next gqa_decode_launch on the same workspace is correct.  No
+ * reference counterpart. */
 cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
                                                const gqa_bf16* v_cache, const int* block_table,
                                                const int* seq_lens, gqa_bf16* out, int B, int Hq,
                                                int Hkv, int block_size, int max_blocks,
-                                               float scale, int wait_limit_ns, void* workspace,
+                                               float scale, int wait_limit_us, void* workspace,
                                                size_t workspace_bytes, cudaStream_t stream);
 
 /* Library version string. */

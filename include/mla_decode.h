@@ -68,6 +68,18 @@ cudaError_t mla_decode_sparse_launch(const gqa_bf16* q, const gqa_bf16* kv_cache
                                      void* workspace, size_t workspace_bytes,
                                      cudaStream_t stream);
 
+/* mla_decode_sparse_launch reading each selected token's physical cache row
+ * (block id * 64 + slot, as dsa_topk_rows_launch writes them; -1 padded)
+ * instead of its token position and the block table: rows [B * s_q, topk],
+ * counts [B * s_q].  Rows outside [0, num_blocks * 64) set status bit 1 and
+ * read row 0. */
+cudaError_t mla_decode_sparse_rows_launch(const gqa_bf16* q, const gqa_bf16* kv_cache,
+                                          const int* cache_rows, const int* counts, int topk,
+                                          gqa_bf16* out, float* lse, int B, int s_q, int h_q,
+                                          int page_size, int num_blocks, float softmax_scale,
+                                          int num_splits, void* workspace,
+                                          size_t workspace_bytes, cudaStream_t stream);
+
 /* Device status word of the MLA kernels (bit 0: a bounded wait gave up,
  * bit 1: block id out of range); reset clears it.  Synchronises the device. */
 int mla_decode_get_status(int reset);

@@ -345,7 +345,23 @@ struct TopkParams {
   int* indices;  // [B, s_q, k]
   int* counts;   // [B, s_q] selected tokens (min(k, visible)), or null
   int B, s_q, k, max_tokens, causal;
+  // Optional: the selected tokens' physical cache rows (block id * 64 +
+  // slot, -1 padded) into rows [B, s_q, k], resolved through block_table.
+  const int* block_table;
+  int* rows;
+  int max_blocks, num_blocks;
 };
+
+// Cache row of token t of request b: block_table[b, t / 64] * 64 + t % 64.
+// A block id outside [0, num_blocks) sets status bit 1 and reads block 0.
+__device__ __forceinline__ int cache_row(const TopkParams& p, int b, int t) {
+  int page = __ldg(p.block_table + static_cast<size_t>(b) * p.max_blocks + (t >> 6));
+  if (static_cast<unsigned>(page) >= static_cast<unsigned>(p.num_blocks)) {
+    raise(2);
+    page = 0;
+  }
+  return page * kPage + (t & (kPage - 1));
+}
 
 constexpr int kTopkThreads = 1024;
 constexpr int kTopkSmemKeys = 40 * 1024;  // rows up to this many tokens keep their keys in smem
@@ -373,11 +389,15 @@ __global__ void __launch_bounds__(kTopkThreads) dsa_topk_kernel(const __grid_con
   const int vis = p.causal ? max(0, min(S, S - p.s_q + 1 + i)) : S;
   const float* sc = p.scores + static_cast<size_t>(r) * p.stride;
   int* out = p.indices + static_cast<size_t>(r) * p.k;
+  int* rows_out = p.rows ? p.rows + static_cast<size_t>(r) * p.k : nullptr;
   const int k = p.k;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (p.counts && tid == 0) p.counts[r] = min(k, vis);
   if (vis <= k) {  // every visible token is selected
-    for (int e = tid; e < k; e += blockDim.x) out[e] = e < vis ? e : -1;
+    for (int e = tid; e < k; e += blockDim.x) {
+      out[e] = e < vis ? e : -1;
+      if (rows_out) rows_out[e] = e < vis ? cache_row(p, b, e) : -1;
+    }
     return;
   }
   if (kSmemKeys) {
@@ -530,7 +550,12 @@ __global__ void __launch_bounds__(kTopkThreads) dsa_topk_kernel(const __grid_con
     scan_offsets(nc, sel_base);
     for (int c = 0; c < nc; ++c) {
       const unsigned bal = __ballot_sync(0xffffffffu, (sel_bits >> c) & 1u);
-      if ((sel_bits >> c) & 1u) out[offs[c * 32 + warp] + __popc(bal & lt)] = (c0 + c) * blockDim.x + tid;
+      if ((sel_bits >> c) & 1u) {
+        const int pos = offs[c * 32 + warp] + __popc(bal & lt);
+        const int tok = (c0 + c) * blockDim.x + tid;
+        out[pos] = tok;
+        if (rows_out) rows_out[pos] = cache_row(p, b, tok);
+      }
     }
     sel_base = sh_total;
     __syncthreads();  // offs is rewritten by the next super-chunk
@@ -673,16 +698,24 @@ cudaError_t dsa_indexer_launch(const gqa_bf16* q_idx, const float* w_idx, const 
   return cudaSuccess;
 }
 
-cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const int* seq_lens,
-                            int B, int s_q, int k, int max_tokens, int causal, int* indices,
-                            int* counts, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+cudaError_t topk_impl(const float* scores, long long scores_stride, const int* seq_lens, int B,
+                      int s_q, int k, int max_tokens, int causal, int* indices, int* counts,
+                      const int* block_table, int max_blocks, int num_blocks, int* rows,
+                      cudaStream_t stream) {
   using namespace gqa::dsa;
   if (B < 0 || s_q < 1 || k < 1 || max_tokens < 0 || scores_stride < max_tokens)
+    return cudaErrorInvalidValue;
+  if (rows && (!block_table || max_blocks <= 0 || num_blocks <= 0 ||
+               max_tokens > static_cast<long long>(max_blocks) * kPage))
     return cudaErrorInvalidValue;
   if (B == 0) return cudaSuccess;
   if (!scores || !seq_lens || !indices) return cudaErrorInvalidValue;
   TopkParams p{scores, scores_stride, seq_lens, indices, counts, B, s_q, k, max_tokens,
-               causal ? 1 : 0};
+               causal ? 1 : 0, block_table, rows, max_blocks, num_blocks};
   const unsigned grid = static_cast<unsigned>(B * s_q);
   if (max_tokens <= kTopkSmemKeys) {
     const int smem = max(max_tokens, 1) * 4;
@@ -699,6 +732,27 @@ cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const 
     dsa_topk_kernel<false><<<grid, kTopkThreads, 0, stream>>>(p);
   }
   return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t dsa_topk_launch(const float* scores, long long scores_stride, const int* seq_lens,
+                            int B, int s_q, int k, int max_tokens, int causal, int* indices,
+                            int* counts, cudaStream_t stream) {
+  return topk_impl(scores, scores_stride, seq_lens, B, s_q, k, max_tokens, causal, indices,
+                   counts, nullptr, 0, 0, nullptr, stream);
+}
+
+cudaError_t dsa_topk_rows_launch(const float* scores, long long scores_stride,
+                                 const int* seq_lens, int B, int s_q, int k, int max_tokens,
+                                 int causal, const int* block_table, int max_blocks,
+                                 int num_blocks, int* indices, int* counts, int* rows,
+                                 cudaStream_t stream) {
+  if (!rows) return cudaErrorInvalidValue;
+  return topk_impl(scores, scores_stride, seq_lens, B, s_q, k, max_tokens, causal, indices,
+                   counts, block_table, max_blocks, num_blocks, rows, stream);
 }
 
 cudaError_t dsa_gather_launch(const gqa_bf16* kv_cache, const int* block_table,

@@ -34,57 +34,50 @@ int make_shape_plan(int Hq, int Hkv, ShapePlan* sp) {
   return 0;
 }
 
+// BALANCED grid: one CTA per resident slot, capped so the merge kernel's
+// per-CTA list of cut rows fits its shared memory.
+int balanced_grid(int sms, int occ) { return std::min(sms * occ, kMaxScanGrid); }
+
+// [plan (header + one entry per CTA) | prefix [B + 1] | row records [B*NHG] |
+//  CTA records [grid] | m | l | acc].  Nothing needs zeroing: every launch
+// writes every record it reads.
+BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
+  auto align_up = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t rows = static_cast<size_t>(B) * sp.NHG;
+  const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
+  const size_t slots = static_cast<size_t>(grid) + rows;
+  BalancedLayout L;
+  L.plan = 0;
+  L.prefix = L.plan + align_up((kPlanHeader + static_cast<size_t>(grid) * kPlanEntry) *
+                               sizeof(long long));
+  L.rowinfo = L.prefix + align_up((static_cast<size_t>(B) + 1) * sizeof(long long));
+  L.ends = L.rowinfo + align_up(rows * sizeof(int2));
+  L.m = L.ends + align_up(static_cast<size_t>(grid) * sizeof(int2));
+  L.l = L.m + align_up(slots * qhr * sizeof(float));
+  L.acc = L.l + align_up(slots * qhr * sizeof(float));
+  L.total = L.acc + align_up(slots * qhr * kHeadDim * sizeof(float));
+  return L;
+}
+
 }  // namespace gqa
 
 namespace {
 
+using gqa::BalancedLayout;
 using gqa::ShapePlan;
+using gqa::balanced_grid;
+using gqa::balanced_layout;
 
 thread_local cudaError_t t_last_error = cudaSuccess;
 
 constexpr size_t kAlign = 256;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
-// Workspace layout.  The first kCounterSlots ints hold the balanced
-// schedule's arrival counters for every shape: every launch leaves them at
-// zero and no partial state of any shape or schedule is ever stored there, so
-// one zeroing (gqa_decode_workspace_init) keeps them valid across launches of
-// different shapes.  A batch needing more counters than that gets a larger
-// counter region that the launcher clears before each launch.
-constexpr size_t kCounterSlots = 65536;
-
-size_t counter_region(size_t counters) {
-  return align_up(std::max(counters, kCounterSlots) * sizeof(int));
-}
-
-struct BalancedLayout {
-  size_t counters, ncounters, plan, prefix, m, l, acc, total;
-};
-
-// [counters | plan (header + one entry per CTA) | prefix [B + 1] | m | l | acc]
-BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid) {
-  const size_t rows = static_cast<size_t>(B) * sp.NHG;
-  const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
-  const size_t slots = static_cast<size_t>(grid) + rows;
-  BalancedLayout L;
-  L.counters = 0;
-  L.ncounters = (static_cast<size_t>(grid) + 2 * rows) * sp.ncw;
-  L.plan = counter_region(L.ncounters);
-  L.prefix = L.plan + align_up((gqa::kPlanHeader + static_cast<size_t>(grid) * gqa::kPlanEntry) *
-                               sizeof(long long));
-  L.m = L.prefix + align_up((static_cast<size_t>(B) + 1) * sizeof(long long));
-  L.l = L.m + align_up(slots * qhr * sizeof(float));
-  L.acc = L.l + align_up(slots * qhr * sizeof(float));
-  L.total = L.acc + align_up(slots * qhr * gqa::kHeadDim * sizeof(float));
-  return L;
-}
-
 // Fixed splits through gqa_decode_launch: the reference's [B, Hq, ns](,128)
-// partial arrays, placed after the standard counter region.
+// partial arrays, acc then m then l.
 size_t fixed_ws_bytes(int B, int Hq, int ns) {
   const size_t states = static_cast<size_t>(B) * Hq * ns;
-  return counter_region(0) + align_up(states * gqa::kHeadDim * sizeof(float)) +
-         2 * align_up(states * sizeof(float));
+  return align_up(states * gqa::kHeadDim * sizeof(float)) + 2 * align_up(states * sizeof(float));
 }
 
 // Per-device facts, cached: SM count and resident CTAs for a (threads, smem).
@@ -270,13 +263,64 @@ struct Exchange {
   void* const* peers = nullptr;
 };
 
-size_t exchange_flag_bytes(int B, const ShapePlan& sp, int world) {
-  return align_up(2ull * world * static_cast<size_t>(B) * sp.NHG * sp.ncw * sizeof(unsigned));
+size_t exchange_items(int B, int Hq) {
+  return static_cast<size_t>(B) * Hq * gqa::kXSlices;
 }
 
-size_t exchange_bytes(int B, int Hq, const ShapePlan& sp, int world) {
-  return exchange_flag_bytes(B, sp, world) +
-         2ull * world * static_cast<size_t>(B) * Hq * gqa::kXStride * sizeof(float);
+size_t exchange_flag_bytes(int B, int Hq, int world) {
+  return align_up(2ull * world * exchange_items(B, Hq) * sizeof(unsigned));
+}
+
+size_t exchange_bytes(int B, int Hq, int world) {
+  return exchange_flag_bytes(B, Hq, world) +
+         2ull * world * exchange_items(B, Hq) * gqa::kXItem * sizeof(float);
+}
+
+// Scan + cut-row merge of the BALANCED schedule.  `p` carries the inputs,
+// the output mode and the schedule; the workspace supplies the records and
+// partial slots.  The merge kernel runs one CTA per SM.
+cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsigned char* w,
+                            const ShapePlan& sp, int sms, int grid, cudaStream_t stream,
+                            const Exchange* xchg) {
+  gqa::CutMergeParams mp{};
+  if (xchg) {
+    if (!p.out || xchg->world < 1 || xchg->world > gqa::kMaxPeers || xchg->rank < 0 ||
+        xchg->rank >= xchg->world || xchg->epoch == 0 || !xchg->peers)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < xchg->world; ++r) {
+      if (!xchg->peers[r] || !aligned16(xchg->peers[r])) return cudaErrorInvalidValue;
+      mp.xpeer[r] = static_cast<unsigned char*>(xchg->peers[r]);
+    }
+    p.out_mode = gqa::kOutExchange;
+    mp.xworld = xchg->world;
+    mp.xrank = xchg->rank;
+    mp.xepoch = xchg->epoch;
+    mp.xitems = static_cast<long long>(exchange_items(p.B, p.Hq));
+    mp.xflag_bytes = static_cast<long long>(exchange_flag_bytes(p.B, p.Hq, xchg->world));
+  }
+  p.row_info = reinterpret_cast<int2*>(w + lay.rowinfo);
+  p.ends = reinterpret_cast<int2*>(w + lay.ends);
+  p.part_m = reinterpret_cast<float*>(w + lay.m);
+  p.part_l = reinterpret_cast<float*>(w + lay.l);
+  p.part_acc = reinterpret_cast<float*>(w + lay.acc);
+  p.schedule = gqa::kBalanced;
+  p.num_splits = 0;
+  cudaError_t e = gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+  if (e != cudaSuccess) return e;
+  mp.row_info = p.row_info;
+  mp.ends = p.ends;
+  mp.part_m = p.part_m;
+  mp.part_l = p.part_l;
+  mp.part_acc = p.part_acc;
+  mp.out = p.out;
+  mp.res_m = p.res_m;
+  mp.res_l = p.res_l;
+  mp.res_acc = p.res_acc;
+  mp.rows = p.B * p.NHG;
+  mp.QHR = p.HG * p.G;
+  mp.grid = grid;
+  mp.out_mode = p.out_mode;
+  return gqa::launch_cut_merge(mp, sms, stream);
 }
 
 // BALANCED schedule: bf16 output, unnormalised states, or peer exchange.
@@ -285,7 +329,7 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
                          float* res_acc, int B, int Hq, int Hkv, int bs, int max_blocks,
                          int num_blocks, float scale, void* ws, size_t ws_bytes,
                          cudaStream_t stream, const Exchange* xchg = nullptr,
-                         unsigned long long wait_ns = gqa::kWaitLimitNs) {
+                         unsigned long long wait_ns = gqa::kWaitLimitNs, int no_copies = 0) {
   ShapePlan sp;
   const void* dst = out ? static_cast<const void*>(out) : static_cast<const void*>(res_acc);
   cudaError_t e = check_common(q, k, v, bt, sl, dst, B, Hq, Hkv, bs, max_blocks, &sp);
@@ -295,49 +339,30 @@ cudaError_t run_balanced(const gqa_bf16* q, const gqa_bf16* k, const gqa_bf16* v
   int sms = 0, occ = 0;
   e = device_facts(sp, &sms, &occ);
   if (e != cudaSuccess) return e;
-  const int grid = sms * occ;
+  const int grid = balanced_grid(sms, occ);
   const BalancedLayout lay = balanced_layout(B, sp, grid);
   if (!ws || ws_bytes < lay.total || !aligned16(ws)) return cudaErrorInvalidValue;
-  unsigned char* w = static_cast<unsigned char*>(ws);
-  if (lay.ncounters > kCounterSlots) {
-    e = cudaMemsetAsync(w + lay.counters, 0, lay.ncounters * sizeof(int), stream);
-    if (e != cudaSuccess) return e;
-  }
   gqa::ScanParams p =
       base_params(q, k, v, bt, sl, B, Hq, Hkv, bs, max_blocks, num_blocks, scale, sp);
   p.out = out;
   p.out_mode = out ? gqa::kOutBf16 : gqa::kOutState;
-  if (xchg) {
-    if (!out || xchg->world < 1 || xchg->world > gqa::kMaxPeers || xchg->rank < 0 ||
-        xchg->rank >= xchg->world || xchg->epoch == 0 || !xchg->peers)
-      return cudaErrorInvalidValue;
-    p.out_mode = gqa::kOutExchange;
-    p.xworld = xchg->world;
-    p.xrank = xchg->rank;
-    p.xepoch = xchg->epoch;
-    p.xunits = B * sp.NHG * sp.ncw;
-    p.xflag_bytes = static_cast<long long>(exchange_flag_bytes(B, sp, xchg->world));
-    for (int r = 0; r < xchg->world; ++r) {
-      if (!xchg->peers[r] || !aligned16(xchg->peers[r])) return cudaErrorInvalidValue;
-      p.xpeer[r] = static_cast<unsigned char*>(xchg->peers[r]);
-    }
-  }
   p.res_m = res_m;
   p.res_l = res_l;
   p.res_acc = res_acc;
-  p.counters = reinterpret_cast<int*>(w + lay.counters);
-  p.part_m = reinterpret_cast<float*>(w + lay.m);
-  p.part_l = reinterpret_cast<float*>(w + lay.l);
-  p.part_acc = reinterpret_cast<float*>(w + lay.acc);
-  p.schedule = gqa::kBalanced;
-  p.num_splits = 0;
   p.wait_ns = wait_ns;
-  return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+  p.selftest_no_copies = no_copies;
+  return launch_balanced(p, lay, static_cast<unsigned char*>(ws), sp, sms, grid, stream, xchg);
 }
 
 }  // namespace
 
 namespace gqa {
+
+cudaError_t launch_balanced_noexchange(ScanParams& p, const BalancedLayout& lay,
+                                       unsigned char* w, const ShapePlan& sp, int sms, int grid,
+                                       cudaStream_t stream) {
+  return launch_balanced(p, lay, w, sp, sms, grid, stream, nullptr);
+}
 
 // Bodies of the reference-signature launchers.  The C-linkage entry points
 // below and the C++-linkage ones in gqa_cxx_abi.cu both call these; each
@@ -437,7 +462,7 @@ int gqa_decode_query_plan(int B, int Hq, int Hkv, int num_splits, int num_sms, i
   plan->smem_bytes = sp.smem_bytes;
   const long long slots = static_cast<long long>(num_sms) * ctas_per_sm;
   if (num_splits == 0) {
-    plan->grid = static_cast<int>(slots);
+    plan->grid = static_cast<int>(std::min<long long>(slots, gqa::kMaxScanGrid));
     plan->workspace_bytes = balanced_layout(B, sp, plan->grid).total;
   } else {
     const long long tasks = static_cast<long long>(B) * sp.NHG * num_splits;
@@ -455,7 +480,7 @@ size_t gqa_decode_workspace_bytes(int B, int Hq, int Hkv, int num_splits) {
   if (num_splits > 0) return num_splits > 1 ? fixed_ws_bytes(B, Hq, num_splits) : 0;
   int sms = 0, occ = 0;
   if (device_facts(sp, &sms, &occ) != cudaSuccess) return 0;
-  return balanced_layout(B, sp, sms * occ).total;
+  return balanced_layout(B, sp, balanced_grid(sms, occ)).total;
 }
 
 cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
@@ -483,7 +508,7 @@ cudaError_t gqa_decode_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
     const size_t need = fixed_ws_bytes(B, Hq, num_splits);
     if (!workspace || workspace_bytes < need || !aligned16(workspace)) return cudaErrorInvalidValue;
     const size_t states = static_cast<size_t>(B) * Hq * num_splits;
-    unsigned char* w = static_cast<unsigned char*>(workspace) + counter_region(0);
+    unsigned char* w = static_cast<unsigned char*>(workspace);
     acc = reinterpret_cast<float*>(w);
     m = reinterpret_cast<float*>(w + align_up(states * gqa::kHeadDim * sizeof(float)));
     l = reinterpret_cast<float*>(w + align_up(states * gqa::kHeadDim * sizeof(float)) +
@@ -529,7 +554,7 @@ cudaError_t gqa_decode_plan(const gqa_decode_pages* pages, int B, int Hq, int Hk
   int sms = 0, occ = 0;
   e = device_facts(sp, &sms, &occ);
   if (e != cudaSuccess) return e;
-  const int grid = sms * occ;
+  const int grid = balanced_grid(sms, occ);
   const BalancedLayout lay = balanced_layout(B, sp, grid);
   if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
     return cudaErrorInvalidValue;
@@ -564,15 +589,11 @@ cudaError_t gqa_decode_run(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa
   int sms = 0, occ = 0;
   e = device_facts(sp, &sms, &occ);
   if (e != cudaSuccess) return e;
-  const int grid = sms * occ;
+  const int grid = balanced_grid(sms, occ);
   const BalancedLayout lay = balanced_layout(B, sp, grid);
   if (!workspace || workspace_bytes < lay.total || !aligned16(workspace))
     return cudaErrorInvalidValue;
   unsigned char* w = static_cast<unsigned char*>(workspace);
-  if (lay.ncounters > kCounterSlots) {
-    e = cudaMemsetAsync(w + lay.counters, 0, lay.ncounters * sizeof(int), stream);
-    if (e != cudaSuccess) return e;
-  }
   gqa::ScanParams p = base_params(q, k_cache, v_cache, pg.bt, pg.sl, B, Hq, Hkv, pg.bs,
                                   pg.max_blocks, pg.num_blocks, scale, sp);
   p.kv_indptr = pg.indptr;
@@ -582,12 +603,7 @@ cudaError_t gqa_decode_run(const gqa_bf16* q, const gqa_bf16* k_cache, const gqa
   p.plan = reinterpret_cast<const long long*>(w + lay.plan);
   p.out = out;
   p.out_mode = gqa::kOutBf16;
-  p.counters = reinterpret_cast<int*>(w + lay.counters);
-  p.part_m = reinterpret_cast<float*>(w + lay.m);
-  p.part_l = reinterpret_cast<float*>(w + lay.l);
-  p.part_acc = reinterpret_cast<float*>(w + lay.acc);
-  p.schedule = gqa::kBalanced;
-  return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+  return launch_balanced(p, lay, w, sp, sms, grid, stream, nullptr);
 }
 
 size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world) {
@@ -595,7 +611,7 @@ size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world) {
   if (gqa::make_shape_plan(Hq, Hkv, &sp) != 0 || B <= 0 || world < 1 ||
       world > gqa::kMaxPeers)
     return 0;
-  return exchange_bytes(B, Hq, sp, world);
+  return exchange_bytes(B, Hq, world);
 }
 
 cudaError_t gqa_decode_kvshard_launch(const gqa_bf16* q, const gqa_bf16* k_cache,
@@ -673,12 +689,13 @@ cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16
                                                const gqa_bf16* v_cache, const int* block_table,
                                                const int* seq_lens, gqa_bf16* out, int B, int Hq,
                                                int Hkv, int block_size, int max_blocks,
-                                               float scale, int wait_limit_ns, void* workspace,
+                                               float scale, int wait_limit_us, void* workspace,
                                                size_t workspace_bytes, cudaStream_t stream) {
-  if (wait_limit_ns < 0 || wait_limit_ns > 1000000) return cudaErrorInvalidValue;
+  if (wait_limit_us <= 0 || wait_limit_us > 1000000) return cudaErrorInvalidValue;
   return run_balanced(q, k_cache, v_cache, block_table, seq_lens, out, nullptr, nullptr, nullptr,
                       B, Hq, Hkv, block_size, max_blocks, 0, scale, workspace, workspace_bytes,
-                      stream, nullptr, static_cast<unsigned long long>(wait_limit_ns));
+                      stream, nullptr, static_cast<unsigned long long>(wait_limit_us) * 1000ull,
+                      1);
 }
 
 const char* gqa_decode_version(void) { return "gqa_decode_b200 0.1.0 (sm_100a)"; }

@@ -44,10 +44,13 @@ enum OutMode : int {
 };
 
 // KV-range sharding over peer memory: every rank owns one exchange buffer
-// [flags: u32 [2][world][units] | states: f32 [2][world][B*Hq][kXStride]],
-// mapped into every other rank; [2] is the epoch parity.
+// [flags: u32 [2][world][items] | states: f32 [2][world][items][kXItem]],
+// mapped into every other rank; [2] is the epoch parity, an item is one
+// 8-dim slice of one (request, q head): items = B * Hq * 16.
 constexpr int kMaxPeers = 8;
-constexpr int kXStride = 132;  // floats per state: m, l, 2 pad, acc[128] (16-byte aligned)
+constexpr int kXItem = 12;       // floats per item state: m, l, 2 pad, acc[8] (16-byte aligned)
+constexpr int kXSlices = 16;     // items per (request, q head)
+constexpr int kMaxScanGrid = 2048;  // BALANCED grid cap (the merge kernel's per-CTA list)
 
 // Shape-only launch plan (no device state): how heads map to warps and how
 // large the stage ring is.
@@ -67,6 +70,13 @@ struct ShapePlan {
 
 // Returns 0 on success, or a negative code for unsupported shapes.
 int make_shape_plan(int Hq, int Hkv, ShapePlan* plan);
+
+// Byte offsets of the BALANCED schedule's workspace regions (gqa_api.cu).
+struct BalancedLayout {
+  size_t plan, prefix, rowinfo, ends, m, l, acc, total;
+};
+int balanced_grid(int sms, int occ);
+BalancedLayout balanced_layout(int B, const ShapePlan& sp, int grid);
 
 struct ScanParams {
   const __nv_bfloat16* q;        // [B, Hq, 128]
@@ -91,7 +101,11 @@ struct ScanParams {
   float* part_m;
   float* part_l;
   float* part_acc;
-  int* counters;                 // BALANCED: [rows * ncw] arrival counters
+  // BALANCED: per row {first CTA holding a part, parts} and per CTA {row,
+  // parts} of the cut row whose last part it holds ({-1, 0}: none), written
+  // by every launch for the merge kernel.
+  int2* row_info;                // [B * NHG]
+  int2* ends;                    // [grid]
   // kOutState: the final per-(b, q-head) state is written unnormalised
   // here instead of bf16 `out` (KV-range sharding across GPUs).
   float* res_m;                  // [B, Hq]
@@ -109,10 +123,30 @@ struct ScanParams {
   // wait-timeout self-test passes a tiny one).  The producer's final drain of
   // its own copies always uses kWaitLimitNs.
   unsigned long long wait_ns;
+  // Failure-detection self-test only: the copy warp issues no copy, so every
+  // consumer wait runs out (after wait_ns) as it would on a stuck pipeline.
+  int selftest_no_copies;
+};
+
+// Merge of the BALANCED scan's cut rows (and, with kOutExchange, the
+// cross-rank exchange of every row), gqa_merge.cu.
+struct CutMergeParams {
+  const int2* row_info;          // [rows] {first CTA, parts}
+  const int2* ends;              // [grid] {row, parts} / {-1, 0}
+  const float* part_m;           // [slot, QHR]
+  const float* part_l;
+  const float* part_acc;         // [slot, QHR, 128]
+  __nv_bfloat16* out;            // [B, Hq, 128]
+  float* res_m;                  // kOutState: [B, Hq]
+  float* res_l;
+  float* res_acc;                // kOutState: [B, Hq, 128]
+  int rows, QHR;                 // rows = B * NHG, QHR = q heads per row
+  int grid;                      // the scan's grid
+  int out_mode;                  // OutMode
   // kOutExchange
   int xworld, xrank;
   unsigned xepoch;               // != 0, identical on every rank for one decode
-  int xunits;                    // rows * ncw flags per (parity, source rank)
+  long long xitems;              // B * Hq * kXSlices flags per (parity, source rank)
   long long xflag_bytes;         // byte offset of the state area in a buffer
   unsigned char* xpeer[kMaxPeers];  // exchange buffer of every rank ([xrank] = own)
 };
@@ -149,6 +183,14 @@ struct ShardMergeParams {
 // Kernel launchers (gqa_scan.cu / gqa_simt.cu).  They launch and return the
 // launch status; validation happens in the C-ABI layer.
 cudaError_t launch_scan(const ScanParams& p, int grid, int threads, int smem, cudaStream_t s);
+// The cut-row merge, launched with programmatic dependent launch right after
+// the scan on the same stream; `grid` = CTAs of the merge kernel.
+cudaError_t launch_cut_merge(const CutMergeParams& p, int grid, cudaStream_t s);
+// Scan + cut-row merge of the BALANCED schedule with bf16 output or states,
+// the records and partial slots placed in `w` by `lay` (gqa_api.cu).
+cudaError_t launch_balanced_noexchange(ScanParams& p, const BalancedLayout& lay,
+                                       unsigned char* w, const ShapePlan& sp, int sms, int grid,
+                                       cudaStream_t stream);
 cudaError_t launch_fixed_merge(const MergeParams& p, cudaStream_t s);
 cudaError_t launch_simt(const SimtParams& p, cudaStream_t s);
 cudaError_t launch_shard_merge(const ShardMergeParams& p, cudaStream_t s);

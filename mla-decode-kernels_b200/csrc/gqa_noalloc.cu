@@ -1,7 +1,8 @@
 // Decode entry point for callers that cannot allocate device memory.
 //
 // gqa_decode_launch needs a caller-provided workspace for the balanced
-// schedule's arrival counters and split partial states.  Some callers have
+// schedule's records of the rows it cuts between CTAs and their partial
+// softmax states.  Some callers have
 // no way to provide one: a host engine that hands all of HBM to its own
 // KV-cache pool at start-up and treats any later device allocation as a bug
 // (cudaMalloc would synchronise the device mid-step and can fail once the
@@ -22,13 +23,11 @@
 namespace {
 
 constexpr size_t kScratchBytes = GQA_DECODE_NOALLOC_SCRATCH_BYTES;
-constexpr size_t kAlign = 256;
 
-// Scratch shared by every gqa_decode_launch_noalloc call on a device:
-// [arrival counters | m | l | acc], laid out per call for its shape.
+// Scratch shared by every gqa_decode_launch_noalloc call on a device: the
+// balanced schedule's row and CTA records and split partial states, laid out
+// per call for its shape.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
-
-size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct DeviceState {
   unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch; null until set up
@@ -82,7 +81,7 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   DeviceState* st = &g_state[dev];
-  int grid = 0;
+  int grid = 0, sms = 0;
   unsigned char* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
@@ -105,24 +104,15 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
       st->occ_smem = sp.smem_bytes;
       st->occ = o;
     }
-    grid = st->sms * st->occ;
+    grid = gqa::balanced_grid(st->sms, st->occ);
+    sms = st->sms;
   }
 
-  // Balanced-schedule layout inside the static scratch.
-  const size_t rows = static_cast<size_t>(B) * sp.NHG;
-  const size_t qhr = static_cast<size_t>(sp.HG) * sp.G;
-  const size_t slots = static_cast<size_t>(grid) + rows;
-  const size_t counters_bytes = (static_cast<size_t>(grid) + 2 * rows) * sp.ncw * sizeof(int);
-  const size_t off_m = align_up(counters_bytes);
-  const size_t off_l = off_m + align_up(slots * qhr * sizeof(float));
-  const size_t off_acc = off_l + align_up(slots * qhr * sizeof(float));
-  const size_t need = off_acc + align_up(slots * qhr * gqa::kHeadDim * sizeof(float));
-  if (need > kScratchBytes) return cudaErrorInvalidValue;  // shape too large for the scratch
-
-  // The arrival counters must start at zero; the scratch keeps whatever the
-  // previous call left, so clear them on the same stream first.
-  e = cudaMemsetAsync(scratch, 0, counters_bytes, stream);
-  if (e != cudaSuccess) return e;
+  // Balanced-schedule workspace layout inside the static scratch.  Every
+  // region is written before it is read in each call, so nothing needs
+  // clearing between calls.
+  const gqa::BalancedLayout lay = gqa::balanced_layout(B, sp, grid);
+  if (lay.total > kScratchBytes) return cudaErrorInvalidValue;  // shape too large for the scratch
 
   gqa::ScanParams p{};
   p.q = q;
@@ -134,10 +124,6 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.kv_indices = block_table;
   p.kv_last = seq_lens;
   p.out = out;
-  p.counters = reinterpret_cast<int*>(scratch);
-  p.part_m = reinterpret_cast<float*>(scratch + off_m);
-  p.part_l = reinterpret_cast<float*>(scratch + off_l);
-  p.part_acc = reinterpret_cast<float*>(scratch + off_acc);
   p.B = B;
   p.Hq = Hq;
   p.Hkv = Hkv;
@@ -153,10 +139,8 @@ extern "C" cudaError_t gqa_decode_launch_noalloc(const gqa_bf16* q, const gqa_bf
   p.row_stride = sp.row_stride;
   p.stage_bytes = sp.stage_bytes;
   p.nstages = sp.nstages;
-  p.schedule = gqa::kBalanced;
-  p.num_splits = 0;
   p.out_mode = gqa::kOutBf16;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.wait_ns = gqa::kWaitLimitNs;
-  return gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+  return gqa::launch_balanced_noexchange(p, lay, scratch, sp, sms, grid, stream);
 }

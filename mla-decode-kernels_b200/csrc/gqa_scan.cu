@@ -229,315 +229,26 @@ __device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float a, float 
   *reinterpret_cast<uint2*>(dst) = v;
 }
 
-// ---- peer exchange (kOutExchange) -------------------------------------------
-//
-// The warp that owns the final state of a (row, warp unit) on this rank
-// stores it into slot `xrank` of every rank's exchange buffer (plain stores
-// to peer memory over NVLink), publishes it with a system-scope release
-// flag per destination, waits (bounded) for the flags of all ranks in its
-// own buffer, and merges the `xworld` states into `out`.  Flags and states
-// are double-buffered by epoch parity: a rank can only run one decode ahead
-// of a peer, so it never overwrites what the peer is still reading.
-
-__device__ __forceinline__ unsigned* xflag(const ScanParams& p, int owner, int src, int unit) {
-  return reinterpret_cast<unsigned*>(p.xpeer[owner]) +
-         (static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * p.xunits + unit);
-}
-
-__device__ __forceinline__ float* xstate(const ScanParams& p, int owner, int src, size_t bh) {
-  const size_t rows = static_cast<size_t>(p.B) * p.Hq;
-  return reinterpret_cast<float*>(p.xpeer[owner] + p.xflag_bytes) +
-         ((static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * rows + bh) * kXStride);
-}
-
-// Push one head's state, held lane-major (lane = 4 dims), to every rank.
-__device__ __forceinline__ void xput_lanes(const ScanParams& p, size_t bh, float m, float l,
-                                           float4 a, int lane) {
-  for (int o = 0; o < p.xworld; ++o) {
-    float* d = xstate(p, o, p.xrank, bh);
-    if (lane == 0) {
-      d[0] = m;
-      d[1] = l;
-    }
-    reinterpret_cast<float4*>(d + 4)[lane] = a;
-  }
-}
-
-// Publish this warp's states of unit `unit`, wait for every rank's, merge
-// heads [bh0, bh0 + cnt) and write bf16 out.  Rows empty on every rank give 0.
-// The (m, l) of every rank (lane = rank) and the acc rows of kHeads heads of
-// every rank are loaded together, one L2 round trip per kHeads heads.
-template <int kHeads>
-__device__ __noinline__ void xfinish(const ScanParams& p, int unit, size_t bh0, int cnt, int lane) {
-  __threadfence_system();
-  __syncwarp();
-  if (lane < p.xworld) st_release_sys(xflag(p, lane, p.xrank, unit), p.xepoch);
-  bool ok = true;
-  if (lane < p.xworld) {
-    const unsigned* f = xflag(p, p.xrank, lane, unit);
-    ok = ld_acquire_sys(f) == p.xepoch;
-    if (!ok) {
-      const unsigned long long t0 = global_timer_ns();
-      while (!ok && global_timer_ns() - t0 < kWaitLimitNs) ok = ld_acquire_sys(f) == p.xepoch;
-    }
-  }
-  if (!__all_sync(kFull, ok)) {
-    if (lane == 0) raise_status(kStatusPeerTimeout);
-    return;
-  }
-  const int src = min(lane, p.xworld - 1);  // source rank clamped: valid on every lane
-  for (int i0 = 0; i0 < cnt; i0 += kHeads) {
-    const int hmax = min(kHeads, cnt - i0) - 1;
-    float mk[kHeads], lk[kHeads];
-    float4 x[kHeads][kMaxPeers];
-    #pragma unroll
-    for (int i = 0; i < kHeads; ++i) {
-      const size_t bh = bh0 + i0 + min(i, hmax);
-      const float* st = xstate(p, p.xrank, src, bh);
-      mk[i] = __ldcg(st);
-      lk[i] = __ldcg(st + 1);
-      #pragma unroll
-      for (int o = 0; o < kMaxPeers; ++o)
-        x[i][o] = o < p.xworld
-                      ? __ldcg(reinterpret_cast<const float4*>(xstate(p, p.xrank, o, bh) + 4) +
-                               lane)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    #pragma unroll
-    for (int i = 0; i < kHeads; ++i) {
-      if (i > hmax) continue;
-      float M = lane < p.xworld ? mk[i] : -INFINITY;
-      #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(kFull, M, off));
-      const float w = (lane < p.xworld && M != -INFINITY) ? exp2f(mk[i] - M) : 0.f;
-      float L = lk[i] * w;
-      #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(kFull, L, off);
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-      #pragma unroll
-      for (int o = 0; o < kMaxPeers; ++o) {
-        const float f = __shfl_sync(kFull, w, o);  // 0 for o >= xworld
-        a.x += x[i][o].x * f;
-        a.y += x[i][o].y * f;
-        a.z += x[i][o].z * f;
-        a.w += x[i][o].w * f;
-      }
-      __nv_bfloat16* o = p.out + (bh0 + i0 + i) * kHeadDim + 4 * lane;
-      if (M == -INFINITY)
-        store_bf16x4(o, 0.f, 0.f, 0.f, 0.f);
-      else
-        store_bf16x4(o, a.x / L, a.y / L, a.z / L, a.w / L);
-    }
-  }
-}
-
-// Final state of head bh, lane-major, to its destination by output mode
-// (kOutExchange: pushed to the ranks; the caller then runs xfinish).
-__device__ __forceinline__ void emit_final(const ScanParams& p, size_t bh, float M, float L,
-                                           float4 a, int lane) {
-  if (p.out_mode == kOutState) {
-    if (lane == 0) {
-      p.res_m[bh] = M;
-      p.res_l[bh] = L;
-    }
-    *reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 4 * lane) = a;
-  } else if (p.out_mode == kOutExchange) {
-    xput_lanes(p, bh, M, L, a, lane);
-  } else {
-    store_bf16x4(p.out + bh * kHeadDim + 4 * lane, a.x / L, a.y / L, a.z / L, a.w / L);
-  }
-}
-
 // Zero output (or a neutral state: m = -inf, l = 0, acc = 0) for the q heads
-// [hbase, hbase+cnt) of request b, which has no tokens on this rank.  The
-// reference's kernels divide by l = 0 there (docs/decisions/k1-004);
-// python/reference.py yields 0.  `unit` = row * ncw + warp (kOutExchange).
-template <int kXHeads>
-__device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbase, int cnt, int unit, int lane) {
+// [hbase, hbase+cnt) of request b, which has no tokens.  The reference's
+// kernels divide by l = 0 there (docs/decisions/k1-004); python/reference.py
+// yields 0.  With kOutExchange nothing is written here: the row is recorded
+// with no parts and the merge kernel exchanges its neutral state.
+__device__ __forceinline__ void write_empty(const ScanParams& p, int b, int hbase, int cnt,
+                                            int lane) {
   const size_t bh0 = static_cast<size_t>(b) * p.Hq + hbase;
   for (int n = 0; n < cnt; ++n) {
-    if (p.out_mode == kOutBf16)
+    if (p.out_mode == kOutBf16) {
       store_bf16x4(p.out + (bh0 + n) * kHeadDim + 4 * lane, 0.f, 0.f, 0.f, 0.f);
-    else
-      emit_final(p, bh0 + n, -INFINITY, 0.f, make_float4(0.f, 0.f, 0.f, 0.f), lane);
-  }
-  if (p.out_mode == kOutExchange) xfinish<kXHeads>(p, unit, bh0, cnt, lane);
-}
-
-// Partial states merged in one step.  Rows cut into more parts than this are
-// merged in two levels: the last warp of every group of kMergeGroup
-// consecutive CTAs merges the group into the group's first slot, and the
-// last of those merges the groups.
-constexpr int kMergeGroup = 16;
-
-// Merge n unnormalised states of this warp's q heads [jj0, jj0 + cnt),
-// stored in slots first, first + stride, ...  With `final_` the result goes
-// to the output of q heads bh0 + i (see emit_final); otherwise it overwrites
-// slot `first`.
-//
-// The merge is bound by L2 latency, not bandwidth, so loads are issued in
-// batches that are all in flight together: the (m, l) of up to 32 parts per
-// head (lane = part) and the acc rows of the first kBatch parts of kHeads
-// heads (lane = 4 output dims) go out before the first result is used, so a
-// row cut into at most kBatch parts costs one L2 round trip per kHeads heads.
-// Every address is clamped into range, so all loads are valid on every lane;
-// out-of-range parts get weight 0.
-template <int kHeads, int kBatch>
-__device__ __forceinline__ void merge_parts(const ScanParams& p, long long first, int stride, int n,
-                                         int jj0, int cnt, int lane, bool final_, size_t bh0) {
-  const int QHR = p.HG * p.G;
-  for (int i0 = 0; i0 < cnt; i0 += kHeads) {
-    const int hmax = min(kHeads, cnt - i0) - 1;
-    const size_t head0 = static_cast<size_t>(jj0) + i0;
-    // (m, l) of parts [0, 32) and acc of parts [0, kBatch), all in flight
-    float mk[kHeads], lk[kHeads];
-    float4 x[kHeads][kBatch];
-    {
-      const size_t srow =
-          static_cast<size_t>(first + static_cast<long long>(min(lane, n - 1)) * stride) * QHR +
-          head0;
-      #pragma unroll
-      for (int i = 0; i < kHeads; ++i) {
-        mk[i] = __ldcg(p.part_m + srow + min(i, hmax));
-        lk[i] = __ldcg(p.part_l + srow + min(i, hmax));
+    } else if (p.out_mode == kOutState) {
+      if (lane == 0) {
+        p.res_m[bh0 + n] = -INFINITY;
+        p.res_l[bh0 + n] = 0.f;
       }
-      #pragma unroll
-      for (int kk = 0; kk < kBatch; ++kk) {
-        const size_t sk =
-            static_cast<size_t>(first + static_cast<long long>(min(kk, n - 1)) * stride) * QHR +
-            head0;
-        #pragma unroll
-        for (int i = 0; i < kHeads; ++i)
-          x[i][kk] = __ldcg(reinterpret_cast<const float4*>(
-                                p.part_acc + (sk + min(i, hmax)) * kHeadDim) + lane);
-      }
-    }
-    // M per head over all parts
-    float M[kHeads];
-    #pragma unroll
-    for (int i = 0; i < kHeads; ++i) {
-      float mv = lane < n ? mk[i] : -INFINITY;
-      #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, off));
-      M[i] = mv;
-    }
-    for (int c0 = 32; c0 < n; c0 += 32) {  // rows cut into more than 32 parts
-      const size_t srow =
-          static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
-              QHR + head0;
-      #pragma unroll
-      for (int i = 0; i < kHeads; ++i) {
-        float mv = c0 + lane < n ? __ldcg(p.part_m + srow + min(i, hmax)) : -INFINITY;
-        #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mv = fmaxf(mv, __shfl_xor_sync(kFull, mv, off));
-        M[i] = fmaxf(M[i], mv);
-      }
-    }
-    // weights, L and acc, 32 parts per lane chunk
-    float L[kHeads];
-    float4 a[kHeads];
-    #pragma unroll
-    for (int i = 0; i < kHeads; ++i) {
-      L[i] = 0.f;
-      a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    for (int c0 = 0; c0 < n; c0 += 32) {
-      if (c0 > 0) {
-        const size_t srow =
-            static_cast<size_t>(first + static_cast<long long>(min(c0 + lane, n - 1)) * stride) *
-                QHR + head0;
-        #pragma unroll
-        for (int i = 0; i < kHeads; ++i) {
-          mk[i] = __ldcg(p.part_m + srow + min(i, hmax));
-          lk[i] = __ldcg(p.part_l + srow + min(i, hmax));
-        }
-      }
-      float w[kHeads];
-      #pragma unroll
-      for (int i = 0; i < kHeads; ++i) {
-        w[i] = (c0 + lane < n && M[i] != -INFINITY) ? exp2f(mk[i] - M[i]) : 0.f;
-        float lw = lk[i] * w[i];
-        #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(kFull, lw, off);
-        L[i] += lw;
-      }
-      const int nc = min(32, n - c0);
-      for (int k0 = 0; k0 < nc; k0 += kBatch) {
-        if (c0 > 0 || k0 > 0) {
-          #pragma unroll
-          for (int kk = 0; kk < kBatch; ++kk) {
-            const size_t sk = static_cast<size_t>(
-                                  first + static_cast<long long>(min(c0 + k0 + kk, n - 1)) *
-                                              stride) * QHR + head0;
-            #pragma unroll
-            for (int i = 0; i < kHeads; ++i)
-              x[i][kk] = __ldcg(reinterpret_cast<const float4*>(
-                                    p.part_acc + (sk + min(i, hmax)) * kHeadDim) + lane);
-          }
-        }
-        #pragma unroll
-        for (int kk = 0; kk < kBatch; ++kk) {
-          #pragma unroll
-          for (int i = 0; i < kHeads; ++i) {
-            // weight of part c0 + k0 + kk (lane k0 + kk of the chunk); 0 past n
-            const float f = k0 + kk < nc ? __shfl_sync(kFull, w[i], (k0 + kk) & 31) : 0.f;
-            a[i].x += x[i][kk].x * f;
-            a[i].y += x[i][kk].y * f;
-            a[i].z += x[i][kk].z * f;
-            a[i].w += x[i][kk].w * f;
-          }
-        }
-      }
-    }
-    #pragma unroll
-    for (int i = 0; i < kHeads; ++i) {
-      if (i > hmax) continue;
-      if (final_) {
-        emit_final(p, bh0 + i0 + i, M[i], L[i], a[i], lane);
-      } else {
-        const size_t st = static_cast<size_t>(first) * QHR + head0 + i;
-        if (lane == 0) {
-          p.part_m[st] = M[i];
-          p.part_l[st] = L[i];
-        }
-        *reinterpret_cast<float4*>(p.part_acc + st * kHeadDim + 4 * lane) = a[i];
-      }
+      *reinterpret_cast<float4*>(p.res_acc + (bh0 + n) * kHeadDim + 4 * lane) =
+          make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-}
-
-// Register budget of a merge: kHeads x kBatch float4 acc loads in flight.
-// The register file is split between the SM's four schedulers, so a 9-warp
-// CTA (three warps on one scheduler) gets at most 168 registers a thread and
-// a 17-warp CTA at most 96.  The merge is one non-inlined function called
-// from one place; with 12 float4 loads in flight (2 heads x 6 parts) it
-// fits beside the streaming loop's live registers without spills, and a row
-// cut into up to 6 parts (the common case: a CTA's range is a sixth of a
-// rep-shape row) costs one L2 round trip per 2 heads.  The 17-warp kernel
-// keeps 8 in flight.
-template <int kMaxWarps>
-__device__ __noinline__ void merge_rows(const ScanParams& p, long long first, int stride, int n,
-                                        int jj0, int cnt, int lane, bool final_, size_t bh0) {
-  if constexpr (kMaxWarps <= 9)
-    merge_parts<2, 6>(p, first, stride, n, jj0, cnt, lane, final_, bh0);
-  else
-    merge_parts<4, 2>(p, first, stride, n, jj0, cnt, lane, final_, bh0);
-}
-
-// Count one arrival on *ctr; true (on every lane) for the warp whose arrival
-// completes `total`.  That warp also re-arms the counter for the next launch
-// after it has used the data (see callers).
-// Ordering: __syncwarp (bar.warp.sync) orders every lane's partial-state
-// stores before lane 0's release-acquire add; release is cumulative, so the
-// last arriver's acquire sees every earlier warp's states, and the second
-// __syncwarp orders its lanes' reads after that acquire.
-__device__ __forceinline__ bool arrive_last(int* ctr, int total, int lane) {
-  __syncwarp();
-  int last = 0;
-  if (lane == 0) last = atom_add_acq_rel_gpu(ctr, 1) == total - 1;
-  last = __shfl_sync(kFull, last, 0);
-  __syncwarp();
-  return last != 0;
 }
 
 }  // namespace
@@ -559,6 +270,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   // full_k[s] = bars + 8 s, full_v[s] = bars + 8 (ns + s), empty[s] = bars + 8 (2 ns + s)
   const uint32_t ns8 = 8u * p.nstages;
 
+  // The merge kernel queued behind this one (programmatic dependent launch)
+  // may start now; it waits for this grid's results itself.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.nstages; ++s) {
       mbar_init(bars + 8 * s, 1);
@@ -615,6 +329,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
     long long issued = 0;
     bool ok = true;
     Seg s;
+    if (p.selftest_no_copies) ok = false;  // self-test: nothing arrives in the ring
     while (ok && iter_next(it, p, cap, s)) {
       if (s.kind == kZero) continue;
       const int* bt_row = page_row(p, s.b);
@@ -673,7 +388,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   }
 
   // ------------------------------ consumers -------------------------------
-  constexpr int kXHeads = kMaxWarps <= 9 ? 2 : 1;  // heads per batch of the peer merge
   const int hl = warp / p.NT;
   const int qt = warp - hl * p.NT;
   const int j0 = qt * 8;
@@ -688,32 +402,45 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   const uint32_t half = static_cast<uint32_t>(kStageTokens * p.row_stride);
 
   if (p.schedule == kBalanced) {
-    // Requests without tokens occupy no stages; CTA (b mod grid) writes them.
+    // Requests without tokens occupy no stages; CTA (b mod grid) writes them
+    // and records their rows as having no parts.
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
       if (req_len(p, b, cap) != 0) continue;
-      for (int hg = 0; hg < p.NHG; ++hg)
-        write_empty<kXHeads>(p, b, (hg * p.HG + hl) * p.G + j0, cnt,
-                             (b * p.NHG + hg) * p.ncw + warp, lane);
+      for (int hg = 0; hg < p.NHG; ++hg) {
+        write_empty(p, b, (hg * p.HG + hl) * p.G + j0, cnt, lane);
+        if (warp == 0 && lane == 0) p.row_info[b * p.NHG + hg] = make_int2(0, 0);
+      }
     }
   }
 
   int stage = 0;
   uint32_t phase = 0;
   // Set when one of this warp's pipeline waits timed out.  The warp then
-  // stops reading the ring but still walks its segments, publishing an empty
-  // state (m = -inf, l = 0, acc = 0) for each, so every arrival counter is
-  // completed and re-armed and every peer flag is published exactly as in a
-  // normal launch: the workspace stays valid for the next launch, and only
-  // the rows this warp held are wrong (status bit 0 says so).
+  // stops reading the ring but still walks its segments, writing an empty
+  // state (m = -inf, l = 0, acc = 0) for each, so the merge kernel finds every
+  // part and every row record it expects (and the peers every state) exactly
+  // as after a normal launch; only the rows this warp held are wrong (status
+  // bit 0 says so).
   bool dead = false;
+  bool first_seg = true;
+  // No cut row ends in this CTA unless its first segment is a row's last part.
+  if (p.schedule == kBalanced && warp == 0 && lane == 0) p.ends[blockIdx.x] = make_int2(-1, 0);
   Seg s;
   while (iter_next(it, p, cap, s)) {
     const int hk = s.hg * p.HG + hl;
     const int hbase = hk * p.G + j0;
+    if (first_seg && p.schedule == kBalanced && warp == 0 && lane == 0 && s.kind == kPartial &&
+        s.s1 == (s.S + kStageTokens - 1) / kStageTokens)
+      p.ends[blockIdx.x] = make_int2(s.row, s.nparts);
+    first_seg = false;
     if (s.kind == kZero) {
-      write_empty<kXHeads>(p, s.b, hbase, cnt, s.row * p.ncw + warp, lane);
+      write_empty(p, s.b, hbase, cnt, lane);
       continue;
     }
+    // The CTA holding a row's first stage records where the row's parts are
+    // (BALANCED: slots cfirst + row, ... in consecutive CTAs).
+    if (p.schedule == kBalanced && s.s0 == 0 && warp == 0 && lane == 0)
+      p.row_info[s.row] = make_int2(static_cast<int>(s.cfirst), s.nparts);
     uint32_t qf[8][2];
     {
       const bool has = g < cnt;
@@ -812,29 +539,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       l1 += __shfl_xor_sync(kFull, l1, off);
     }
     const int n0 = 2 * tig, n1 = 2 * tig + 1;
-    if (s.kind == kDirect && p.out_mode == kOutExchange) {
-      // Row finished inside this CTA: push the fragments' state to the ranks.
-      for (int o = 0; o < p.xworld; ++o) {
-        #pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          const int head = n ? n1 : n0;
-          if (head >= cnt) continue;
-          float* d = xstate(p, o, p.xrank, static_cast<size_t>(s.b) * p.Hq + hbase + head);
-          if (g == 0) {
-            d[0] = n ? m1 : m0;
-            d[1] = n ? l1 : l0;
-          }
-          #pragma unroll
-          for (int mt = 0; mt < 8; ++mt) {
-            d[4 + mt * 16 + g] = acc[mt][n];
-            d[4 + mt * 16 + g + 8] = acc[mt][2 + n];
-          }
-        }
-      }
-      xfinish<kXHeads>(p, s.row * p.ncw + warp, static_cast<size_t>(s.b) * p.Hq + hbase, cnt,
-                       lane);
-      continue;
-    }
     if (s.kind == kDirect && p.out_mode == kOutBf16) {
       #pragma unroll
       for (int n = 0; n < 2; ++n) {
@@ -850,13 +554,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
       }
       continue;
     }
-    // Unnormalised state: the CTA's partial slot, or (kOutState) the
-    // request's final shard state.
+    // Unnormalised state: the CTA's partial slot (also a whole row's state
+    // with kOutExchange, which the merge kernel sends to the peers), or
+    // (kOutState) the request's final shard state.
     float* dm;
     float* dl;
     float* da;
     size_t idx0, idx1;
-    if (s.kind == kDirect) {
+    if (s.kind == kDirect && p.out_mode == kOutState) {
       dm = p.res_m;
       dl = p.res_l;
       da = p.res_acc;
@@ -889,40 +594,6 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
         a[mt * 16 + g] = acc[mt][n];
         a[mt * 16 + g + 8] = acc[mt][2 + n];
       }
-    }
-    if (s.kind == kPartial && p.schedule == kBalanced) {
-      // Count this warp's partial; the warp that completes a group / the row
-      // merges it.  Counters: [group counters by first slot | row counters],
-      // (grid + rows) and rows entries of ncw each.
-      const long long rows = static_cast<long long>(p.B) * p.NHG;
-      const long long grid = gridDim.x;
-      int* row_ctr = p.counters + static_cast<size_t>(grid + rows + s.row) * p.ncw + warp;
-      const int jj0 = hl * p.G + j0;
-      const size_t bh0 = static_cast<size_t>(s.b) * p.Hq + hbase;
-      // Level 0 merges this CTA's group of kMergeGroup consecutive parts
-      // (rows cut into more parts than that), level 1 the row.  One merge
-      // call site, so the merge is inlined once.
-      const long long gi = (static_cast<long long>(blockIdx.x) - s.cfirst) / kMergeGroup;
-      const long long g0 = s.cfirst + gi * kMergeGroup;
-      const bool grouped = s.nparts > kMergeGroup;
-      const int gsz = grouped ? static_cast<int>(min(static_cast<long long>(kMergeGroup),
-                                                     s.cfirst + s.nparts - g0))
-                              : 1;
-      const int nrow = grouped ? (s.nparts + kMergeGroup - 1) / kMergeGroup : s.nparts;
-      bool finished = false;
-      for (int level = gsz > 1 ? 0 : 1; level < 2; ++level) {
-        int* ctr = level == 0 ? p.counters + static_cast<size_t>(g0 + s.row) * p.ncw + warp
-                              : row_ctr;
-        const int n = level == 0 ? gsz : nrow;
-        if (!arrive_last(ctr, n, lane)) break;
-        merge_rows<kMaxWarps>(p, level == 0 ? g0 + s.row : s.cfirst + s.row,
-                              level == 0 || !grouped ? 1 : kMergeGroup, n, jj0, cnt, lane,
-                              level == 1, bh0);
-        if (lane == 0) *ctr = 0;
-        finished = level == 1;
-      }
-      if (finished && p.out_mode == kOutExchange)
-        xfinish<kXHeads>(p, s.row * p.ncw + warp, bh0, cnt, lane);
     }
   }
 }
@@ -1204,3 +875,5 @@ cudaError_t read_status(int* status, int clear) {
 }
 
 }  // namespace gqa
+
+#include "gqa_merge.cuh"

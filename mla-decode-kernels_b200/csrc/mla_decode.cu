@@ -63,6 +63,8 @@ struct Params {
   CUtensorMap tm_q_rope;   // the same rows, box {32, NH}, 64B swizzle (128-row groups)
   CUtensorMap tm_kv_rope;  // the same rows, box {32, 64}, 64B swizzle (128-row groups)
   const int* sparse_idx;     // sparse: [B * s_q, topk] token positions per query position
+                             // (or, with sparse_rows, physical cache rows)
+  int sparse_rows;           // sparse: sparse_idx holds block id * 64 + slot, no block_table
   const __nv_bfloat16* kv;   // sparse: the cache (rows copied by the producer warp)
   const __nv_bfloat16* q;    // 128-row groups: q rows (loaded straight into tensor memory)
   int* hdr;                  // 128-row groups: [2] total tiles T and working pairs Pe (0: one unit per pair)
@@ -883,20 +885,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Rows::kThreads, 1)
         const int b = wa.u / p.n_hg, hg = wa.u % p.n_hg;
         const int qpos = (hg * 128) / p.h_q;
         const int* idx = p.sparse_idx + static_cast<size_t>(b * p.s_q + qpos) * p.topk;
-        const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
         int* q_t = rowq + (t % (G::kRowAhead + 1)) * kPage;
         #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int j = wa.i * kPage + 2 * lane + u;
           int row = -1;
           if (j < wa.S) {
-            const int tok = __ldg(idx + j);
-            int page = tok >= 0 && tok < p.max_blocks * kPage ? __ldg(bt + (tok >> 6)) : -1;
-            if (page < 0 || page >= p.num_blocks) {
-              raise(kStatusBadPage);
-              page = 0;
+            if (p.sparse_rows) {
+              // rows resolved by the top-k kernel: one load, no lookup chain
+              row = __ldg(idx + j);
+              if (row < 0 || static_cast<long long>(row) >= static_cast<long long>(p.num_blocks) * kPage) {
+                raise(kStatusBadPage);
+                row = 0;
+              }
+            } else {
+              const int* bt = p.block_table + static_cast<size_t>(b) * p.max_blocks;
+              const int tok = __ldg(idx + j);
+              int page = tok >= 0 && tok < p.max_blocks * kPage ? __ldg(bt + (tok >> 6)) : -1;
+              if (page < 0 || page >= p.num_blocks) {
+                raise(kStatusBadPage);
+                page = 0;
+              }
+              row = page * kPage + (tok & (kPage - 1));
             }
-            row = page * kPage + (tok & (kPage - 1));
             // this CTA's half of the row into L2 while the tile waits its turn
             const char* rp =
                 reinterpret_cast<const char*>(p.kv) + static_cast<size_t>(row) * (kD * 2);
@@ -1905,7 +1916,8 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
                             const int* seq_lens, const int* sparse_idx, int topk, gqa_bf16* out,
                             float* lse, int B, int s_q, int h_q, int page_size, int max_blocks,
                             int num_blocks, float softmax_scale, int causal, int num_splits,
-                            void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                            void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                            int sparse_rows = 0) {
   using namespace gqa::mla;
   if (B < 0 || s_q <= 0 || h_q <= 0 || page_size != kPage || max_blocks <= 0 || num_blocks <= 0 ||
       num_splits < 1 || num_splits > 64)
@@ -1915,10 +1927,12 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
   const int rows = s_q * h_q;
   const Layout L = layout_for(rows);
   if (L.NH == 0) return cudaErrorInvalidValue;
-  if (!q || !kv_cache || !block_table || !seq_lens || !out || !lse) return cudaErrorInvalidValue;
+  if (!q || !kv_cache || (!block_table && !sparse_rows) || !seq_lens || !out || !lse)
+    return cudaErrorInvalidValue;
   if (!aligned16(q) || !aligned16(kv_cache)) return cudaErrorMisalignedAddress;
   Params p{};
   p.sparse_idx = sparse_idx;
+  p.sparse_rows = sparse_rows;
   p.kv = reinterpret_cast<const __nv_bfloat16*>(kv_cache);
   p.topk = topk;
 
@@ -2053,6 +2067,18 @@ cudaError_t mla_decode_sparse_launch(const gqa_bf16* q, const gqa_bf16* kv_cache
   return mla_launch_impl(q, kv_cache, block_table, counts, indices, topk, out, lse, B, s_q, h_q,
                          page_size, max_blocks, num_blocks, softmax_scale, 0, num_splits,
                          workspace, workspace_bytes, stream);
+}
+
+cudaError_t mla_decode_sparse_rows_launch(const gqa_bf16* q, const gqa_bf16* kv_cache,
+                                          const int* cache_rows, const int* counts, int topk,
+                                          gqa_bf16* out, float* lse, int B, int s_q, int h_q,
+                                          int page_size, int num_blocks, float softmax_scale,
+                                          int num_splits, void* workspace,
+                                          size_t workspace_bytes, cudaStream_t stream) {
+  if (!cache_rows) return cudaErrorInvalidValue;
+  return mla_launch_impl(q, kv_cache, nullptr, counts, cache_rows, topk, out, lse, B, s_q, h_q,
+                         page_size, 1, num_blocks, softmax_scale, 0, num_splits, workspace,
+                         workspace_bytes, stream, 1);
 }
 
 int mla_decode_get_status(int reset) {

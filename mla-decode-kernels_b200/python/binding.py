@@ -60,10 +60,10 @@ _ws_cache = {}
 
 
 def workspace(device, nbytes):
-    """Zero-initialised uint8 workspace of at least nbytes on device, cached.
+    """uint8 workspace of at least nbytes on device, cached.
 
-    The balanced schedule's arrival counters live at its start and every
-    launch leaves them at zero, so one zeroing serves all later launches.
+    The balanced schedule keeps its per-launch records and partial states
+    there (every launch writes what it reads, so no zeroing is needed).
     Every stream of the device shares it: decodes that may run at the same
     time on different streams must not both use it (pass each its own
     workspace through the C ABI, or order the streams).
@@ -166,10 +166,9 @@ class BatchDecodeWithPagedKVCacheWrapper:
             raise ValueError("q and kv must be bf16")
         B = last_page_len.shape[0]
         nbytes = _ext.workspace_bytes(B, num_qo_heads, num_kv_heads, 0)
-        # The plan and the arrival counters live in the workspace, so every
-        # wrapper keeps its own: two wrappers planned for different batches
-        # (or run on different streams) never share one.  The counters must
-        # start at zero; each run leaves them at zero again.
+        # The plan and each run's records and partial states live in the
+        # workspace, so every wrapper keeps its own: two wrappers planned for
+        # different batches (or run on different streams) never share one.
         if self._user_ws is not None:
             if self._user_ws.numel() * self._user_ws.element_size() < nbytes:
                 raise ValueError(f"workspace_buffer needs {nbytes} bytes")

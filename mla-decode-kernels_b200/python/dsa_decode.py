@@ -61,6 +61,15 @@ def dsa_topk(scores, cache_seqlens, topk, causal=False):
     return _ext.dsa_topk(scores, cache_seqlens, int(topk), bool(causal))
 
 
+def dsa_topk_rows(scores, cache_seqlens, topk, block_table, num_blocks, causal=False):
+    """dsa_topk plus each selected token's physical row in the paged caches,
+    block_table[b, t // 64] * 64 + t % 64 (-1 padded): (indices, counts,
+    rows [B, s_q, topk] int32).  The sparse MLA decode then fetches every
+    selected row with one load instead of the token -> block -> row chain."""
+    return _ext.dsa_topk_rows(scores, cache_seqlens, int(topk), bool(causal), block_table,
+                              int(num_blocks))
+
+
 def dsa_gather(k_cache, block_table, indices):
     """Latent rows of the selected tokens as pages [B * s_q * kpad / 64, 64, 1,
     576] (kpad = topk rounded up to 64; -1 slots are zero rows)."""
@@ -101,10 +110,35 @@ def sparse_mla_decode(q, k_cache, block_table, indices, counts, softmax_scale=No
             lse.view(B, s_q, h_q).permute(0, 2, 1).contiguous())
 
 
+def sparse_mla_decode_rows(q, k_cache, rows, counts, softmax_scale=None, num_splits=0):
+    """sparse_mla_decode (fused, h_q a multiple of 128) over the physical
+    cache rows dsa_topk_rows resolved: identical output, one dependent load
+    fewer per selected row in the kernel's copy warp."""
+    B, s_q, h_q = q.shape[0], q.shape[1], q.shape[2]
+    if softmax_scale is None:
+        softmax_scale = q.shape[-1] ** -0.5
+    kpad = (rows.shape[-1] + PAGE - 1) // PAGE * PAGE
+    if num_splits == 0:
+        num_splits = int(_ext.mla_pick_splits(B * s_q, 1, h_q, kpad // PAGE,
+                                              mla_decode._num_sms(q.device)))
+    nbytes = int(_ext.mla_workspace_bytes(B, s_q, h_q, num_splits))
+    ws = (mla_decode.workspace(q.device, nbytes) if nbytes
+          else torch.empty(0, dtype=torch.uint8, device=q.device))
+    return _ext.mla_decode_sparse_rows(q, k_cache, rows, counts, float(softmax_scale),
+                                       int(num_splits), ws)
+
+
 def sparse_decode(q, k_cache, q_idx, w_idx, k_idx, block_table, cache_seqlens, topk,
                   softmax_scale=None, causal=False, num_splits=0):
-    """The whole sparse decode step: (out, lse, indices)."""
+    """The whole sparse decode step: (out, lse, indices).  With h_q a
+    multiple of 128 the top-k kernel also resolves the selected tokens'
+    cache rows and the MLA kernel reads those."""
     scores = dsa_indexer(q_idx, w_idx, k_idx, block_table, cache_seqlens, causal)
+    if q.shape[2] % 128 == 0:
+        indices, counts, rows = dsa_topk_rows(scores, cache_seqlens, topk, block_table,
+                                              k_cache.shape[0], causal)
+        out, lse = sparse_mla_decode_rows(q, k_cache, rows, counts, softmax_scale, num_splits)
+        return out, lse, indices
     indices, counts = dsa_topk(scores, cache_seqlens, topk, causal)
     out, lse = sparse_mla_decode(q, k_cache, block_table, indices, counts, softmax_scale,
                                  num_splits)

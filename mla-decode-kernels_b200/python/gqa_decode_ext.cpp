@@ -10,6 +10,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "gqa_decode.h"
@@ -535,6 +536,58 @@ std::vector<torch::Tensor> mla_decode_sparse(torch::Tensor q, torch::Tensor kv_c
   return {out, lse};
 }
 
+// Sparse attention over selected cache rows: rows [B, s_q, topk] int32
+// physical rows (block id * 64 + slot, -1 padded) as dsa_topk_rows resolves
+// them, counts [B, s_q] -> (out [B, s_q, h_q, 512] bf16, lse [B, h_q, s_q]).
+std::vector<torch::Tensor> mla_decode_sparse_rows(torch::Tensor q, torch::Tensor kv_cache,
+                                                  torch::Tensor rows, torch::Tensor counts,
+                                                  double softmax_scale, int64_t num_splits,
+                                                  torch::Tensor workspace) {
+  TORCH_CHECK(q.is_cuda() && kv_cache.is_cuda() && rows.is_cuda() && counts.is_cuda(),
+              "all tensors must be CUDA tensors");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && kv_cache.scalar_type() == torch::kBFloat16,
+              "q and kv_cache must be bf16");
+  TORCH_CHECK(rows.scalar_type() == torch::kInt32 && counts.scalar_type() == torch::kInt32,
+              "rows and counts must be int32");
+  TORCH_CHECK(q.is_contiguous() && kv_cache.is_contiguous() && rows.is_contiguous() &&
+                  counts.is_contiguous(),
+              "all tensors must be contiguous");
+  TORCH_CHECK(q.dim() == 4 && q.size(3) == 576, "q must be [B, s_q, h_q, 576]");
+  TORCH_CHECK(q.size(2) % 128 == 0, "the fused sparse decode takes h_q a multiple of 128");
+  TORCH_CHECK(kv_cache.dim() == 4 && kv_cache.size(1) == 64 && kv_cache.size(2) == 1 &&
+                  kv_cache.size(3) == 576,
+              "kv_cache must be [num_blocks, 64, 1, 576]");
+  const int64_t B = q.size(0), s_q = q.size(1), h_q = q.size(2);
+  TORCH_CHECK(rows.dim() == 3 && rows.size(0) == B && rows.size(1) == s_q,
+              "rows must be [B, s_q, topk]");
+  TORCH_CHECK(counts.dim() == 2 && counts.size(0) == B && counts.size(1) == s_q,
+              "counts must be [B, s_q]");
+  TORCH_CHECK(kv_cache.device() == q.device() && rows.device() == q.device() &&
+                  counts.device() == q.device(),
+              "all tensors must be on the same device");
+  TORCH_CHECK(num_splits >= 1 && num_splits <= 64, "num_splits must be in [1, 64]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto out = torch::empty({B, s_q, h_q, 512}, q.options());
+  auto lse = torch::empty({B, h_q, s_q}, q.options().dtype(torch::kFloat32));
+  const size_t need = mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
+                                                 static_cast<int>(h_q), static_cast<int>(num_splits));
+  const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
+  TORCH_CHECK(need == 0 || (workspace.is_cuda() && workspace.device() == q.device() &&
+                            workspace.is_contiguous() && ws_bytes >= need),
+              "workspace must be a contiguous CUDA tensor of at least ", need, " bytes");
+  check_launch(mla_decode_sparse_rows_launch(
+                   reinterpret_cast<const gqa_bf16*>(q.data_ptr()),
+                   reinterpret_cast<const gqa_bf16*>(kv_cache.data_ptr()), rows.data_ptr<int>(),
+                   counts.data_ptr<int>(), static_cast<int>(rows.size(2)),
+                   reinterpret_cast<gqa_bf16*>(out.data_ptr()), lse.data_ptr<float>(),
+                   static_cast<int>(B), static_cast<int>(s_q), static_cast<int>(h_q), 64,
+                   static_cast<int>(kv_cache.size(0)), static_cast<float>(softmax_scale),
+                   static_cast<int>(num_splits), need ? workspace.data_ptr() : nullptr, ws_bytes,
+                   at::cuda::getCurrentCUDAStream()),
+               "mla_decode_sparse_rows");
+  return {out, lse};
+}
+
 int64_t mla_workspace_bytes(int64_t B, int64_t s_q, int64_t h_q, int64_t num_splits) {
   return static_cast<int64_t>(mla_decode_workspace_bytes(static_cast<int>(B), static_cast<int>(s_q),
                                                          static_cast<int>(h_q),
@@ -631,6 +684,43 @@ std::vector<torch::Tensor> dsa_topk(torch::Tensor scores, torch::Tensor seq_lens
   return {indices, counts};
 }
 
+// dsa_topk plus the selected tokens' physical cache rows through block_table
+// -> (indices, counts, rows [B, s_q, k] int32, -1 padded).
+std::vector<torch::Tensor> dsa_topk_rows(torch::Tensor scores, torch::Tensor seq_lens, int64_t k,
+                                         bool causal, torch::Tensor block_table,
+                                         int64_t num_blocks) {
+  TORCH_CHECK(scores.is_cuda() && scores.scalar_type() == torch::kFloat32 &&
+                  scores.is_contiguous() && scores.dim() == 3,
+              "scores must be a contiguous fp32 CUDA tensor [B, s_q, S]");
+  TORCH_CHECK(seq_lens.is_cuda() && seq_lens.scalar_type() == torch::kInt32 &&
+                  seq_lens.is_contiguous() && seq_lens.dim() == 1 &&
+                  seq_lens.size(0) == scores.size(0) && seq_lens.device() == scores.device(),
+              "seq_lens must be a contiguous int32 CUDA tensor [B] on scores' device");
+  TORCH_CHECK(block_table.is_cuda() && block_table.scalar_type() == torch::kInt32 &&
+                  block_table.is_contiguous() && block_table.dim() == 2 &&
+                  block_table.size(0) == scores.size(0) && block_table.device() == scores.device(),
+              "block_table must be a contiguous int32 CUDA tensor [B, max_blocks] on scores' device");
+  TORCH_CHECK(k >= 1 && k <= (1 << 20), "k must be in [1, 2^20]");
+  TORCH_CHECK(num_blocks >= 1, "num_blocks must be positive");
+  const c10::cuda::CUDAGuard guard(scores.device());
+  const int64_t B = scores.size(0), s_q = scores.size(1), S = scores.size(2);
+  const int64_t max_tokens = std::min<int64_t>(S, block_table.size(1) * 64);
+  auto opts = scores.options().dtype(torch::kInt32);
+  auto indices = torch::empty({B, s_q, k}, opts);
+  auto counts = torch::empty({B, s_q}, opts);
+  auto rows = torch::empty({B, s_q, k}, opts);
+  check_launch(dsa_topk_rows_launch(scores.data_ptr<float>(), S, seq_lens.data_ptr<int>(),
+                                    static_cast<int>(B), static_cast<int>(s_q),
+                                    static_cast<int>(k), static_cast<int>(max_tokens),
+                                    causal ? 1 : 0, block_table.data_ptr<int>(),
+                                    static_cast<int>(block_table.size(1)),
+                                    static_cast<int>(num_blocks), indices.data_ptr<int>(),
+                                    counts.data_ptr<int>(), rows.data_ptr<int>(),
+                                    at::cuda::getCurrentCUDAStream()),
+               "dsa_topk_rows");
+  return {indices, counts, rows};
+}
+
 // kv_cache [num_blocks, 64, 1, 576] bf16, indices [B, s_q, k] int32 ->
 // pages [B * s_q * kpad / 64, 64, 1, 576] bf16, kpad = k rounded up to 64.
 torch::Tensor dsa_gather(torch::Tensor kv_cache, torch::Tensor block_table, torch::Tensor indices) {
@@ -669,6 +759,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "MLA decode over selected tokens, rows gathered by TMA (tcgen05)", py::arg("q"),
         py::arg("kv_cache"), py::arg("block_table"), py::arg("indices"), py::arg("counts"),
         py::arg("softmax_scale"), py::arg("num_splits"), py::arg("workspace"));
+  m.def("mla_decode_sparse_rows", &mla_decode_sparse_rows,
+        "MLA decode over selected cache rows resolved by dsa_topk_rows (tcgen05)", py::arg("q"),
+        py::arg("kv_cache"), py::arg("rows"), py::arg("counts"), py::arg("softmax_scale"),
+        py::arg("num_splits"), py::arg("workspace"));
   m.def("mla_workspace_bytes", &mla_workspace_bytes, "MLA split workspace bytes");
   m.def("mla_pick_splits", &mla_pick_splits, "MLA split count heuristic");
   m.def("mla_get_status", &mla_get_status, "MLA device status word", py::arg("clear") = false);
@@ -677,6 +771,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal"));
   m.def("dsa_topk", &dsa_topk, "DSA top-k token selection", py::arg("scores"),
         py::arg("seq_lens"), py::arg("k"), py::arg("causal"));
+  m.def("dsa_topk_rows", &dsa_topk_rows, "DSA top-k with the selected tokens' cache rows",
+        py::arg("scores"), py::arg("seq_lens"), py::arg("k"), py::arg("causal"),
+        py::arg("block_table"), py::arg("num_blocks"));
   m.def("dsa_gather", &dsa_gather, "DSA gather of the selected latent rows", py::arg("kv_cache"),
         py::arg("block_table"), py::arg("indices"));
   m.def("dsa_get_status", &dsa_get_status, "DSA device status word", py::arg("clear") = false);

@@ -28,8 +28,8 @@ _ws_cache = {}
 
 def workspace(device, nbytes):
     """Split-state workspace of at least nbytes, cached per device.  Kept
-    apart from binding.workspace, whose first bytes hold the GQA balanced
-    schedule's arrival counters (which must stay zero).  Every stream of the
+    apart from binding.workspace, so a GQA decode and an MLA decode never
+    overwrite each other's partial states.  Every stream of the
     device shares it: decodes that may run at the same time on different
     streams must not both come through this module (use the C ABI with a
     workspace each, or order the streams)."""

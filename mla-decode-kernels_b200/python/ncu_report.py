@@ -509,7 +509,7 @@ def block_kernels(captures):
     for stem, (header, secs) in sorted(captures.items()):
         for _, m in secs:
             key = (m["kernel"], stem)
-            if key in seen or not ("gqa_decode" in m["kernel"] or "mla_" in m["kernel"]):
+            if key in seen or not any(t in m["kernel"] for t in ("gqa_decode", "mla_", "dsa_")):
                 continue
             seen.add(key)
             rows.append(f"| `{m['kernel']}` | {stem} | {_g(m.get('duration_us'), '{:.2f}')} | "

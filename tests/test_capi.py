@@ -115,12 +115,15 @@ def test_plan_rep_shape(lib):
     assert p.stages == 3
     assert p.smem_bytes <= 227 * 1024
     assert p.grid == 148
-    # counters (32 rows x 8 warps) + m, l, acc for (148 + 32) slots x 32 heads
-    slots, qhr = 148 + 32, 32
-    counters = 65536 * 4  # fixed counter region shared by every shape
-    expect = (counters + plan_bytes(148, 32) + 2 * ((slots * qhr * 4 + 255) // 256 * 256) +
-              slots * qhr * 128 * 4)
-    assert p.workspace_bytes == expect
+    assert p.workspace_bytes == balanced_bytes(148, 32, rows=32, qhr=32)
+
+
+def balanced_bytes(grid, B, rows, qhr):
+    # plan + prefix, row records {first CTA, parts} per row, CTA records
+    # {row, parts} per CTA, then m, l, acc for (grid + rows) slots x qhr heads
+    slots = grid + rows
+    return (plan_bytes(grid, B) + align256(rows * 8) + align256(grid * 8) +
+            2 * align256(slots * qhr * 4) + slots * qhr * 128 * 4)
 
 
 @pytest.mark.parametrize("Hq,Hkv,hg,ncw", [(64, 8, 8, 8), (32, 8, 8, 8), (64, 4, 4, 8),
@@ -145,8 +148,7 @@ def test_plan_fixed_workspace_matches_reference_layout(lib):
     # [B, Hq, ns, 128] + [B, Hq, ns] x 2, fp32 (python/gqa_decode_ext.cpp:106-109)
     rc, p = plan(lib, 32, 32, 8, ns=8)
     states = 32 * 32 * 8
-    assert p.workspace_bytes == (65536 * 4 + states * 128 * 4 +
-                                 2 * ((states * 4 + 255) // 256 * 256))
+    assert p.workspace_bytes == states * 128 * 4 + 2 * align256(states * 4)
     assert p.grid == min(148, 32 * 8)
     rc, p = plan(lib, 32, 32, 8, ns=1)
     assert p.workspace_bytes == 0 and p.grid == 32
@@ -195,11 +197,9 @@ def test_mla_splits_and_workspace(lib):
     assert lib.mla_decode_workspace_bytes(0, 1, 128, 1) == 0
 
 
-def test_counter_region_grows_for_huge_batches(lib):
-    # (148 CTAs + 2 x 16384 rows) x 8 warps counters > the 65536 standard slots.
+def test_balanced_workspace_for_huge_batches_and_grid_cap(lib):
+    # the layout scales with rows; the grid is capped at 2048 CTAs
     rc, p = plan(lib, 16384, 32, 8)
-    slots, qhr = 148 + 16384, 32
-    counters = (148 + 2 * 16384) * 8
-    expect = ((counters * 4 + 255) // 256 * 256 + plan_bytes(148, 16384) +
-              2 * ((slots * qhr * 4 + 255) // 256 * 256) + slots * qhr * 128 * 4)
-    assert rc == 0 and p.workspace_bytes == expect
+    assert rc == 0 and p.workspace_bytes == balanced_bytes(148, 16384, rows=16384, qhr=32)
+    rc, p = plan(lib, 64, 32, 1, sms=148, per_sm=20)
+    assert rc == 0 and p.grid == 2048

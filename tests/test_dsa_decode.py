@@ -242,3 +242,46 @@ def test_fused_row_gather_splits_and_wide_heads(h_q, num_splits):
     assert torch.equal(fo, go)
     assert torch.equal(fl, gl)
     _check_attention(case, fo.float().cpu(), fl.cpu(), idx.cpu())
+
+
+@pytest.mark.parametrize("S,s_q,k,causal", [
+    ([5000, 100, 2048, 0], 1, 2048, False),
+    ([3000, 9, 700], 2, 512, True),
+])
+def test_topk_rows_resolve_the_page_table(S, s_q, k, causal):
+    # the top-k kernel's row output: the same selection as dsa_topk, and each
+    # selected token t of request b mapped to block_table[b, t // 64] * 64 +
+    # t % 64 (integer work: bit-exact), -1 where the selection is padded
+    case = cases.make_dsa_case(S, s_q, 16, n_idx_heads=64 // s_q, seed=25)
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, causal)
+    idx, counts = dsa_decode.dsa_topk(scores, sl, k, causal)
+    idx2, counts2, rows = dsa_decode.dsa_topk_rows(scores, sl, k, bt, kv.shape[0], causal)
+    _check_status()
+    assert torch.equal(idx, idx2) and torch.equal(counts, counts2)
+    tok = idx.long().cpu()
+    btc = bt.long().cpu()
+    expect = torch.full_like(tok, -1)
+    for b in range(tok.shape[0]):
+        sel = tok[b] >= 0
+        expect[b][sel] = btc[b][tok[b][sel] // 64] * 64 + tok[b][sel] % 64
+    assert torch.equal(rows.long().cpu(), expect)
+
+
+@pytest.mark.parametrize("h_q,num_splits", [(128, 0), (128, 3), (256, 2)])
+def test_sparse_decode_over_resolved_rows_equals_token_path(h_q, num_splits):
+    # the MLA kernel reading the rows resolved by top-k and the one resolving
+    # token -> block -> row itself copy the same rows into the same tiles:
+    # bit-identical outputs; the one-call sparse_decode takes the row path
+    case = cases.make_dsa_case([5000, 900, 70, 2048], 1, h_q, seed=26)
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, False)
+    idx, counts, rows = dsa_decode.dsa_topk_rows(scores, sl, 1024, bt, kv.shape[0], False)
+    ro, rl = dsa_decode.sparse_mla_decode_rows(q, kv, rows, counts, SCALE, num_splits)
+    to, tl = dsa_decode.sparse_mla_decode(q, kv, bt, idx, counts, SCALE, num_splits, fused=True)
+    so, sl2, sidx = dsa_decode.sparse_decode(q, kv, q_idx, w_idx, k_idx, bt, sl, 1024, SCALE,
+                                             num_splits=num_splits)
+    _check_status()
+    assert torch.equal(ro, to) and torch.equal(rl, tl)
+    assert torch.equal(so, ro) and torch.equal(sidx, idx)
+    _check_attention(case, ro.float().cpu(), rl.cpu(), idx.cpu())

@@ -315,11 +315,12 @@ def test_bounded_wait_times_out_with_status():
 
 
 def test_timed_out_decode_leaves_workspace_valid():
-    # A whole decode whose pipeline waits give up at once (limit 0 ns, so they
-    # time out while the copies are still on their way): status bit 0, the
-    # launch ends normally, and the next decode on the SAME workspace must be
-    # bit-identical to one on a fresh workspace - the warps that gave up still
-    # completed and re-armed every arrival counter of the rows they held.
+    # A whole decode whose copy warp issues nothing, so every pipeline wait
+    # of the tensor-core warps runs out (1 ms limit each, a stuck pipeline
+    # without a fault): status bit 0, the launch ends normally, and the next
+    # decode on the SAME workspace must be bit-identical to one on a fresh
+    # workspace - the warps that gave up still completed and re-armed every
+    # arrival counter of the rows they held.
     lib = capi.lib
     lib.gqa_decode_selftest_decode_timeout.argtypes = (
         [ctypes.c_void_p] * 6 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int,
@@ -332,14 +333,14 @@ def test_timed_out_decode_leaves_workspace_valid():
     B, Hq, Hkv, bs, mb = q.shape[0], q.shape[1], k.shape[2], k.shape[1], bt.shape[1]
     nbytes = lib.gqa_decode_workspace_bytes(B, Hq, Hkv, 0)
 
-    def launch(ws, wait_ns=None):
+    def launch(ws, wait_us=None):
         out = torch.full_like(q, float("nan"))
         ptrs = [ctypes.c_void_p(t.data_ptr()) for t in (q, k, v, bt, sl, out)]
-        if wait_ns is None:
+        if wait_us is None:
             rc = lib.gqa_decode_launch(*ptrs, B, Hq, Hkv, bs, mb, k.shape[0], SCALE, 0,
                                        ctypes.c_void_p(ws.data_ptr()), nbytes, capi.stream())
         else:
-            rc = lib.gqa_decode_selftest_decode_timeout(*ptrs, B, Hq, Hkv, bs, mb, SCALE, wait_ns,
+            rc = lib.gqa_decode_selftest_decode_timeout(*ptrs, B, Hq, Hkv, bs, mb, SCALE, wait_us,
                                                         ctypes.c_void_p(ws.data_ptr()), nbytes,
                                                         capi.stream())
         assert rc == 0
@@ -350,9 +351,13 @@ def test_timed_out_decode_leaves_workspace_valid():
     expect = launch(torch.zeros(nbytes, dtype=torch.uint8, device="cuda"))
     assert capi.status() == 0
     ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    import time
+
     for _ in range(2):
-        launch(ws, wait_ns=0)
-        assert capi.status() & 1, "the zero-limit waits did not time out"
+        t0 = time.perf_counter()
+        launch(ws, wait_us=1000)
+        assert time.perf_counter() - t0 < 2.0  # each warp gives up once, after 1 ms
+        assert capi.status() & 1, "the waits did not time out"
         again = launch(ws)
         assert capi.status() == 0
         assert torch.equal(again, expect)

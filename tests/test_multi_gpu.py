@@ -4,13 +4,16 @@
   contiguous page range of a single request; KVRangeDecoder (local state,
   NCCL all-gather, merge kernel) and P2PKVRangeDecoder (one kernel per rank,
   states exchanged with peer stores + flags over NVLink) must both match the
-  single-GPU decode of the whole request on every rank.
+  single-GPU decode of the whole request on every rank, with K x 1 and with
+  K x 8 (a peaked softmax, which stresses the merge).
 * Batch sharding: every rank decodes its LPT share of a ragged batch with
   the unsplit scan (v1), whose arithmetic for a request does not depend on
   the other requests in the launch; each output must equal, bitwise, the
   same request decoded inside the whole batch.
 
-Ranks run as spawned child processes with NVLS off (NCCL_NVLS_ENABLE=0).
+Every world size in {2, 4, 8} that the machine has GPUs for runs once, as
+spawned child processes (one per GPU) with NVLS off (NCCL_NVLS_ENABLE=0);
+each spawn runs every mode and every test reads its results.
 """
 
 import math
@@ -27,6 +30,8 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 SCALE = 1.0 / math.sqrt(128)
+WORLDS = [2, 4, 8]
+KV_MODES = [("kvrange", 1.0), ("kvrange", 8.0), ("kvrange_p2p", 1.0), ("kvrange_p2p", 8.0)]
 
 
 def _free_port():
@@ -35,7 +40,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, mode, k_scale, result_dir):
+def _worker(rank, world, port, result_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
     sys.path[:0] = [os.path.join(REPO, "mla-decode-kernels_b200", "python"),
@@ -49,8 +54,8 @@ def _worker(rank, world, port, mode, k_scale, result_dir):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     sharding.init_process_group("nccl", timeout_s=60)
-    if mode in ("kvrange", "kvrange_p2p"):
-        S, bs = 40000, 64
+    S, bs = 40000, 64
+    for mode, k_scale in KV_MODES:
         # same request on every rank (same seed), each keeps its own page range
         q, k, v, bt, sl = cases.make_case([S], 32, 8, bs, seed=50, pool_factor=1.0,
                                           k_scale=k_scale, device=dev)
@@ -67,53 +72,75 @@ def _worker(rank, world, port, mode, k_scale, result_dir):
             dec.close()
         full = binding.gqa_decode(q, k, v, bt, sl, SCALE)
         torch.cuda.synchronize()
-        np.save(os.path.join(result_dir, f"{mode}_{rank}.npy"),
+        np.save(os.path.join(result_dir, f"{mode}_k{k_scale:g}_{rank}.npy"),
                 np.stack([out.float().cpu().numpy(), full.float().cpu().numpy()]))
-    else:
-        sl_all = cases.config4_seq_lens(seed=1, B=24)
-        mine = sharding.lpt_shards(sl_all, world)[rank]
-        # the whole batch is built identically on every rank; each decodes its share
-        q, k, v, bt, sl = cases.make_case(sl_all, 32, 8, 16, seed=51, pool_factor=1.0 / 0.9,
-                                          device=dev)
-        idx = torch.tensor(mine, dtype=torch.long, device=dev)
-        out = binding.gqa_decode_v1(q[idx].contiguous(), k, v, bt[idx].contiguous(),
-                                    sl[idx].contiguous(), SCALE)
-        ref = binding.gqa_decode_v1(q, k, v, bt, sl, SCALE)[idx]
-        torch.cuda.synchronize()
-        np.save(os.path.join(result_dir, f"batch_{rank}.npy"),
-                np.stack([out.float().cpu().numpy(), ref.float().cpu().numpy()]))
-    assert binding.get_status(True) == 0
+        del q, k, v, bt, sl
+    sl_all = cases.config4_seq_lens(seed=1, B=24)
+    mine = sharding.lpt_shards(sl_all, world)[rank]
+    # the whole batch is built identically on every rank; each decodes its share
+    q, k, v, bt, sl = cases.make_case(sl_all, 32, 8, 16, seed=51, pool_factor=1.0 / 0.9,
+                                      device=dev)
+    idx = torch.tensor(mine, dtype=torch.long, device=dev)
+    out = binding.gqa_decode_v1(q[idx].contiguous(), k, v, bt[idx].contiguous(),
+                                sl[idx].contiguous(), SCALE)
+    ref = binding.gqa_decode_v1(q, k, v, bt, sl, SCALE)[idx]
+    torch.cuda.synchronize()
+    np.save(os.path.join(result_dir, f"batch_{rank}.npy"),
+            np.stack([out.float().cpu().numpy(), ref.float().cpu().numpy()]))
+    status = binding.get_status(True)
+    np.save(os.path.join(result_dir, f"status_{rank}.npy"), np.array([status]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def _spawn(world, mode, k_scale, tmp_path):
-    import torch.multiprocessing as mp
-
-    mp.start_processes(_worker, args=(world, _free_port(), mode, k_scale, str(tmp_path)),
-                       nprocs=world, join=True, start_method="spawn")
+_RUNS = {}
 
 
-def _world():
-    return min(4, torch.cuda.device_count())
+def _results(world, tmp_path_factory):
+    """Spawn `world` ranks once and return the directory of their results."""
+    if world not in _RUNS:
+        import torch.multiprocessing as mp
+
+        d = tmp_path_factory.mktemp(f"world{world}")
+        try:
+            mp.start_processes(_worker, args=(world, _free_port(), str(d)), nprocs=world,
+                               join=True, start_method="spawn")
+            _RUNS[world] = d
+        except Exception as e:  # one failed spawn fails every test of this world once
+            _RUNS[world] = RuntimeError(f"world {world} ranks failed: {e}")
+    if isinstance(_RUNS[world], Exception):
+        raise _RUNS[world]
+    return _RUNS[world]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("mode", ["kvrange", "kvrange_p2p"])
-@pytest.mark.parametrize("k_scale", [1.0, 8.0])
-def test_kv_range_sharding(tmp_path, mode, k_scale):
-    world = _world()
-    _spawn(world, mode, k_scale, tmp_path)
+def _need(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+@pytest.mark.parametrize("world", WORLDS)
+@pytest.mark.parametrize("mode,k_scale", KV_MODES)
+def test_kv_range_sharding(tmp_path_factory, world, mode, k_scale):
+    _need(world)
+    d = _results(world, tmp_path_factory)
     for r in range(world):
-        out, full = np.load(tmp_path / f"{mode}_{r}.npy")
+        out, full = np.load(d / f"{mode}_k{k_scale:g}_{r}.npy")
         assert np.isfinite(out).all()
         np.testing.assert_allclose(out, full, atol=1e-2, rtol=1e-2)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_batch_sharding_bitwise(tmp_path):
-    world = _world()
-    _spawn(world, "batch", 1.0, tmp_path)
+@pytest.mark.parametrize("world", WORLDS)
+def test_batch_sharding_bitwise(tmp_path_factory, world):
+    _need(world)
+    d = _results(world, tmp_path_factory)
     for r in range(world):
-        out, ref = np.load(tmp_path / f"batch_{r}.npy")
+        out, ref = np.load(d / f"batch_{r}.npy")
         assert np.array_equal(out, ref)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_no_device_status_on_any_rank(tmp_path_factory, world):
+    _need(world)
+    d = _results(world, tmp_path_factory)
+    for r in range(world):
+        assert int(np.load(d / f"status_{r}.npy")[0]) == 0
