@@ -281,6 +281,13 @@ def sum_over_ranks(x, world, device):
     return float(t.item())
 
 
+# GPU cycles (~0.1 ms) of a spin kernel queued ahead of the start event, so
+# the host has queued the start event and the first steps before the GPU
+# reaches them: the timed region then holds the K steps back to back, not
+# the host's latency to issue the first launch after the synchronize.
+LEAD_CYCLES = 200_000
+
+
 def time_loop(step, K, world, stream, finish=None):
     """Mean ms per step over exactly K steps, CUDA events on `stream`,
     barrier + synchronize on both sides.  `finish` joins any side streams
@@ -289,6 +296,8 @@ def time_loop(step, K, world, stream, finish=None):
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(LEAD_CYCLES)
     start.record(stream)
     for _ in range(K):
         step()

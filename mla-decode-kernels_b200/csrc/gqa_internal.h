@@ -46,10 +46,10 @@ enum OutMode : int {
 // KV-range sharding over peer memory: every rank owns one exchange buffer
 // [flags: u32 [2][world][items] | states: f32 [2][world][items][kXItem]],
 // mapped into every other rank; [2] is the epoch parity, an item is one
-// 8-dim slice of one (request, q head): items = B * Hq * 16.
+// 32-dim chunk of one (request, q head): items = B * Hq * 4.
 constexpr int kMaxPeers = 8;
-constexpr int kXItem = 12;       // floats per item state: m, l, 2 pad, acc[8] (16-byte aligned)
-constexpr int kXSlices = 16;     // items per (request, q head)
+constexpr int kXItem = 36;       // floats per item state: m, l, 2 pad, acc[32] (16-byte aligned)
+constexpr int kXSlices = 4;      // items per (request, q head)
 constexpr int kMaxScanGrid = 2048;  // BALANCED grid cap (the merge kernel's per-CTA list)
 
 // Shape-only launch plan (no device state): how heads map to warps and how

@@ -36,9 +36,12 @@ namespace gqa {
 
 namespace merge_detail {
 
-constexpr int kSlices = kHeadDim / 8;   // 8-dim slices of a head
-constexpr int kFewParts = 16;           // up to this many parts: one warp per head
-constexpr int kPerLane = 5;             // parts a lane loads per batch (many-part rows)
+constexpr int kThreads = 256;           // 8 warps per CTA
+constexpr int kWarps = kThreads / 32;
+constexpr int kChunk = 32;              // dims of a chunk item (lane = dim)
+constexpr int kChunks = kHeadDim / kChunk;
+constexpr int kFewParts = 16;           // up to this many parts: one warp per q head
+constexpr int kBatch = 24;              // parts a warp loads per batch (chunk items)
 
 __device__ __forceinline__ float warp_max(float v) {
   #pragma unroll
@@ -59,67 +62,10 @@ __device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d)
   return v;
 }
 
-// One slice item's merged state, identical on every lane.
-struct SliceState {
-  float m, l;
-  float a[8];
-};
-
-// Merge n parts (slots base, base + 1, ...) of q head j (of QHR per row),
-// dims [8 s, 8 s + 8), lanes over parts.  n = 0 gives the neutral state.
-__device__ __forceinline__ SliceState merge_slice(const CutMergeParams& p, long long base, int n,
-                                                  int j, int s, int lane) {
-  float Ml = -INFINITY, Ll = 0.f;
-  float a[8];
-  #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = 0.f;
-  for (int k0 = 0; k0 < n; k0 += 32 * kPerLane) {
-    float m[kPerLane], l[kPerLane];
-    float4 x0[kPerLane], x1[kPerLane];
-    #pragma unroll
-    for (int t = 0; t < kPerLane; ++t) {
-      const int k = k0 + lane + 32 * t;
-      const size_t st = static_cast<size_t>(base + min(k, n - 1)) * p.QHR + j;  // valid address
-      const float4* src = reinterpret_cast<const float4*>(p.part_acc + st * kHeadDim + 8 * s);
-      m[t] = k < n ? __ldcg(p.part_m + st) : -INFINITY;
-      l[t] = k < n ? __ldcg(p.part_l + st) : 0.f;
-      x0[t] = k < n ? __ldcg(src) : make_float4(0.f, 0.f, 0.f, 0.f);
-      x1[t] = k < n ? __ldcg(src + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    float mb = Ml;
-    #pragma unroll
-    for (int t = 0; t < kPerLane; ++t) mb = fmaxf(mb, m[t]);
-    if (mb == -INFINITY) continue;  // nothing on this lane yet
-    const float sc = Ml == -INFINITY ? 0.f : exp2f(Ml - mb);
-    Ll *= sc;
-    #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] *= sc;
-    #pragma unroll
-    for (int t = 0; t < kPerLane; ++t) {
-      const float w = m[t] == -INFINITY ? 0.f : exp2f(m[t] - mb);
-      Ll += l[t] * w;
-      a[0] += x0[t].x * w;
-      a[1] += x0[t].y * w;
-      a[2] += x0[t].z * w;
-      a[3] += x0[t].w * w;
-      a[4] += x1[t].x * w;
-      a[5] += x1[t].y * w;
-      a[6] += x1[t].z * w;
-      a[7] += x1[t].w * w;
-    }
-    Ml = mb;
-  }
-  SliceState r;
-  r.m = warp_max(Ml);
-  const float f = (Ml == -INFINITY) ? 0.f : exp2f(Ml - r.m);
-  r.l = warp_sum(Ll * f);
-  #pragma unroll
-  for (int i = 0; i < 8; ++i) r.a[i] = warp_sum(a[i] * f);
-  return r;
-}
-
-// Merge n <= kFewParts parts of q head j, lane = output dims 4 lane .. 4 lane + 3;
-// writes the bf16 output or the unnormalised state of head bh.
+// Merge n <= kFewParts parts (slots base, base + 1, ...) of q head j (of QHR
+// per row) in one warp, lane = output dims 4 lane .. 4 lane + 3, every load
+// in flight at once; writes the bf16 output or the unnormalised state of
+// head bh.
 __device__ __forceinline__ void merge_head(const CutMergeParams& p, long long base, int n, int j,
                                            size_t bh, int lane) {
   const size_t sl = static_cast<size_t>(base + min(lane, n - 1)) * p.QHR + j;
@@ -156,8 +102,77 @@ __device__ __forceinline__ void merge_head(const CutMergeParams& p, long long ba
   }
 }
 
+// Shared memory of the CTA-wide chunk merge: each warp's (m, l) and acc.
+struct ChunkSmem {
+  float m[kWarps], l[kWarps];
+  float a[kWarps][kChunk];
+};
+
+// Merge n parts of q head j, dims [32 c, 32 c + 32), with the whole CTA:
+// warp w takes parts [w n / 8, (w + 1) n / 8), lane = one dim, so each
+// part's 32 dims are one coalesced 128-byte load and its (m, l) a broadcast
+// load; up to kBatch parts per warp are in flight at once, merged online in
+// registers, and the warps' states are combined through shared memory.  The
+// result (m, l, acc of lane's dim) is valid in warp 0; n = 0 gives the
+// neutral state.  Every thread of the CTA must call it.
+__device__ __forceinline__ void merge_chunk(const CutMergeParams& p, long long base, int n, int j,
+                                            int c, ChunkSmem& cs, float& Mo, float& Lo,
+                                            float& Ao) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int k0 = static_cast<int>(static_cast<long long>(warp) * n / kWarps);
+  const int k1 = static_cast<int>(static_cast<long long>(warp + 1) * n / kWarps);
+  float M = -INFINITY, L = 0.f, A = 0.f;
+  for (int b0 = k0; b0 < k1; b0 += kBatch) {
+    float m[kBatch], l[kBatch], x[kBatch];
+    #pragma unroll
+    for (int t = 0; t < kBatch; ++t) {
+      const int k = b0 + t;
+      const size_t st = static_cast<size_t>(base + min(k, k1 - 1)) * p.QHR + j;  // valid address
+      m[t] = k < k1 ? __ldcg(p.part_m + st) : -INFINITY;
+      l[t] = k < k1 ? __ldcg(p.part_l + st) : 0.f;
+      x[t] = k < k1 ? __ldcg(p.part_acc + st * kHeadDim + kChunk * c + lane) : 0.f;
+    }
+    float mb = M;
+    #pragma unroll
+    for (int t = 0; t < kBatch; ++t) mb = fmaxf(mb, m[t]);
+    if (mb == -INFINITY) continue;  // warp-uniform: every lane read the same m
+    const float sc = M == -INFINITY ? 0.f : exp2f(M - mb);
+    L *= sc;
+    A *= sc;
+    #pragma unroll
+    for (int t = 0; t < kBatch; ++t) {
+      const float w = m[t] == -INFINITY ? 0.f : exp2f(m[t] - mb);
+      L += l[t] * w;
+      A += x[t] * w;
+    }
+    M = mb;
+  }
+  if (lane == 0) {
+    cs.m[warp] = M;
+    cs.l[warp] = L;
+  }
+  cs.a[warp][lane] = A;
+  __syncthreads();
+  if (warp == 0) {
+    float Mc = -INFINITY;
+    #pragma unroll
+    for (int w = 0; w < kWarps; ++w) Mc = fmaxf(Mc, cs.m[w]);
+    float Lc = 0.f, Ac = 0.f;
+    #pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = cs.m[w] == -INFINITY ? 0.f : exp2f(cs.m[w] - Mc);
+      Lc += cs.l[w] * f;
+      Ac += cs.a[w][lane] * f;
+    }
+    Mo = Mc;
+    Lo = Lc;
+    Ao = Ac;
+  }
+  __syncthreads();  // cs is reused by the next item
+}
+
 // Exchange buffer: [flags u32 [2][world][items] | states f32 [2][world][items][kXItem]],
-// item = (b * Hq + q head) * kSlices + slice; a state is {m, l, -, -, acc[8]}.
+// item = (b * Hq + q head) * kXSlices + chunk; a state is {m, l, -, -, acc[32]}.
 __device__ __forceinline__ unsigned* xflag(const CutMergeParams& p, int owner, int src,
                                            size_t item) {
   return reinterpret_cast<unsigned*>(p.xpeer[owner]) +
@@ -169,15 +184,14 @@ __device__ __forceinline__ float* xstate(const CutMergeParams& p, int owner, int
          (static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * p.xitems + item) * kXItem;
 }
 
-// Send this rank's state of `item` to every rank, wait for every rank's,
-// merge and write out's 8 dims.  Lane o handles rank o.
-__device__ __forceinline__ void exchange_item(const CutMergeParams& p, const SliceState& st,
-                                              size_t item, size_t bh, int s, int lane) {
-  if (lane < p.xworld) {
-    float* d = xstate(p, lane, p.xrank, item);
-    *reinterpret_cast<float4*>(d) = make_float4(st.m, st.l, 0.f, 0.f);
-    reinterpret_cast<float4*>(d)[1] = make_float4(st.a[0], st.a[1], st.a[2], st.a[3]);
-    reinterpret_cast<float4*>(d)[2] = make_float4(st.a[4], st.a[5], st.a[6], st.a[7]);
+// Warp 0: send this rank's state of `item` (lane = one of its 32 dims) to
+// every rank, wait for every rank's, merge and write out's 32 dims.
+__device__ __forceinline__ void exchange_chunk(const CutMergeParams& p, float M, float L, float A,
+                                               size_t item, size_t bh, int c, int lane) {
+  for (int o = 0; o < p.xworld; ++o) {
+    float* d = xstate(p, o, p.xrank, item);
+    if (lane == 0) *reinterpret_cast<float4*>(d) = make_float4(M, L, 0.f, 0.f);
+    d[4 + lane] = A;
   }
   __threadfence_system();
   __syncwarp();
@@ -195,84 +209,63 @@ __device__ __forceinline__ void exchange_item(const CutMergeParams& p, const Sli
     if (lane == 0) raise_status(kStatusPeerTimeout);
     return;
   }
-  float4 h = make_float4(-INFINITY, 0.f, 0.f, 0.f), a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
-  if (lane < p.xworld) {
-    const float4* d = reinterpret_cast<const float4*>(xstate(p, p.xrank, lane, item));
-    h = __ldcg(d);
-    a0 = __ldcg(d + 1);
-    a1 = __ldcg(d + 2);
-  }
-  const float M = warp_max(h.x);
-  const float w = (lane < p.xworld && h.x != -INFINITY) ? exp2f(h.x - M) : 0.f;
-  const float L = warp_sum(h.y * w);
-  float a[8] = {a0.x * w, a0.y * w, a0.z * w, a0.w * w, a1.x * w, a1.y * w, a1.z * w, a1.w * w};
+  float m[kMaxPeers], l[kMaxPeers], a[kMaxPeers];
   #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = warp_sum(a[i]);
-  if (lane == 0) {
-    __nv_bfloat16* o = p.out + bh * kHeadDim + 8 * s;
-    uint4 v;
-    if (M == -INFINITY) {  // no tokens on any rank: 0, as python/reference.py gives
-      v = make_uint4(0u, 0u, 0u, 0u);
-    } else {
-      const uint2 lo = pack_bf16x4(a[0] / L, a[1] / L, a[2] / L, a[3] / L);
-      const uint2 hi = pack_bf16x4(a[4] / L, a[5] / L, a[6] / L, a[7] / L);
-      v = make_uint4(lo.x, lo.y, hi.x, hi.y);
-    }
-    *reinterpret_cast<uint4*>(o) = v;
+  for (int o = 0; o < kMaxPeers; ++o) {
+    const float* d = xstate(p, p.xrank, min(o, p.xworld - 1), item);
+    m[o] = o < p.xworld ? __ldcg(d) : -INFINITY;
+    l[o] = o < p.xworld ? __ldcg(d + 1) : 0.f;
+    a[o] = o < p.xworld ? __ldcg(d + 4 + lane) : 0.f;
   }
-}
-
-// Bf16 output or unnormalised state of one slice item.
-__device__ __forceinline__ void write_slice(const CutMergeParams& p, const SliceState& st,
-                                            size_t bh, int s, int lane) {
-  if (lane != 0) return;
-  if (p.out_mode == kOutState) {
-    if (s == 0) {
-      p.res_m[bh] = st.m;
-      p.res_l[bh] = st.l;
-    }
-    float4* d = reinterpret_cast<float4*>(p.res_acc + bh * kHeadDim + 8 * s);
-    d[0] = make_float4(st.a[0], st.a[1], st.a[2], st.a[3]);
-    d[1] = make_float4(st.a[4], st.a[5], st.a[6], st.a[7]);
-  } else {
-    const uint2 lo = pack_bf16x4(st.a[0] / st.l, st.a[1] / st.l, st.a[2] / st.l, st.a[3] / st.l);
-    const uint2 hi = pack_bf16x4(st.a[4] / st.l, st.a[5] / st.l, st.a[6] / st.l, st.a[7] / st.l);
-    *reinterpret_cast<uint4*>(p.out + bh * kHeadDim + 8 * s) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+  float Mx = -INFINITY;
+  #pragma unroll
+  for (int o = 0; o < kMaxPeers; ++o) Mx = fmaxf(Mx, m[o]);
+  float Lx = 0.f, Ax = 0.f;
+  #pragma unroll
+  for (int o = 0; o < kMaxPeers; ++o) {
+    const float w = m[o] == -INFINITY ? 0.f : exp2f(m[o] - Mx);
+    Lx += l[o] * w;
+    Ax += a[o] * w;
   }
+  // no tokens on any rank: 0, as python/reference.py gives
+  p.out[bh * kHeadDim + kChunk * c + lane] =
+      __float2bfloat16(Mx == -INFINITY ? 0.f : Ax / Lx);
 }
 
 }  // namespace merge_detail
 
 // Every CTA first compacts, in shared memory, the list of cut rows from the
 // scan's per-CTA records (CTA c ends at most one cut row: only its first
-// segment can be a row's last part) with each row's number of work items -
-// QHR (one per q head) for rows of at most kFewParts parts, else QHR x
-// kSlices - and their prefix; then all warps of the grid stride over the
-// items.  With kOutExchange every row, cut or not, is an item set of QHR x
-// kSlices (the same on every rank) read from the per-row records; a warp
-// handles the same items on every rank (the grid is the same), always
-// sending an item before waiting for it.
-__global__ void __launch_bounds__(128, 4) gqa_decode_cut_merge_kernel(const __grid_constant__ CutMergeParams p) {
+// segment can be a row's last part) with each row's number of work units -
+// ceil(QHR / 8) units of 8 q heads (one warp each) for rows of at most
+// kFewParts parts, else QHR x 4 units of one (q head, 32-dim chunk) merged by
+// the whole CTA - and their prefix; then the CTAs stride over the units.
+// With kOutExchange every row, cut or not, is QHR x 4 chunk units (the same
+// on every rank) read from the per-row records; a CTA handles the same units
+// on every rank (the grid is the same), always sending a unit before waiting
+// for it.
+__global__ void __launch_bounds__(merge_detail::kThreads, 2)
+    gqa_decode_cut_merge_kernel(const __grid_constant__ CutMergeParams p) {
   using namespace merge_detail;
-  extern __shared__ int sh[];  // [grid] rows | [grid] parts | [grid + 1] item prefix
-  __shared__ int sh_warp[4];
+  extern __shared__ int sh[];  // [grid] rows | [grid] parts | [grid + 1] unit prefix
+  __shared__ ChunkSmem cs;
+  __shared__ int sh_warp[kWarps];
   // Everything below reads what the scan wrote.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  const long long gw = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp;
 
   if (p.out_mode == kOutExchange) {
-    const long long heads = static_cast<long long>(p.rows) * p.QHR;
-    for (long long f = gw; f < heads * kSlices; f += warps) {
-      const int s = static_cast<int>(f / heads);
-      const long long rh = f - s * heads;  // = b * Hq + q head
+    const long long units = static_cast<long long>(p.rows) * p.QHR * kChunks;
+    for (long long u = blockIdx.x; u < units; u += gridDim.x) {
+      const long long rh = u / kChunks;  // = b * Hq + q head
+      const int c = static_cast<int>(u - rh * kChunks);
       const int r = static_cast<int>(rh / p.QHR);
       const int j = static_cast<int>(rh - static_cast<long long>(r) * p.QHR);
       const int2 ri = p.row_info[r];  // {first CTA, parts}
-      const SliceState st = merge_slice(p, static_cast<long long>(ri.x) + r, ri.y, j, s, lane);
-      exchange_item(p, st, static_cast<size_t>(rh) * kSlices + s, static_cast<size_t>(rh), s,
-                    lane);
+      float M = 0.f, L = 0.f, A = 0.f;
+      merge_chunk(p, static_cast<long long>(ri.x) + r, ri.y, j, c, cs, M, L, A);
+      if (warp == 0) exchange_chunk(p, M, L, A, static_cast<size_t>(u),
+                                    static_cast<size_t>(rh), c, lane);
     }
     return;
   }
@@ -280,17 +273,18 @@ __global__ void __launch_bounds__(128, 4) gqa_decode_cut_merge_kernel(const __gr
   int* s_row = sh;
   int* s_n = sh + p.grid;
   int* s_pre = sh + 2 * p.grid;
-  // chunk of the scan's CTAs per thread, local item sum, block scan
+  const int few_units = (p.QHR + kWarps - 1) / kWarps;
+  // chunk of the scan's CTAs per thread, local unit sum, block scan
   const int per = (p.grid + blockDim.x - 1) / blockDim.x;
   const int c0 = min(p.grid, static_cast<int>(threadIdx.x) * per);
   const int c1 = min(p.grid, c0 + per);
   int local = 0;
   for (int c = c0; c < c1; ++c) {
     const int2 e = p.ends[c];  // {row, parts} or {-1, 0}
-    const int w = e.x < 0 ? 0 : (e.y <= kFewParts ? p.QHR : p.QHR * kSlices);
+    const int w = e.x < 0 ? 0 : (e.y <= kFewParts ? few_units : p.QHR * kChunks);
     s_row[c] = e.x;
     s_n[c] = e.y;
-    s_pre[c] = w;  // item count for now
+    s_pre[c] = w;  // unit count for now
     local += w;
   }
   int x = local;
@@ -312,24 +306,35 @@ __global__ void __launch_bounds__(128, 4) gqa_decode_cut_merge_kernel(const __gr
   if (threadIdx.x == blockDim.x - 1) s_pre[p.grid] = run;
   __syncthreads();
   const int total = s_pre[p.grid];
-  for (long long f = gw; f < total; f += warps) {
-    // the CTA record holding item f: largest c with s_pre[c] <= f
+  for (int u = blockIdx.x; u < total; u += gridDim.x) {
+    // the CTA record holding unit u: largest c with s_pre[c] <= u
     int lo = 0, hi = p.grid - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
-      if (s_pre[mid] <= f) lo = mid; else hi = mid - 1;
+      if (s_pre[mid] <= u) lo = mid; else hi = mid - 1;
     }
     const int r = s_row[lo], n = s_n[lo];
     const long long base = static_cast<long long>(lo) - n + 1 + r;  // slot of the first part
-    const int local_item = static_cast<int>(f - s_pre[lo]);
+    const int lu = u - s_pre[lo];
     if (n <= kFewParts) {
-      const int j = local_item;
-      merge_head(p, base, n, j, static_cast<size_t>(r) * p.QHR + j, lane);
+      const int j = lu * kWarps + warp;
+      if (j < p.QHR) merge_head(p, base, n, j, static_cast<size_t>(r) * p.QHR + j, lane);
     } else {
-      const int s = local_item / p.QHR;
-      const int j = local_item - s * p.QHR;
-      const SliceState st = merge_slice(p, base, n, j, s, lane);
-      write_slice(p, st, static_cast<size_t>(r) * p.QHR + j, s, lane);
+      const int j = lu / kChunks, c = lu - j * kChunks;
+      float M = 0.f, L = 0.f, A = 0.f;
+      merge_chunk(p, base, n, j, c, cs, M, L, A);
+      if (warp == 0) {
+        const size_t bh = static_cast<size_t>(r) * p.QHR + j;
+        if (p.out_mode == kOutState) {
+          if (c == 0 && lane == 0) {
+            p.res_m[bh] = M;
+            p.res_l[bh] = L;
+          }
+          p.res_acc[bh * kHeadDim + kChunk * c + lane] = A;
+        } else {
+          p.out[bh * kHeadDim + kChunk * c + lane] = __float2bfloat16(A / L);
+        }
+      }
     }
   }
 }
@@ -342,7 +347,7 @@ size_t cut_merge_smem_bytes(int grid) { return (3 * static_cast<size_t>(grid) + 
 cudaError_t launch_cut_merge(const CutMergeParams& p, int grid, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(merge_detail::kThreads);
   cfg.dynamicSmemBytes = p.out_mode == kOutExchange ? 0 : cut_merge_smem_bytes(p.grid);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
