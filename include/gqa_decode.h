@@ -205,11 +205,12 @@ size_t gqa_decode_kvshard_buffer_bytes(int B, int Hq, int Hkv, int world);
  * buffer (gqa_decode_kvshard_buffer_bytes, zeroed once before the first
  * call, 16-byte aligned) as mapped into this process (CUDA IPC;
  * peer_buffers[rank] is this rank's own buffer).  After the scan, the merge
- * kernel merges this rank's state of every (request, q head, 8-dim slice),
- * stores it into every rank's buffer with plain peer stores, publishes it
- * with a system-scope release flag, waits (bounded, 4 s; on timeout status
- * bit 2, value 4, and that slice of out is left unwritten) for every rank's
- * state of the slice and merges them into out, identical on all ranks.
+ * kernel merges this rank's state of every (request, q head, 32-dim chunk),
+ * stores it into every rank's buffer with plain peer stores as 64-bit words
+ * tagged with the epoch (no fence, no separate flag), waits (bounded, 4 s;
+ * on timeout status bit 2, value 4, and that chunk of out is left unwritten)
+ * until every rank's words of the chunk carry the epoch, and merges them
+ * into out, identical on all ranks.
  * epoch: non-zero, the same on every rank for one decode, +1 per decode
  * (states are double-buffered by its parity).  Each rank must run on its own
  * GPU, and all ranks' GPUs must have the same number of SMs (their merge

@@ -267,13 +267,8 @@ size_t exchange_items(int B, int Hq) {
   return static_cast<size_t>(B) * Hq * gqa::kXSlices;
 }
 
-size_t exchange_flag_bytes(int B, int Hq, int world) {
-  return align_up(2ull * world * exchange_items(B, Hq) * sizeof(unsigned));
-}
-
 size_t exchange_bytes(int B, int Hq, int world) {
-  return exchange_flag_bytes(B, Hq, world) +
-         2ull * world * exchange_items(B, Hq) * gqa::kXItem * sizeof(float);
+  return 2ull * world * exchange_items(B, Hq) * gqa::kXItem * sizeof(unsigned long long);
 }
 
 // Scan + cut-row merge of the BALANCED schedule.  `p` carries the inputs,
@@ -296,7 +291,6 @@ cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsig
     mp.xrank = xchg->rank;
     mp.xepoch = xchg->epoch;
     mp.xitems = static_cast<long long>(exchange_items(p.B, p.Hq));
-    mp.xflag_bytes = static_cast<long long>(exchange_flag_bytes(p.B, p.Hq, xchg->world));
   }
   p.row_info = reinterpret_cast<int2*>(w + lay.rowinfo);
   p.ends = reinterpret_cast<int2*>(w + lay.ends);

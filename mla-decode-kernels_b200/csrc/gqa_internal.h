@@ -43,12 +43,13 @@ enum OutMode : int {
   kOutExchange = 2,  // state pushed to every rank's exchange buffer, merged in-kernel
 };
 
-// KV-range sharding over peer memory: every rank owns one exchange buffer
-// [flags: u32 [2][world][items] | states: f32 [2][world][items][kXItem]],
-// mapped into every other rank; [2] is the epoch parity, an item is one
-// 32-dim chunk of one (request, q head): items = B * Hq * 4.
+// KV-range sharding over peer memory: every rank owns one exchange buffer of
+// u64 words [2][world][items][kXItem], mapped into every other rank; [2] is
+// the epoch parity, an item is one 32-dim chunk of one (request, q head):
+// items = B * Hq * 4, each {m, l, acc[32], 2 pad} with the epoch in every
+// word's upper half.
 constexpr int kMaxPeers = 8;
-constexpr int kXItem = 36;       // floats per item state: m, l, 2 pad, acc[32] (16-byte aligned)
+constexpr int kXItem = 36;       // u64 words per item state
 constexpr int kXSlices = 4;      // items per (request, q head)
 constexpr int kMaxScanGrid = 2048;  // BALANCED grid cap (the merge kernel's per-CTA list)
 
@@ -146,8 +147,7 @@ struct CutMergeParams {
   // kOutExchange
   int xworld, xrank;
   unsigned xepoch;               // != 0, identical on every rank for one decode
-  long long xitems;              // B * Hq * kXSlices flags per (parity, source rank)
-  long long xflag_bytes;         // byte offset of the state area in a buffer
+  long long xitems;              // B * Hq * kXSlices items per (parity, source rank)
   unsigned char* xpeer[kMaxPeers];  // exchange buffer of every rank ([xrank] = own)
 };
 

@@ -12,21 +12,23 @@
 // The work is spread over every SM in items of one L2 round trip each:
 //   * a row cut into at most 16 parts: one warp per (row, q head), lane = 4
 //     output dims, the parts' (m, l) and acc rows all loaded at once;
-//   * a row cut into more parts (one long request over every SM): one warp
-//     per (row, q head, 8-dim slice), lane = parts lane, lane + 32, ...,
-//     each lane merging its parts online, then one warp reduction.
+//   * a row cut into more parts (one long request over every SM): one CTA
+//     per (row, q head, 32-dim chunk), its 8 warps taking an eighth of the
+//     parts each (lane = one dim: coalesced 128-byte loads), combined
+//     through shared memory.
 // Merge identity (kernels/gqa_decode/v2_splitkv.cu:97-107 of the reference),
 // in log2 units: M = max m_i, w_i = 2^(m_i - M), out = sum w_i acc_i /
 // sum w_i l_i.  Parts are combined in a fixed order, so results are
 // deterministic.
 //
 // KV-range sharding over peer memory (kOutExchange): every row, cut or not,
-// is merged here per (row, q head, 8-dim slice) - the same items on every
+// is merged here per (row, q head, 32-dim chunk) - the same items on every
 // rank - and each item's local state is stored with plain peer stores into
-// slot `rank` of every rank's exchange buffer, published with a system-scope
-// release flag per item, and merged with the other ranks' states once their
-// flags arrive (bounded wait).  Buffers are double-buffered by epoch parity:
-// a rank can only run one decode ahead of a peer.
+// slot `rank` of every rank's exchange buffer as 64-bit words tagged with
+// the decode's epoch, then merged with the other ranks' states once every
+// word it needs carries the epoch (bounded wait).  Buffers are
+// double-buffered by epoch parity: a rank can only run one decode ahead of a
+// peer.
 //
 // Included once, at the end of gqa_scan.cu, so that it shares that
 // translation unit's device status word and helpers (raise_status, kFull).
@@ -171,51 +173,62 @@ __device__ __forceinline__ void merge_chunk(const CutMergeParams& p, long long b
   __syncthreads();  // cs is reused by the next item
 }
 
-// Exchange buffer: [flags u32 [2][world][items] | states f32 [2][world][items][kXItem]],
-// item = (b * Hq + q head) * kXSlices + chunk; a state is {m, l, -, -, acc[32]}.
-__device__ __forceinline__ unsigned* xflag(const CutMergeParams& p, int owner, int src,
-                                           size_t item) {
-  return reinterpret_cast<unsigned*>(p.xpeer[owner]) +
-         (static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * p.xitems + item);
-}
-
-__device__ __forceinline__ float* xstate(const CutMergeParams& p, int owner, int src, size_t item) {
-  return reinterpret_cast<float*>(p.xpeer[owner] + p.xflag_bytes) +
+// Exchange buffer: u64 words [2][world][items][kXItem], [2] the epoch
+// parity, item = (b * Hq + q head) * kXSlices + chunk; an item's words are
+// {m, l, acc[32], -, -}, each the float's bits in the low half and the
+// decode's epoch in the high half.
+__device__ __forceinline__ unsigned long long* xitem(const CutMergeParams& p, int owner, int src,
+                                                     size_t item) {
+  return reinterpret_cast<unsigned long long*>(p.xpeer[owner]) +
          (static_cast<size_t>((p.xepoch & 1) * p.xworld + src) * p.xitems + item) * kXItem;
 }
 
+__device__ __forceinline__ unsigned long long tag_word(unsigned epoch, float v) {
+  return (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+}
+
 // Warp 0: send this rank's state of `item` (lane = one of its 32 dims) to
-// every rank, wait for every rank's, merge and write out's 32 dims.
+// every rank, wait for every rank's, merge and write out's 32 dims.  Every
+// word carries the epoch, so each lane just polls the words it needs (its
+// dim's acc and the (m, l) of every rank) until all carry this decode's
+// epoch: no fence and no separate flag, one NVLink latency per exchange.
 __device__ __forceinline__ void exchange_chunk(const CutMergeParams& p, float M, float L, float A,
                                                size_t item, size_t bh, int c, int lane) {
   for (int o = 0; o < p.xworld; ++o) {
-    float* d = xstate(p, o, p.xrank, item);
-    if (lane == 0) *reinterpret_cast<float4*>(d) = make_float4(M, L, 0.f, 0.f);
-    d[4 + lane] = A;
+    unsigned long long* d = xitem(p, o, p.xrank, item);
+    st_relaxed_sys_u64(d + 2 + lane, tag_word(p.xepoch, A));
+    if (lane < 2) st_relaxed_sys_u64(d + lane, tag_word(p.xepoch, lane == 0 ? M : L));
   }
-  __threadfence_system();
-  __syncwarp();
-  if (lane < p.xworld) st_release_sys(xflag(p, lane, p.xrank, item), p.xepoch);
+  float m[kMaxPeers], l[kMaxPeers], a[kMaxPeers];
   bool ok = true;
-  if (lane < p.xworld) {
-    const unsigned* f = xflag(p, p.xrank, lane, item);
-    ok = ld_acquire_sys(f) == p.xepoch;
-    if (!ok) {
-      const unsigned long long t0 = global_timer_ns();
-      while (!ok && global_timer_ns() - t0 < kWaitLimitNs) ok = ld_acquire_sys(f) == p.xepoch;
+  const unsigned long long t0 = global_timer_ns();
+  #pragma unroll
+  for (int o = 0; o < kMaxPeers; ++o) {
+    m[o] = -INFINITY;
+    l[o] = 0.f;
+    a[o] = 0.f;
+    if (o >= p.xworld || !ok) continue;
+    const unsigned long long* d = xitem(p, p.xrank, o, item);
+    while (true) {
+      const unsigned long long wm = ld_relaxed_sys_u64(d);
+      const unsigned long long wl = ld_relaxed_sys_u64(d + 1);
+      const unsigned long long wa = ld_relaxed_sys_u64(d + 2 + lane);
+      if (static_cast<unsigned>(wm >> 32) == p.xepoch && static_cast<unsigned>(wl >> 32) == p.xepoch &&
+          static_cast<unsigned>(wa >> 32) == p.xepoch) {
+        m[o] = __uint_as_float(static_cast<unsigned>(wm));
+        l[o] = __uint_as_float(static_cast<unsigned>(wl));
+        a[o] = __uint_as_float(static_cast<unsigned>(wa));
+        break;
+      }
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        ok = false;
+        break;
+      }
     }
   }
   if (!__all_sync(kFull, ok)) {
     if (lane == 0) raise_status(kStatusPeerTimeout);
     return;
-  }
-  float m[kMaxPeers], l[kMaxPeers], a[kMaxPeers];
-  #pragma unroll
-  for (int o = 0; o < kMaxPeers; ++o) {
-    const float* d = xstate(p, p.xrank, min(o, p.xworld - 1), item);
-    m[o] = o < p.xworld ? __ldcg(d) : -INFINITY;
-    l[o] = o < p.xworld ? __ldcg(d + 1) : 0.f;
-    a[o] = o < p.xworld ? __ldcg(d + 4 + lane) : 0.f;
   }
   float Mx = -INFINITY;
   #pragma unroll

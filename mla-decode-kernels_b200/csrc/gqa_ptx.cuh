@@ -111,6 +111,19 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
+// 64-bit words tagged with an epoch in their upper half (the peer exchange):
+// an aligned 64-bit access is single-copy atomic, so a reader that sees the
+// tag also sees the value stored with it, without any fence.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ---- bulk copy (TMA, non-tensor) -----------------------------------------
 
 // L2 policy for data that is streamed exactly once (the KV pages).

@@ -9,12 +9,12 @@ identity, kernels/gqa_decode/v2_splitkv.cu:97-107, is what crosses GPUs):
 
 * KV-range sharding - one long request's pages are cut into contiguous
   ranges, one per rank.  Two exchanges of the per-rank softmax states:
-  - P2PKVRangeDecoder (default): one kernel per rank.  The warp that finishes
-    a request's state stores it straight into every rank's exchange buffer
-    (CUDA IPC mappings of one cudaMalloc per rank, plain peer stores over
-    NVLink), raises a release flag and merges all ranks' states once their
-    flags arrive (bounded wait), so the all-gather and the merge happen
-    inside the decode kernel.
+  - P2PKVRangeDecoder (default): the decode's own merge kernel stores each
+    rank's state straight into every rank's exchange buffer (CUDA IPC
+    mappings of one cudaMalloc per rank, plain peer stores over NVLink, every
+    64-bit word tagged with the decode's epoch) and merges all ranks' states
+    once their words carry the epoch (bounded wait), so the all-gather and
+    the merge happen inside the decode's kernels.
   - KVRangeDecoder: gqa_decode_partial, an NCCL all-gather of the packed
     states (Hq * 130 floats per request per rank: 16.6 KB at Hq = 32) and the
     merge kernel.  The collective-library baseline.
@@ -123,7 +123,8 @@ def _cuda_check(err, what):
 
 
 class P2PKVRangeDecoder:
-    """KV-range sharded decode with the cross-rank merge in the kernel.
+    """KV-range sharded decode with the cross-rank merge in the decode's
+    merge kernel.
 
     Every rank allocates one exchange buffer (kvshard_buffer_bytes for the
     batch shape) with cudaMalloc, exports it with CUDA IPC and maps every
