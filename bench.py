@@ -593,13 +593,15 @@ def run_ours(args, world, rank, local):
         if args.exchange == "p2p":
             dec = sharding.P2PKVRangeDecoder(q.shape[0], q.shape[1], k.shape[2], device)
             launches_per_step = 2  # scan + merge/exchange kernel
+
+            def step():
+                dec.decode(q, k, v, bt, sl, SCALE, out=out)
         else:
             dec = sharding.KVRangeDecoder()
-            launches_per_step = 3  # scan + cut-row merge (states), state merge after NCCL
+            launches_per_step = 4  # scan + cut-row merge (states), state merge after NCCL, copy
 
-        def step():
-            out.copy_(dec.decode(q, k, v, bt, sl, SCALE))
-        launches_per_step += 1  # the copy into the step's output buffer
+            def step():
+                out.copy_(dec.decode(q, k, v, bt, sl, SCALE))
 
     # correctness spot check before timing (bench/common.py:75-89): the first
     # two requests (or the whole shard) against the CPU oracle.
@@ -662,6 +664,9 @@ def run_ours(args, world, rank, local):
     elif kind == "batch":
         def decode(q_d, bt_d, sl_d, out_d):
             binding.gqa_decode(q_d, k, v, bt_d, sl_d, SCALE, num_splits=ns, out=out_d)
+    elif args.exchange == "p2p":
+        def decode(q_d, bt_d, sl_d, out_d):
+            dec.decode(q_d, k, v, bt_d, sl_d, SCALE, out=out_d)
     else:
         def decode(q_d, bt_d, sl_d, out_d):
             out_d.copy_(dec.decode(q_d, k, v, bt_d, sl_d, SCALE))

@@ -199,31 +199,46 @@ __device__ __forceinline__ void exchange_chunk(const CutMergeParams& p, float M,
     st_relaxed_sys_u64(d + 2 + lane, tag_word(p.xepoch, A));
     if (lane < 2) st_relaxed_sys_u64(d + lane, tag_word(p.xepoch, lane == 0 ? M : L));
   }
+  // Poll every rank's words at once (all loads of a round in flight), again
+  // for the ranks not yet arrived, until all carry this decode's epoch.
   float m[kMaxPeers], l[kMaxPeers], a[kMaxPeers];
+  unsigned pending = (1u << p.xworld) - 1u;
   bool ok = true;
   const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    unsigned long long wm[kMaxPeers], wl[kMaxPeers], wa[kMaxPeers];
+    #pragma unroll
+    for (int o = 0; o < kMaxPeers; ++o) {
+      if ((pending >> o) & 1u) {
+        const unsigned long long* d = xitem(p, p.xrank, o, item);
+        wm[o] = ld_relaxed_sys_u64(d);
+        wl[o] = ld_relaxed_sys_u64(d + 1);
+        wa[o] = ld_relaxed_sys_u64(d + 2 + lane);
+      }
+    }
+    #pragma unroll
+    for (int o = 0; o < kMaxPeers; ++o) {
+      if (((pending >> o) & 1u) && static_cast<unsigned>(wm[o] >> 32) == p.xepoch &&
+          static_cast<unsigned>(wl[o] >> 32) == p.xepoch &&
+          static_cast<unsigned>(wa[o] >> 32) == p.xepoch) {
+        m[o] = __uint_as_float(static_cast<unsigned>(wm[o]));
+        l[o] = __uint_as_float(static_cast<unsigned>(wl[o]));
+        a[o] = __uint_as_float(static_cast<unsigned>(wa[o]));
+        pending &= ~(1u << o);
+      }
+    }
+    if (pending == 0u) break;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      ok = false;
+      break;
+    }
+  }
   #pragma unroll
   for (int o = 0; o < kMaxPeers; ++o) {
-    m[o] = -INFINITY;
-    l[o] = 0.f;
-    a[o] = 0.f;
-    if (o >= p.xworld || !ok) continue;
-    const unsigned long long* d = xitem(p, p.xrank, o, item);
-    while (true) {
-      const unsigned long long wm = ld_relaxed_sys_u64(d);
-      const unsigned long long wl = ld_relaxed_sys_u64(d + 1);
-      const unsigned long long wa = ld_relaxed_sys_u64(d + 2 + lane);
-      if (static_cast<unsigned>(wm >> 32) == p.xepoch && static_cast<unsigned>(wl >> 32) == p.xepoch &&
-          static_cast<unsigned>(wa >> 32) == p.xepoch) {
-        m[o] = __uint_as_float(static_cast<unsigned>(wm));
-        l[o] = __uint_as_float(static_cast<unsigned>(wl));
-        a[o] = __uint_as_float(static_cast<unsigned>(wa));
-        break;
-      }
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        ok = false;
-        break;
-      }
+    if (o >= p.xworld) {
+      m[o] = -INFINITY;
+      l[o] = 0.f;
+      a[o] = 0.f;
     }
   }
   if (!__all_sync(kFull, ok)) {

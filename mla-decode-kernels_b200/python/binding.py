@@ -120,14 +120,15 @@ kvshard_buffer_bytes = _ext.kvshard_buffer_bytes
 
 
 def gqa_decode_kvshard(q, k_cache, v_cache, block_table, seq_lens, scale, rank, world,
-                       peer_ptrs, epoch, check_blocks=True):
+                       peer_ptrs, epoch, check_blocks=True, out=None):
     """KV-range sharded decode with the cross-rank merge fused into the
-    kernel (peer stores + flags over NVLink); see sharding.P2PKVRangeDecoder."""
+    decode's merge kernel (epoch-tagged peer stores over NVLink); see
+    sharding.P2PKVRangeDecoder.  out: optional [B, Hq, 128] bf16 to write."""
     nbytes = _ext.workspace_bytes(q.shape[0], q.shape[1], k_cache.shape[2], 0)
     ws = workspace(q.device, nbytes)
     return _ext.gqa_decode_kvshard(q, k_cache, v_cache, block_table, seq_lens, float(scale),
                                    int(rank), int(world), [int(x) for x in peer_ptrs], int(epoch),
-                                   ws, bool(check_blocks))
+                                   ws, bool(check_blocks), out)
 
 
 def block_table_to_paged(block_table, seq_lens, page_size):

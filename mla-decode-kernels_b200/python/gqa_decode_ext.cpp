@@ -209,7 +209,8 @@ std::vector<torch::Tensor> gqa_decode_partial(torch::Tensor q, torch::Tensor k_c
 torch::Tensor gqa_decode_kvshard(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                  torch::Tensor block_table, torch::Tensor seq_lens, double scale,
                                  int64_t rank, int64_t world, std::vector<int64_t> peer_ptrs,
-                                 int64_t epoch, torch::Tensor workspace, bool check_blocks) {
+                                 int64_t epoch, torch::Tensor workspace, bool check_blocks,
+                                 c10::optional<torch::Tensor> out_opt) {
   const GqaDims d = check_inputs(q, k_cache, v_cache, block_table, seq_lens);
   TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world,
               "rank/world must satisfy 0 <= rank < world <= 8");
@@ -220,7 +221,15 @@ torch::Tensor gqa_decode_kvshard(torch::Tensor q, torch::Tensor k_cache, torch::
   const c10::cuda::CUDAGuard guard(q.device());
   void* peers[8] = {nullptr};
   for (int64_t r = 0; r < world; ++r) peers[r] = reinterpret_cast<void*>(peer_ptrs[r]);
-  auto out = torch::empty_like(q);
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = *out_opt;
+    TORCH_CHECK(out.is_cuda() && out.device() == q.device() && out.scalar_type() == torch::kBFloat16 &&
+                    out.is_contiguous() && out.sizes() == q.sizes(),
+                "out must be a contiguous bf16 CUDA tensor shaped like q on q's device");
+  } else {
+    out = torch::empty_like(q);
+  }
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   const size_t ws_bytes = static_cast<size_t>(workspace.numel()) * workspace.element_size();
   check_launch(gqa_decode_kvshard_launch(
@@ -795,7 +804,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "KV-range sharded decode, cross-rank merge over peer memory", py::arg("q"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"), py::arg("seq_lens"),
         py::arg("scale"), py::arg("rank"), py::arg("world"), py::arg("peer_ptrs"),
-        py::arg("epoch"), py::arg("workspace"), py::arg("check_blocks") = true);
+        py::arg("epoch"), py::arg("workspace"), py::arg("check_blocks") = true,
+        py::arg("out") = py::none());
   m.def("kvshard_buffer_bytes", &kvshard_buffer_bytes, "exchange buffer bytes per rank");
   m.def("merge_states", &merge_states, "merge per-shard softmax states into bf16 output");
   m.def("block_table_to_csr", &block_table_to_csr, "dense page table -> CSR (GPU)");

@@ -180,11 +180,11 @@ class P2PKVRangeDecoder:
         self.peers = peers
         self.epoch = 0
 
-    def decode(self, q, k_local, v_local, block_table_local, seq_lens_local, scale):
+    def decode(self, q, k_local, v_local, block_table_local, seq_lens_local, scale, out=None):
         self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFFF else 1
         return self._binding.gqa_decode_kvshard(q, k_local, v_local, block_table_local,
                                                 seq_lens_local, scale, self.rank, self.world,
-                                                self.peers, self.epoch)
+                                                self.peers, self.epoch, out=out)
 
     def close(self):
         from cuda.bindings import runtime as rt
