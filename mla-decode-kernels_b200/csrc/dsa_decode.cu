@@ -22,6 +22,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "device_once.h"
 #include "dsa_decode.h"
 #include "gqa_ptx.cuh"
 #include "umma_ptx.cuh"
@@ -653,14 +654,13 @@ cudaError_t dsa_indexer_launch(const gqa_bf16* q_idx, const float* w_idx, const 
   if (!q_idx || !w_idx || !k_idx || !block_table || !seq_lens || !scores)
     return cudaErrorInvalidValue;
   if (!aligned16(q_idx) || !aligned16(k_idx)) return cudaErrorMisalignedAddress;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
+  static gqa::DeviceOnce attr_once;
+  const cudaError_t attr_err = attr_once.run([] {
     const cudaError_t e1 = cudaFuncSetAttribute(
         dsa_indexer_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, IdxGeom<64>::kSmem);
     const cudaError_t e2 = cudaFuncSetAttribute(
         dsa_indexer_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, IdxGeom<128>::kSmem);
-    attr_err = e1 != cudaSuccess ? e1 : e2;
+    return e1 != cudaSuccess ? e1 : e2;
   });
   if (attr_err != cudaSuccess) return attr_err;
   int dev = 0, sms = 148;
@@ -719,12 +719,10 @@ cudaError_t topk_impl(const float* scores, long long scores_stride, const int* s
   const unsigned grid = static_cast<unsigned>(B * s_q);
   if (max_tokens <= kTopkSmemKeys) {
     const int smem = max(max_tokens, 1) * 4;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-      attr_err = cudaFuncSetAttribute(dsa_topk_kernel<true>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      kTopkSmemKeys * 4);
+    static gqa::DeviceOnce attr_once;
+    const cudaError_t attr_err = attr_once.run([] {
+      return cudaFuncSetAttribute(dsa_topk_kernel<true>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkSmemKeys * 4);
     });
     if (attr_err != cudaSuccess) return attr_err;
     dsa_topk_kernel<true><<<grid, kTopkThreads, smem, stream>>>(p);

@@ -40,6 +40,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "device_once.h"
 #include "gqa_decode.h"
 #include "gqa_ptx.cuh"
 #include "mla_decode.h"
@@ -1996,9 +1997,8 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
     p.part_m = reinterpret_cast<float*>(w + acc);
     p.part_l = reinterpret_cast<float*>(w + acc + ml);
   }
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
+  static gqa::DeviceOnce attr_once;
+  const cudaError_t attr_err = attr_once.run([] {
     const cudaError_t e[4] = {
         cudaFuncSetAttribute(mla_decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Pair<16>::kSmem),
@@ -2009,7 +2009,8 @@ cudaError_t mla_launch_impl(const gqa_bf16* q, const gqa_bf16* kv_cache, const i
         cudaFuncSetAttribute(mla_decode_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Rows::kSmem)};
     for (cudaError_t x : e)
-      if (x != cudaSuccess) attr_err = x;
+      if (x != cudaSuccess) return x;
+    return cudaSuccess;
   });
   if (attr_err != cudaSuccess) return attr_err;
   if (L.NH == 128) {

@@ -27,7 +27,7 @@ EXT_PATH = os.path.join(BUILD_DIR, EXT_NAME + ".so")
 
 CU_SOURCES = ["gqa_scan.cu", "gqa_simt.cu", "gqa_api.cu", "gqa_cxx_abi.cu", "gqa_noalloc.cu",
               "mla_decode.cu", "dsa_decode.cu"]
-CU_HEADERS = ["gqa_internal.h", "gqa_ptx.cuh", "gqa_merge.cuh", "umma_ptx.cuh"]
+CU_HEADERS = ["gqa_internal.h", "gqa_ptx.cuh", "gqa_merge.cuh", "umma_ptx.cuh", "device_once.h"]
 PUBLIC_HEADERS = ["gqa_decode.h", "mla_decode.h", "dsa_decode.h"]
 
 NVCC_FLAGS = [
