@@ -285,3 +285,25 @@ def test_sparse_decode_over_resolved_rows_equals_token_path(h_q, num_splits):
     assert torch.equal(ro, to) and torch.equal(rl, tl)
     assert torch.equal(so, ro) and torch.equal(sidx, idx)
     _check_attention(case, ro.float().cpu(), rl.cpu(), idx.cpu())
+
+
+def test_every_device_of_one_process():
+    # kernel shared-memory limits are per device: a process that decodes on
+    # a second GPU gets the same bits as on the first
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs visible to one process")
+    case = cases.make_dsa_case([3000, 2048, 100], 1, 128, seed=16)
+    mcase = cases.make_mla_case([700, 64, 2049], 1, 64, seed=17)
+    got = []
+    for d in range(2):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            q, kv, q_idx, w_idx, k_idx, bt, sl = (t.to(dev) for t in case)
+            out, lse, idx = dsa_decode.sparse_decode(q, kv, q_idx, w_idx, k_idx, bt, sl, 2048,
+                                                     SCALE, False, 0)
+            mq, mkv, mbt, msl = (t.to(dev) for t in mcase)
+            mout, mlse = mla_decode.mla_decode(mq, mkv, mbt, msl, SCALE)
+            _check_status()
+            got.append([t.cpu() for t in (out, lse, idx, mout, mlse)])
+    for a, b in zip(*got):
+        assert torch.equal(a, b)
