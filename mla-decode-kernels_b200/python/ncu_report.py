@@ -293,10 +293,12 @@ _KEEP = {
            "dtype", "gpu_launches", "unavailable", "stages_us"),
     "config": ("workload", "api", "kernel", "num_splits", "exchange", "parallelism",
                "global_batch", "kv_bytes_per_step", "bytes_per_step", "per_step_sample_requests"),
-    "e2e": ("value", "unit", "ms_per_step", "h2d_bytes_per_step", "d2h_bytes_per_step"),
+    "e2e": ("value", "unit", "ms_per_step", "h2d_bytes_per_step", "d2h_bytes_per_step",
+            "serial_ms_per_step", "serial_value"),
     "roofline": ("bound", "achieved", "peak", "unit", "frac", "traffic", "kernel"),
     "clocks": ("sm_mhz", "sm_max_mhz", "reasons", "samples"),
     "cpu_baseline": ("value", "unit", "cores", "kind"),
+    "reference_py": ("value", "unit", "cores", "kind", "ms_per_full_step_extrapolated", "sample"),
 }
 
 
@@ -477,10 +479,17 @@ def block_bench(stem, note, lines):
         ci = commands.index(command) + 1
         c = d.get("config", {})
         if d.get("impl") == "reference":
-            rows.append(f"| {ci} | {c.get('workload')} | reference (CPU) | {d.get('n_gpus')} | "
-                        f"{d.get('ms_per_step')} | {d.get('median_us_per_step')} | "
-                        f"{d.get('value')} | | | | "
+            rows.append(f"| {ci} | {c.get('workload')} | reference (CPU, C port) | "
+                        f"{d.get('n_gpus')} | {d.get('ms_per_step')} | "
+                        f"{d.get('median_us_per_step')} | {d.get('value')} | | | | "
                         f"{(d.get('cpu_baseline') or {}).get('cores')} host threads |")
+            rp = d.get("reference_py")
+            if rp:
+                # the reference's own python/reference.py on a sample of the
+                # same step, extrapolated to the whole step
+                rows.append(f"| {ci} | {c.get('workload')} | reference.py (CPU, unmodified) | "
+                            f"{d.get('n_gpus')} | {rp.get('ms_per_full_step_extrapolated')} | | "
+                            f"{rp.get('value')} | | | | {rp.get('cores')} host threads |")
             continue
         kern = c.get("api", "block_table") if c.get("kernel", "auto") == "auto" else c.get("kernel")
         if c.get("kernel") == "v2":
