@@ -307,3 +307,31 @@ def test_every_device_of_one_process():
             got.append([t.cpu() for t in (out, lse, idx, mout, mlse)])
     for a, b in zip(*got):
         assert torch.equal(a, b)
+
+
+def test_rows_out_of_range_raise_status_and_read_block_zero():
+    # integer bounds checks of the row path: a block id outside the cache
+    # (top-k's resolve) and a row id outside it (the MLA copy warp) each set
+    # status bit 1 and read block / row 0 instead; nothing reads outside
+    case = cases.make_dsa_case([3000, 900], 1, 128, seed=27, poison=False)  # block 0 is finite
+    q, kv, q_idx, w_idx, k_idx, bt, sl = _cuda(case)
+    nb = kv.shape[0]
+    scores = dsa_decode.dsa_indexer(q_idx, w_idx, k_idx, bt, sl, False)
+    idx, counts, rows = dsa_decode.dsa_topk_rows(scores, sl, 512, bt, nb, False)
+    _check_status()
+    bad_bt = bt.clone()
+    bad_bt[1, 3] = nb + 5  # request 1, tokens 192..255
+    _, _, rows_bad = dsa_decode.dsa_topk_rows(scores, sl, 512, bad_bt, nb, False)
+    torch.cuda.synchronize()
+    assert dsa_decode.get_status(True) == 2
+    tok = idx[1].long()
+    hit = (tok >= 192) & (tok < 256)
+    assert hit.any()
+    assert torch.equal(rows_bad[1][hit].long(), tok[hit] % 64)
+    assert torch.equal(rows_bad[1][~hit], rows[1][~hit]) and torch.equal(rows_bad[0], rows[0])
+    bad_rows = rows.clone()
+    bad_rows[0, 0, 5] = nb * 64 + 7
+    out, _ = dsa_decode.sparse_mla_decode_rows(q, kv, bad_rows, counts, SCALE)
+    torch.cuda.synchronize()
+    assert mla_decode.get_status(True) == 2
+    assert torch.isfinite(out.float()).all()
