@@ -112,8 +112,8 @@ cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
 /* Decode with the split count chosen by the library (num_splits == 0) or
  * given (1..512, same semantics as gqa_decode_v2_launch).  num_splits == 0
  * selects the balanced schedule: one persistent CTA per SM, each streaming
- * an equal share of all requests' KV, with partial rows merged in the same
- * launch.  num_blocks > 0 makes the kernel check every block id against
+ * an equal share of all requests' KV, then the rows cut between CTAs
+ * merged by a second kernel (below).  num_blocks > 0 makes the kernel check every block id against
  * [0, num_blocks) (a bad id sets status bit 1, value 2, and reads block 0
  * instead).
  * The balanced schedule is two kernels on `stream`: the scan (one
@@ -243,7 +243,7 @@ cudaError_t gqa_decode_merge_states(const float* state_m, const float* state_l,
  * JNI binding with no device allocator to hand over a workspace.  No
  * counterpart in the reference (its extension allocates a workspace on every
  * call, python/gqa_decode_ext.cpp:106-109).
- * - The scratch (arrival counters and split states) is a file-scope
+ * - The scratch (the schedule, row records and split states) is a file-scope
  *   GQA_DECODE_NOALLOC_SCRATCH_BYTES (16 MiB) device array that every GPU
  *   loading this library holds until the process exits.  This call allocates
  *   nothing: no cudaMalloc, no cudaFree.
@@ -291,9 +291,9 @@ cudaError_t gqa_decode_selftest_wait_timeout(int limit_us, cudaStream_t stream);
  * wait of the tensor-core warps runs out, each after wait_limit_us
  * (1..1,000,000) instead of 4 s - a stuck pipeline without any fault.  Status
  * bit 0 is then set and out holds no result (NaN / garbage rows), but the
- * launch ends normally and every arrival counter in the workspace is back at
- * zero: the next gqa_decode_launch on the same workspace is correct.  No
- * reference counterpart. */
+ * launch ends normally and the warps that gave up still wrote empty states
+ * and row records for their segments, so the next gqa_decode_launch on the
+ * same workspace is correct.  No reference counterpart. */
 cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
                                                const gqa_bf16* v_cache, const int* block_table,
                                                const int* seq_lens, gqa_bf16* out, int B, int Hq,

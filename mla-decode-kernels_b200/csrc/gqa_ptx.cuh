@@ -89,15 +89,6 @@ __device__ __forceinline__ int ld_nc_s32(const int* p) {
   return v;
 }
 
-// Atomic add with acquire-release semantics at GPU scope; returns the old value.
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
-               : "=r"(old)
-               : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
 
 // ---- system-scope flags (peer ranks over NVLink) ----------------------------
 

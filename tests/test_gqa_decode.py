@@ -319,15 +319,16 @@ def test_timed_out_decode_leaves_workspace_valid():
     # of the tensor-core warps runs out (1 ms limit each, a stuck pipeline
     # without a fault): status bit 0, the launch ends normally, and the next
     # decode on the SAME workspace must be bit-identical to one on a fresh
-    # workspace - the warps that gave up still completed and re-armed every
-    # arrival counter of the rows they held.
+    # workspace - the warps that gave up still wrote empty states and row
+    # records for the segments they held, and nothing in the workspace needs
+    # clearing between launches.
     lib = capi.lib
     lib.gqa_decode_selftest_decode_timeout.argtypes = (
         [ctypes.c_void_p] * 6 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int,
                                                       ctypes.c_void_p, ctypes.c_size_t,
                                                       ctypes.c_void_p])
     lib.gqa_decode_selftest_decode_timeout.restype = ctypes.c_int
-    # one long request (rows cut into many parts, two merge levels) and
+    # one long request (rows cut into many parts, merged by whole CTAs) and
     # shorter ones (rows cut into a few parts or held whole)
     q, k, v, bt, sl = to_gpu(cases.make_case([60000, 9000, 700, 33], 32, 8, 16, seed=27))
     B, Hq, Hkv, bs, mb = q.shape[0], q.shape[1], k.shape[2], k.shape[1], bt.shape[1]

@@ -148,7 +148,7 @@ def test_one_plan_many_runs_and_graph_replay():
 
 def test_two_wrappers_keep_their_own_plans():
     # two batches planned up front, then run alternately: each wrapper's plan
-    # and counters live in its own workspace, so neither clobbers the other
+    # and partial states live in its own workspace, so neither clobbers the other
     a = to_gpu(cases.make_case([700, 5000, 64], 32, 8, 16, seed=61))
     b = to_gpu(cases.make_case([3000] * 9, 32, 8, 16, seed=62))
     wa, wb = binding.BatchDecodeWithPagedKVCacheWrapper(), binding.BatchDecodeWithPagedKVCacheWrapper()
