@@ -301,6 +301,24 @@ cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16
                                                float scale, int wait_limit_us, void* workspace,
                                                size_t workspace_bytes, cudaStream_t stream);
 
+/* Failure-detection self-test of the cross-rank exchange: the decode of
+ * gqa_decode_kvshard_launch as rank 0 of a world of two whose rank 1 never
+ * runs, on one GPU.  exchange_buffers holds both ranks' buffers
+ * (2 * gqa_decode_kvshard_buffer_bytes(B, Hq, Hkv, 2) bytes, 16-byte
+ * aligned; cleared here on `stream`).  Rank 0 sends its states into both
+ * and waits for rank 1's, which never arrive: every wait gives up after
+ * wait_limit_us (1..1,000,000) instead of 4 s, status bit 2 (value 4) is
+ * set, out holds no result, and the launch ends normally - what a rank sees
+ * when a peer died between decodes.  No reference counterpart. */
+cudaError_t gqa_decode_selftest_exchange_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                                 const gqa_bf16* v_cache, const int* block_table,
+                                                 const int* seq_lens, gqa_bf16* out, int B,
+                                                 int Hq, int Hkv, int block_size, int max_blocks,
+                                                 float scale, int wait_limit_us,
+                                                 void* exchange_buffers, size_t exchange_bytes,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 cudaStream_t stream);
+
 /* Library version string. */
 const char* gqa_decode_version(void);
 

@@ -314,6 +314,7 @@ cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsig
   mp.QHR = p.HG * p.G;
   mp.grid = grid;
   mp.out_mode = p.out_mode;
+  mp.wait_ns = p.wait_ns;
   return gqa::launch_cut_merge(mp, sms, stream);
 }
 
@@ -690,6 +691,33 @@ cudaError_t gqa_decode_selftest_decode_timeout(const gqa_bf16* q, const gqa_bf16
                       B, Hq, Hkv, block_size, max_blocks, 0, scale, workspace, workspace_bytes,
                       stream, nullptr, static_cast<unsigned long long>(wait_limit_us) * 1000ull,
                       1);
+}
+
+cudaError_t gqa_decode_selftest_exchange_timeout(const gqa_bf16* q, const gqa_bf16* k_cache,
+                                                 const gqa_bf16* v_cache, const int* block_table,
+                                                 const int* seq_lens, gqa_bf16* out, int B,
+                                                 int Hq, int Hkv, int block_size, int max_blocks,
+                                                 float scale, int wait_limit_us,
+                                                 void* exchange_buffers, size_t exchange_bytes,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 cudaStream_t stream) {
+  if (wait_limit_us <= 0 || wait_limit_us > 1000000 || !exchange_buffers) return cudaErrorInvalidValue;
+  const size_t one = gqa_decode_kvshard_buffer_bytes(B, Hq, Hkv, 2);
+  if (one == 0 || exchange_bytes < 2 * one || !aligned16(exchange_buffers))
+    return cudaErrorInvalidValue;
+  // rank 0 of a world of two whose rank 1 never runs: its words never reach
+  // rank 0's buffer (cleared here, so no word carries the epoch)
+  cudaError_t e = cudaMemsetAsync(exchange_buffers, 0, 2 * one, stream);
+  if (e != cudaSuccess) return e;
+  void* peers[2] = {exchange_buffers, static_cast<unsigned char*>(exchange_buffers) + one};
+  Exchange x;
+  x.world = 2;
+  x.rank = 0;
+  x.epoch = 1;
+  x.peers = peers;
+  return run_balanced(q, k_cache, v_cache, block_table, seq_lens, out, nullptr, nullptr, nullptr,
+                      B, Hq, Hkv, block_size, max_blocks, 0, scale, workspace, workspace_bytes,
+                      stream, &x, static_cast<unsigned long long>(wait_limit_us) * 1000ull);
 }
 
 const char* gqa_decode_version(void) { return "gqa_decode_b200 0.1.0 (sm_100a)"; }

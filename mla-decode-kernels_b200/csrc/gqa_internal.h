@@ -149,6 +149,7 @@ struct CutMergeParams {
   unsigned xepoch;               // != 0, identical on every rank for one decode
   long long xitems;              // B * Hq * kXSlices items per (parity, source rank)
   unsigned char* xpeer[kMaxPeers];  // exchange buffer of every rank ([xrank] = own)
+  unsigned long long wait_ns;    // limit of the wait for the peers' states (kWaitLimitNs)
 };
 
 struct MergeParams {

@@ -228,7 +228,7 @@ __device__ __forceinline__ void exchange_chunk(const CutMergeParams& p, float M,
       }
     }
     if (pending == 0u) break;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > p.wait_ns) {
       ok = false;
       break;
     }

@@ -366,6 +366,46 @@ def test_timed_out_decode_leaves_workspace_valid():
     assert_close(expect, ref)
 
 
+def test_peer_that_never_arrives_times_out_with_status():
+    # The cross-rank exchange of KV-range sharding with a peer that never
+    # runs (rank 1 of 2 on this one GPU): every wait for its states gives up
+    # after 2 ms, status bit 2 says so, the launch ends normally and the
+    # context still decodes correctly.
+    lib = capi.lib
+    lib.gqa_decode_selftest_exchange_timeout.argtypes = (
+        [ctypes.c_void_p] * 6 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int,
+                                                      ctypes.c_void_p, ctypes.c_size_t,
+                                                      ctypes.c_void_p, ctypes.c_size_t,
+                                                      ctypes.c_void_p])
+    lib.gqa_decode_selftest_exchange_timeout.restype = ctypes.c_int
+    lib.gqa_decode_kvshard_buffer_bytes.argtypes = [ctypes.c_int] * 4
+    lib.gqa_decode_kvshard_buffer_bytes.restype = ctypes.c_size_t
+    q, k, v, bt, sl = to_gpu(cases.make_case([5000, 700], 32, 8, 16, seed=28))
+    B, Hq, Hkv, bs, mb = q.shape[0], q.shape[1], k.shape[2], k.shape[1], bt.shape[1]
+    nbytes = lib.gqa_decode_workspace_bytes(B, Hq, Hkv, 0)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    xbytes = 2 * lib.gqa_decode_kvshard_buffer_bytes(B, Hq, Hkv, 2)
+    xbuf = torch.empty(xbytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(q)
+    ptrs = [ctypes.c_void_p(t.data_ptr()) for t in (q, k, v, bt, sl, out)]
+    capi.status()
+    import time
+
+    t0 = time.perf_counter()
+    rc = lib.gqa_decode_selftest_exchange_timeout(*ptrs, B, Hq, Hkv, bs, mb, SCALE, 2000,
+                                                  ctypes.c_void_p(xbuf.data_ptr()), xbytes,
+                                                  ctypes.c_void_p(ws.data_ptr()), nbytes,
+                                                  capi.stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 2.0  # a few 2 ms waits per CTA, not 4 s
+    assert capi.status() == 4, "the exchange waits did not time out"
+    again = binding.gqa_decode(q, k, v, bt, sl, SCALE)
+    torch.cuda.synchronize()
+    assert capi.status() == 0
+    assert_close(again, oracle.attention_ref(*(t.cpu() for t in (q, k, v, bt, sl)), SCALE))
+
+
 def test_cuda_graph_replay():
     q, k, v, bt, sl = to_gpu(cases.ref_case("a_base", seed=3))
     eager = binding.gqa_decode(q, k, v, bt, sl, SCALE)
