@@ -119,8 +119,8 @@ cudaError_t gqa_decode_workspace_init(void* workspace, size_t workspace_bytes,
  * The balanced schedule is two kernels on `stream`: the scan (one
  * persistent CTA per SM; rows held whole by a CTA are written out there) and
  * a small merge of the rows cut between CTAs, launched with programmatic
- * dependent launch so that it is resident before the scan ends and merges
- * every cut row across all SMs.
+ * dependent launch so that its CTAs take the SMs as the scan's CTAs leave
+ * and merge every cut row across all SMs as soon as the scan has ended.
  * Workspace: gqa_decode_workspace_bytes (no initialisation needed).
  * Concurrent launches must not share one workspace.  Additive to the
  * reference API (its extension exposes num_splits only on v2,

@@ -6,9 +6,10 @@
 // per CTA the record {row, parts} of the cut row whose last part it holds,
 // and per row the record {cfirst, parts}.  This kernel is launched right
 // behind it with programmatic dependent launch: the scan lets it start at
-// once, so its CTAs are resident beside the scan's and begin the moment the
-// scan's last CTA has written its state (griddepcontrol.wait), instead of the
-// last CTA of a row merging the row's parts on one SM after its own stream.
+// once, so its CTAs take each SM as the scan's CTA there leaves (the two do
+// not fit on one SM together) and begin the moment the scan's last CTA has
+// written its state (griddepcontrol.wait), instead of the last CTA of a row
+// merging the row's parts on one SM after its own stream.
 // The work is spread over every SM in items of one L2 round trip each:
 //   * a row cut into at most 16 parts: one warp per (row, q head), lane = 4
 //     output dims, the parts' (m, l) and acc rows all loaded at once;
