@@ -319,6 +319,29 @@ cudaError_t gqa_decode_selftest_exchange_timeout(const gqa_bf16* q, const gqa_bf
                                                  void* workspace, size_t workspace_bytes,
                                                  cudaStream_t stream);
 
+/* Test emulation of the KV-range sharded decode (gqa_decode_kvshard_launch)
+ * on ONE GPU: `world` (2..8) ranks, rank r decoding the pages of
+ * block_tables[r] / seq_lens[r] (device arrays, as each rank would pass
+ * them; q and the caches are shared) into outs[r].  Every rank's scan runs,
+ * then one cooperative launch runs every rank's exchange merge at once, so
+ * the ranks' waits for each other always end; the peer buffers are slices
+ * of exchange_buffers and the ranks' workspaces slices of workspaces
+ * (sizes from gqa_decode_selftest_kvshard_emulated_bytes).  Every outs[r]
+ * must come out equal to the single-GPU decode of the whole request, and
+ * identical across r.  No reference counterpart. */
+cudaError_t gqa_decode_selftest_kvshard_emulated(
+    const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+    const int* const* block_tables, const int* const* seq_lens, gqa_bf16* const* outs, int world,
+    int B, int Hq, int Hkv, int block_size, int max_blocks, int num_blocks, float scale,
+    void* exchange_buffers, size_t exchange_bytes_total, void* workspaces,
+    size_t workspace_bytes_total, cudaStream_t stream);
+
+/* Workspace bytes (all ranks) of gqa_decode_selftest_kvshard_emulated on the
+ * current device, and in *exchange_bytes_total the exchange buffers' bytes;
+ * 0 for an invalid shape. */
+size_t gqa_decode_selftest_kvshard_emulated_bytes(int B, int Hq, int Hkv, int world,
+                                                  size_t* exchange_bytes_total);
+
 /* Library version string. */
 const char* gqa_decode_version(void);
 

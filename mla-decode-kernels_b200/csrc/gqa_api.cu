@@ -271,13 +271,12 @@ size_t exchange_bytes(int B, int Hq, int world) {
   return 2ull * world * exchange_items(B, Hq) * gqa::kXItem * sizeof(unsigned long long);
 }
 
-// Scan + cut-row merge of the BALANCED schedule.  `p` carries the inputs,
-// the output mode and the schedule; the workspace supplies the records and
-// partial slots.  The merge kernel runs one CTA per SM.
-cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsigned char* w,
-                            const ShapePlan& sp, int sms, int grid, cudaStream_t stream,
-                            const Exchange* xchg) {
-  gqa::CutMergeParams mp{};
+// Parameters of the scan and the cut-row merge of the BALANCED schedule.
+// `p` carries the inputs, the output mode and the schedule; the workspace
+// supplies the records and partial slots.
+cudaError_t setup_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsigned char* w,
+                           int grid, const Exchange* xchg, gqa::CutMergeParams& mp) {
+  mp = gqa::CutMergeParams{};
   if (xchg) {
     if (!p.out || xchg->world < 1 || xchg->world > gqa::kMaxPeers || xchg->rank < 0 ||
         xchg->rank >= xchg->world || xchg->epoch == 0 || !xchg->peers)
@@ -299,8 +298,6 @@ cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsig
   p.part_acc = reinterpret_cast<float*>(w + lay.acc);
   p.schedule = gqa::kBalanced;
   p.num_splits = 0;
-  cudaError_t e = gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
-  if (e != cudaSuccess) return e;
   mp.row_info = p.row_info;
   mp.ends = p.ends;
   mp.part_m = p.part_m;
@@ -315,6 +312,19 @@ cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsig
   mp.grid = grid;
   mp.out_mode = p.out_mode;
   mp.wait_ns = p.wait_ns;
+  return cudaSuccess;
+}
+
+// Scan + cut-row merge of the BALANCED schedule; the merge kernel runs one
+// CTA per SM.
+cudaError_t launch_balanced(gqa::ScanParams& p, const BalancedLayout& lay, unsigned char* w,
+                            const ShapePlan& sp, int sms, int grid, cudaStream_t stream,
+                            const Exchange* xchg) {
+  gqa::CutMergeParams mp;
+  cudaError_t e = setup_balanced(p, lay, w, grid, xchg, mp);
+  if (e != cudaSuccess) return e;
+  e = gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+  if (e != cudaSuccess) return e;
   return gqa::launch_cut_merge(mp, sms, stream);
 }
 
@@ -718,6 +728,72 @@ cudaError_t gqa_decode_selftest_exchange_timeout(const gqa_bf16* q, const gqa_bf
   return run_balanced(q, k_cache, v_cache, block_table, seq_lens, out, nullptr, nullptr, nullptr,
                       B, Hq, Hkv, block_size, max_blocks, 0, scale, workspace, workspace_bytes,
                       stream, &x, static_cast<unsigned long long>(wait_limit_us) * 1000ull);
+}
+
+cudaError_t gqa_decode_selftest_kvshard_emulated(
+    const gqa_bf16* q, const gqa_bf16* k_cache, const gqa_bf16* v_cache,
+    const int* const* block_tables, const int* const* seq_lens, gqa_bf16* const* outs, int world,
+    int B, int Hq, int Hkv, int block_size, int max_blocks, int num_blocks, float scale,
+    void* exchange_buffers, size_t exchange_bytes_total, void* workspaces,
+    size_t workspace_bytes_total, cudaStream_t stream) {
+  if (world < 2 || world > gqa::kMaxPeers || !block_tables || !seq_lens || !outs ||
+      !exchange_buffers || !workspaces || num_blocks < 0 || !aligned16(exchange_buffers) ||
+      !aligned16(workspaces))
+    return cudaErrorInvalidValue;
+  ShapePlan sp;
+  cudaError_t e = check_common(q, k_cache, v_cache, block_tables[0], seq_lens[0], outs[0], B, Hq,
+                               Hkv, block_size, max_blocks, &sp);
+  if (e != cudaSuccess) return e;
+  if (B == 0) return cudaErrorInvalidValue;
+  int sms = 0, occ = 0;
+  e = device_facts(sp, &sms, &occ);
+  if (e != cudaSuccess) return e;
+  const int grid = balanced_grid(sms, occ);
+  const BalancedLayout lay = balanced_layout(B, sp, grid);
+  const size_t ws_one = (lay.total + 255) / 256 * 256;
+  const size_t x_one = exchange_bytes(B, Hq, world);
+  if (workspace_bytes_total < ws_one * world || exchange_bytes_total < x_one * world)
+    return cudaErrorInvalidValue;
+  gqa::ExchangeEmulParams ep{};
+  ep.world = world;
+  ep.per_rank = gqa::exchange_emul_per_rank(world, sms);
+  if (ep.per_rank < 1) return cudaErrorInvalidConfiguration;
+  void* peers[gqa::kMaxPeers];
+  for (int r = 0; r < world; ++r)
+    peers[r] = static_cast<unsigned char*>(exchange_buffers) + r * x_one;
+  e = cudaMemsetAsync(exchange_buffers, 0, x_one * world, stream);  // no word has the epoch
+  if (e != cudaSuccess) return e;
+  for (int r = 0; r < world; ++r) {
+    e = check_common(q, k_cache, v_cache, block_tables[r], seq_lens[r], outs[r], B, Hq, Hkv,
+                     block_size, max_blocks, &sp);
+    if (e != cudaSuccess) return e;
+    gqa::ScanParams p = base_params(q, k_cache, v_cache, block_tables[r], seq_lens[r], B, Hq, Hkv,
+                                    block_size, max_blocks, num_blocks, scale, sp);
+    p.out = outs[r];
+    Exchange x;
+    x.world = world;
+    x.rank = r;
+    x.epoch = 1;
+    x.peers = peers;
+    e = setup_balanced(p, lay, static_cast<unsigned char*>(workspaces) + r * ws_one, grid, &x,
+                       ep.rank[r]);
+    if (e != cudaSuccess) return e;
+    e = gqa::launch_scan(p, grid, sp.threads, sp.smem_bytes, stream);
+    if (e != cudaSuccess) return e;
+  }
+  return gqa::launch_exchange_emulated(ep, stream);
+}
+
+size_t gqa_decode_selftest_kvshard_emulated_bytes(int B, int Hq, int Hkv, int world,
+                                                  size_t* exchange_bytes_total) {
+  ShapePlan sp;
+  if (gqa::make_shape_plan(Hq, Hkv, &sp) != 0 || B <= 0 || world < 2 || world > gqa::kMaxPeers)
+    return 0;
+  int sms = 0, occ = 0;
+  if (device_facts(sp, &sms, &occ) != cudaSuccess) return 0;
+  const BalancedLayout lay = balanced_layout(B, sp, balanced_grid(sms, occ));
+  if (exchange_bytes_total) *exchange_bytes_total = exchange_bytes(B, Hq, world) * world;
+  return (lay.total + 255) / 256 * 256 * world;
 }
 
 const char* gqa_decode_version(void) { return "gqa_decode_b200 0.1.0 (sm_100a)"; }

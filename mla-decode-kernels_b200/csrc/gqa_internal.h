@@ -152,6 +152,13 @@ struct CutMergeParams {
   unsigned long long wait_ns;    // limit of the wait for the peers' states (kWaitLimitNs)
 };
 
+// Every rank's exchange merge in one cooperative launch on one GPU (test
+// emulation of the KV-range sharded decode): CTA c plays rank c / per_rank.
+struct ExchangeEmulParams {
+  CutMergeParams rank[kMaxPeers];
+  int world, per_rank;
+};
+
 struct MergeParams {
   const float* part_m;
   const float* part_l;
@@ -187,6 +194,10 @@ cudaError_t launch_scan(const ScanParams& p, int grid, int threads, int smem, cu
 // The cut-row merge, launched with programmatic dependent launch right after
 // the scan on the same stream; `grid` = CTAs of the merge kernel.
 cudaError_t launch_cut_merge(const CutMergeParams& p, int grid, cudaStream_t s);
+// Cooperative launch of the emulated exchange merge (world * per_rank CTAs,
+// all resident at once); per_rank from exchange_emul_per_rank.
+cudaError_t launch_exchange_emulated(const ExchangeEmulParams& e, cudaStream_t s);
+int exchange_emul_per_rank(int world, int sms);
 // Scan + cut-row merge of the BALANCED schedule with bf16 output or states,
 // the records and partial slots placed in `w` by `lay` (gqa_api.cu).
 cudaError_t launch_balanced_noexchange(ScanParams& p, const BalancedLayout& lay,

@@ -261,6 +261,25 @@ __device__ __forceinline__ void exchange_chunk(const CutMergeParams& p, float M,
       __float2bfloat16(Mx == -INFINITY ? 0.f : Ax / Lx);
 }
 
+// kOutExchange: every row, cut or not, is QHR x 4 chunk units, unit u
+// handled by CTA u mod ncta (the same units on every rank).
+__device__ __forceinline__ void exchange_units(const CutMergeParams& p, int cta, int ncta,
+                                               ChunkSmem& cs) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long units = static_cast<long long>(p.rows) * p.QHR * kChunks;
+  for (long long u = cta; u < units; u += ncta) {
+    const long long rh = u / kChunks;  // = b * Hq + q head
+    const int c = static_cast<int>(u - rh * kChunks);
+    const int r = static_cast<int>(rh / p.QHR);
+    const int j = static_cast<int>(rh - static_cast<long long>(r) * p.QHR);
+    const int2 ri = p.row_info[r];  // {first CTA, parts}
+    float M = 0.f, L = 0.f, A = 0.f;
+    merge_chunk(p, static_cast<long long>(ri.x) + r, ri.y, j, c, cs, M, L, A);
+    if (warp == 0) exchange_chunk(p, M, L, A, static_cast<size_t>(u),
+                                  static_cast<size_t>(rh), c, lane);
+  }
+}
+
 }  // namespace merge_detail
 
 // Every CTA first compacts, in shared memory, the list of cut rows from the
@@ -284,18 +303,7 @@ __global__ void __launch_bounds__(merge_detail::kThreads, 2)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   if (p.out_mode == kOutExchange) {
-    const long long units = static_cast<long long>(p.rows) * p.QHR * kChunks;
-    for (long long u = blockIdx.x; u < units; u += gridDim.x) {
-      const long long rh = u / kChunks;  // = b * Hq + q head
-      const int c = static_cast<int>(u - rh * kChunks);
-      const int r = static_cast<int>(rh / p.QHR);
-      const int j = static_cast<int>(rh - static_cast<long long>(r) * p.QHR);
-      const int2 ri = p.row_info[r];  // {first CTA, parts}
-      float M = 0.f, L = 0.f, A = 0.f;
-      merge_chunk(p, static_cast<long long>(ri.x) + r, ri.y, j, c, cs, M, L, A);
-      if (warp == 0) exchange_chunk(p, M, L, A, static_cast<size_t>(u),
-                                    static_cast<size_t>(rh), c, lane);
-    }
+    exchange_units(p, blockIdx.x, gridDim.x, cs);
     return;
   }
 
@@ -366,6 +374,41 @@ __global__ void __launch_bounds__(merge_detail::kThreads, 2)
       }
     }
   }
+}
+
+// Test emulation of the KV-range sharded decode on one GPU: the exchange
+// merge of every rank in one grid, CTA c acting as CTA c mod per_rank of
+// rank c / per_rank.  Launched cooperatively, so every CTA is resident and
+// each rank's waits for the others' states end.
+__global__ void __launch_bounds__(merge_detail::kThreads, 2)
+    gqa_decode_exchange_emul_kernel(const __grid_constant__ ExchangeEmulParams e) {
+  using namespace merge_detail;
+  __shared__ ChunkSmem cs;
+  const int r = static_cast<int>(blockIdx.x) / e.per_rank;
+  exchange_units(e.rank[r], static_cast<int>(blockIdx.x) - r * e.per_rank, e.per_rank, cs);
+}
+
+int exchange_emul_per_rank(int world, int sms) {
+  int occ = 0;
+  if (world < 1 || cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                       &occ, gqa_decode_exchange_emul_kernel, merge_detail::kThreads, 0) !=
+                       cudaSuccess)
+    return 0;
+  return occ * sms / world;
+}
+
+cudaError_t launch_exchange_emulated(const ExchangeEmulParams& e, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(e.world * e.per_rank);
+  cfg.blockDim = dim3(merge_detail::kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gqa_decode_exchange_emul_kernel, e);
 }
 
 size_t cut_merge_smem_bytes(int grid) { return (3 * static_cast<size_t>(grid) + 1) * sizeof(int); }

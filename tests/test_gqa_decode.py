@@ -274,6 +274,62 @@ def test_kvshard_peer_exchange_single_rank(seq_lens):
         dec.close()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_kvshard_peer_exchange_emulated(world):
+    # The fused peer exchange of KV-range sharding with every rank on this
+    # one GPU: each rank's scan over its page range, then one cooperative
+    # launch running every rank's exchange merge (so the ranks' waits for
+    # each other end).  Every rank's output must be identical and equal to
+    # the single-GPU decode of the whole batch: a long request, a short one,
+    # an empty one and one with fewer pages than ranks.
+    import sharding
+
+    lib = capi.lib
+    P, PP, I, Z = ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_size_t
+    lib.gqa_decode_selftest_kvshard_emulated.argtypes = (
+        [P, P, P, PP, PP, PP] + [I] * 7 + [ctypes.c_float, P, Z, P, Z, P])
+    lib.gqa_decode_selftest_kvshard_emulated.restype = I
+    lib.gqa_decode_selftest_kvshard_emulated_bytes.argtypes = [I] * 4 + [ctypes.POINTER(Z)]
+    lib.gqa_decode_selftest_kvshard_emulated_bytes.restype = Z
+    seq_lens, bs = [40000, 3000, 0, 17], 64
+    case = cases.make_case(seq_lens, 32, 8, bs, seed=29, pool_factor=1.0, device="cuda")
+    q, k, v, bt, sl = case
+    B, mb = len(seq_lens), bt.shape[1]
+    bts, sls = [], []
+    for r in range(world):
+        rows, lens = [], []
+        for b, S in enumerate(seq_lens):
+            t0, t1 = sharding.kv_range(S, bs, r, world)
+            pages = bt[b, t0 // bs:(t1 + bs - 1) // bs]
+            row = torch.zeros(mb, dtype=torch.int32, device="cuda")
+            row[:pages.numel()] = pages
+            rows.append(row)
+            lens.append(t1 - t0)
+        bts.append(torch.stack(rows).contiguous())
+        sls.append(torch.tensor(lens, dtype=torch.int32, device="cuda"))
+    outs = [torch.full_like(q, float("nan")) for _ in range(world)]
+    xbytes = Z(0)
+    wbytes = lib.gqa_decode_selftest_kvshard_emulated_bytes(B, 32, 8, world, ctypes.byref(xbytes))
+    assert wbytes > 0 and xbytes.value > 0
+    ws = torch.empty(wbytes, dtype=torch.uint8, device="cuda")
+    xb = torch.empty(xbytes.value, dtype=torch.uint8, device="cuda")
+
+    def ptrs(ts):
+        return (ctypes.c_void_p * world)(*[t.data_ptr() for t in ts])
+
+    rc = lib.gqa_decode_selftest_kvshard_emulated(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), ptrs(bts), ptrs(sls), ptrs(outs), world, B, 32,
+        8, bs, mb, k.shape[0], SCALE, xb.data_ptr(), xbytes.value, ws.data_ptr(), wbytes,
+        capi.stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    check_status()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert_close(outs[0], capi.auto(*case, SCALE), "emulated peer exchange vs single GPU")
+    check_subset(outs[0], case, [1, 2, 3])
+
+
 def test_merge_states_all_empty_shards():
     m = torch.full((3, 5), -float("inf"), device="cuda")
     l = torch.zeros(3, 5, device="cuda")
