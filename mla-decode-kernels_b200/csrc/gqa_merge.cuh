@@ -292,7 +292,7 @@ __device__ __forceinline__ void exchange_units(const CutMergeParams& p, int cta,
 // on every rank) read from the per-row records; a CTA handles the same units
 // on every rank (the grid is the same), always sending a unit before waiting
 // for it.
-__global__ void __launch_bounds__(merge_detail::kThreads, 2)
+__global__ void __launch_bounds__(merge_detail::kThreads, 1)
     gqa_decode_cut_merge_kernel(const __grid_constant__ CutMergeParams p) {
   using namespace merge_detail;
   extern __shared__ int sh[];  // [grid] rows | [grid] parts | [grid + 1] unit prefix
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(merge_detail::kThreads, 2)
 // merge of every rank in one grid, CTA c acting as CTA c mod per_rank of
 // rank c / per_rank.  Launched cooperatively, so every CTA is resident and
 // each rank's waits for the others' states end.
-__global__ void __launch_bounds__(merge_detail::kThreads, 2)
+__global__ void __launch_bounds__(merge_detail::kThreads, 1)
     gqa_decode_exchange_emul_kernel(const __grid_constant__ ExchangeEmulParams e) {
   using namespace merge_detail;
   __shared__ ChunkSmem cs;
