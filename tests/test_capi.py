@@ -203,3 +203,25 @@ def test_balanced_workspace_for_huge_batches_and_grid_cap(lib):
     assert rc == 0 and p.workspace_bytes == balanced_bytes(148, 16384, rows=16384, qhr=32)
     rc, p = plan(lib, 64, 32, 1, sms=148, per_sm=20)
     assert rc == 0 and p.grid == 2048
+
+
+def test_selftests_reject_bad_arguments_before_any_device_call(lib):
+    # argument checks come first, so these return without a GPU
+    P, PP, I, Z = ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_size_t
+    f = lib.gqa_decode_selftest_kvshard_emulated
+    f.argtypes = [P, P, P, PP, PP, PP] + [I] * 7 + [ctypes.c_float, P, Z, P, Z, P]
+    f.restype = I
+    arr = (ctypes.c_void_p * 1)(None)
+    for world in (1, 9):  # one rank is no exchange; more than 8 peers is unsupported
+        assert f(None, None, None, arr, arr, arr, world, 1, 32, 8, 16, 4, 0, 1.0, None, 0,
+                 None, 0, None) == 1  # cudaErrorInvalidValue
+    g = lib.gqa_decode_selftest_kvshard_emulated_bytes
+    g.argtypes = [I] * 4 + [ctypes.POINTER(Z)]
+    g.restype = Z
+    assert g(1, 32, 8, 1, None) == 0 and g(1, 33, 8, 2, None) == 0 and g(0, 32, 8, 2, None) == 0
+    h = lib.gqa_decode_selftest_exchange_timeout
+    h.argtypes = [P] * 6 + [I] * 5 + [ctypes.c_float, I, P, Z, P, Z, P]
+    h.restype = I
+    for wait_us in (0, 1000001):
+        assert h(None, None, None, None, None, None, 1, 32, 8, 16, 4, 1.0, wait_us, None, 0,
+                 None, 0, None) == 1
